@@ -1,0 +1,167 @@
+"""Seeded synthetic workloads with the shapes of the benchmark configurations.
+
+No public dataset is involved: every input is drawn from
+``numpy.random.default_rng(seed)`` with the shapes, sizes and distributions
+of the five configurations this package is measured on.
+
+* c1 -- one request, 1 layer, 8 KV heads, head_dim 64, 4096 tokens, three
+  dropped spans of 128..512 tokens, plain RoPE theta 10000.
+* c2 -- GPT-OSS-120B-shaped cache: 36 layers, 8 KV heads, head_dim 64, one
+  65536-token request, about 40 % dropped in 20 spans, YaRN RoPE (theta
+  150000, factor 32, original 4096).  Span lengths are drawn uniform in
+  [256, 4096] and then rescaled so that they total 0.4 T (20 spans drawn
+  uniform in that range would average 66 % of T), clipped to [256, 4096].
+* c3 -- 64 requests, lengths uniform 2K..32K, one shared radix prefix of
+  1K..4K tokens, per-request drop fraction uniform 10..60 % in
+  ceil(f L / 1024) spans, the first span starting inside the first half of
+  the prefix so that shared tokens behind it must be copied (COW).
+* c4 -- ragged decode attention: batch 128, 64 q heads / 8 KV heads,
+  head_dim 64, lognormal KV lengths (median 8192, sigma 1.0, clipped to
+  [1, 65536]), sinks ~ N(0, 1).
+* c5 -- Llama-3-70B-shaped cache: 80 layers, 8 KV heads, head_dim 128,
+  8 requests of 131072 tokens, 30 % dropped, plain RoPE theta 500000.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+
+def place_spans(rng, token_count, lengths, lo=0):
+    """Place spans of the given lengths, in order and disjoint, inside
+    [lo, token_count), with the free tokens split by a sorted uniform draw.
+    Returns an int32 array of (start, end) pairs, flattened."""
+    lengths = np.asarray(lengths, np.int64)
+    free = token_count - lo - int(lengths.sum())
+    if free < 0:
+        raise ValueError("spans do not fit")
+    cuts = np.sort(rng.integers(0, free + 1, size=len(lengths)))
+    starts = lo + cuts + np.concatenate(([0], np.cumsum(lengths)[:-1]))
+    return np.stack((starts, starts + lengths), 1).reshape(-1).astype(np.int32)
+
+
+def rescaled_lengths(rng, count, lo, hi, total):
+    """``count`` lengths drawn uniform in [lo, hi], rescaled to sum to about
+    ``total`` and clipped back into [lo, hi]."""
+    raw = rng.uniform(lo, hi, size=count)
+    scaled = np.clip(np.round(raw * (total / raw.sum())), lo, hi).astype(np.int64)
+    return scaled
+
+
+@dataclass
+class DropProgram:
+    """Batched Drop + Reposition program in request-local raw indices."""
+
+    token_counts: np.ndarray  # int64 [R]
+    range_offsets: np.ndarray  # int32 [R+1], in pairs
+    ranges: np.ndarray  # int32 [2 * n_ranges], (start, end) pairs
+    shared_prefix: np.ndarray  # int64 [R], borrowed radix tokens per request
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def requests(self):
+        return len(self.token_counts)
+
+    @property
+    def total_tokens(self):
+        return int(self.token_counts.sum())
+
+    def request_ranges(self, r):
+        a, b = self.range_offsets[r], self.range_offsets[r + 1]
+        return self.ranges[2 * a: 2 * b]
+
+    def keep_mask(self, r):
+        keep = np.ones(int(self.token_counts[r]), bool)
+        rr = self.request_ranges(r).reshape(-1, 2)
+        for s, e in rr:
+            keep[s:e] = False
+        return keep
+
+
+def _program(counts, per_request, shared=None, meta=None):
+    offsets = [0]
+    for spans in per_request:
+        offsets.append(offsets[-1] + len(spans) // 2)
+    ranges = (np.concatenate(per_request) if per_request else np.zeros(0)).astype(np.int32)
+    shared = np.zeros(len(counts), np.int64) if shared is None else np.asarray(shared, np.int64)
+    return DropProgram(np.asarray(counts, np.int64), np.asarray(offsets, np.int32), ranges,
+                       shared, meta or {})
+
+
+def c1_program(seed=0, tokens=4096):
+    rng = np.random.default_rng(seed)
+    lengths = rng.integers(128, 513, size=3)
+    return _program([tokens], [place_spans(rng, tokens, lengths)], meta=dict(config="c1"))
+
+
+def c2_program(seed=0, tokens=65536, spans=20, frac=0.4):
+    rng = np.random.default_rng(seed)
+    lengths = rescaled_lengths(rng, spans, 256, 4096, frac * tokens)
+    return _program([tokens], [place_spans(rng, tokens, lengths)], meta=dict(config="c2"))
+
+
+def c3_program(seed=0, requests=64, min_len=2048, max_len=32768):
+    rng = np.random.default_rng(seed)
+    prefix = int(rng.integers(1024, 4097))
+    counts = rng.integers(max(min_len, prefix + 2), max_len + 1, size=requests)
+    per_request = []
+    for length in counts:
+        length = int(length)
+        frac = rng.uniform(0.1, 0.6)
+        total = int(round(frac * length))
+        count = max(1, int(np.ceil(total / 1024)))
+        lengths = np.maximum(1, rescaled_lengths(rng, count, 1, 2048, total))
+        first_start = int(rng.integers(0, prefix // 2))
+        first_end = first_start + int(lengths[0])
+        rest = lengths[1:]
+        while first_end + int(rest.sum()) > length:
+            rest = rest[:-1]
+        spans = [np.array([first_start, first_end], np.int32)]
+        if len(rest):
+            spans.append(place_spans(rng, length, rest, lo=first_end))
+        per_request.append(np.concatenate(spans))
+    return _program(counts, per_request, shared=np.full(requests, prefix),
+                    meta=dict(config="c3", prefix=prefix))
+
+
+def c5_program(seed=0, requests=8, tokens=131072, spans=20, frac=0.3):
+    rng = np.random.default_rng(seed)
+    per_request = []
+    for _ in range(requests):
+        lengths = rescaled_lengths(rng, spans, 256, 4096, frac * tokens)
+        per_request.append(place_spans(rng, tokens, lengths))
+    return _program([tokens] * requests, per_request, meta=dict(config="c5"))
+
+
+def slot_rows(rng, program, shared_slots=None, first_slot=1):
+    """req_to_token rows: each request's private tokens get distinct slots
+    from a random permutation of ``first_slot..``; slot 0 is the padding slot.
+    Tokens below the shared prefix all map to the same shared slots."""
+    prefix = int(program.shared_prefix.max()) if program.requests else 0
+    private = int((program.token_counts - program.shared_prefix).sum())
+    perm = rng.permutation(prefix + private).astype(np.int64) + first_slot
+    shared = perm[:prefix]
+    cursor = prefix
+    rows = []
+    for r in range(program.requests):
+        t, p = int(program.token_counts[r]), int(program.shared_prefix[r])
+        row = np.empty(t, np.int32)
+        row[:p] = shared[:p]
+        row[p:] = perm[cursor: cursor + t - p]
+        cursor += t - p
+        rows.append(row)
+    return rows, prefix + private + first_slot
+
+
+@dataclass
+class DecodeBatch:
+    lengths: np.ndarray  # int64 [bs]
+    meta: dict = field(default_factory=dict)
+
+
+def c4_lengths(seed=0, batch=128, median=8192, sigma=1.0, max_len=65536):
+    rng = np.random.default_rng(seed)
+    lengths = np.clip(np.round(rng.lognormal(np.log(median), sigma, size=batch)), 1, max_len)
+    return lengths.astype(np.int64)
