@@ -1,0 +1,98 @@
+"""ctypes binding of ``libakv_b200.so`` (declared in include/akv_b200.h).
+
+The library is built in-tree by ``python -m akv_b200.build``.  There is no
+fallback: importing the ops without the built library raises ImportError,
+and a failed launch raises RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libakv_b200.so")
+
+AKV_OK, AKV_ERR_INVALID, AKV_ERR_CUDA, AKV_ERR_UNSUPPORTED = 0, 1, 2, 3
+AKV_F16, AKV_BF16, AKV_F32 = 0, 1, 2
+DROP_RING_UNDERFLOW, DROP_RING_OVERFLOW, DROP_BAD_RANGE, DROP_NO_ACTIVE = 1, 2, 4, 8
+
+DTYPE_CODE = {torch.float16: AKV_F16, torch.bfloat16: AKV_BF16, torch.float32: AKV_F32}
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+
+# name -> argument types, in the order of include/akv_b200.h
+SIGNATURES = {
+    "akv_version": [],
+    "akv_reposition_kv_layers": [
+        _P, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64,
+        _P, _P, _I32, _I64, _I32, _I32, _I64, _I64, _P, _P,
+    ],
+    "akv_drop_compact_tile_tokens": [],
+    "akv_drop_compact_workspace_bytes": [_I32, _I32],
+    "akv_drop_compact": [
+        _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P,
+        _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+    ],
+    "akv_context_decode_indices": [
+        _P, _P, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _I32, _P, _I32, _P, _I32, _I64, _I32,
+        _P,
+    ],
+    "akv_context_window_lengths": [_P, _P, _I32, _P, _I32, _P, _I32, _I64, _I32, _P],
+    "akv_build_decode_metadata": [
+        _P, _P, _I64, _P, _P, _I64, _P, _I64, _I32, _P, _P, _P, _P, _P,
+    ],
+    "akv_write_row_slots": [_P, _P, _I32, _P, _I32, _P, _I32, _I64, _P],
+}
+RESTYPES = {
+    "akv_version": ctypes.c_char_p,
+    "akv_drop_compact_tile_tokens": _I64,
+    "akv_drop_compact_workspace_bytes": _I64,
+}
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is not built; run `python -m akv_b200.build` (nvcc, sm_100a). "
+            "akv_b200 has no CPU or Triton fallback."
+        )
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = RESTYPES.get(name, ctypes.c_int)
+    return lib
+
+
+lib = _load()
+
+
+def ptr(t):
+    """Device address of a tensor (None -> NULL)."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def check(status: int, what: str) -> None:
+    if status == AKV_OK:
+        return
+    if status == AKV_ERR_INVALID:
+        raise ValueError(f"{what}: invalid arguments")
+    if status == AKV_ERR_UNSUPPORTED:
+        raise ValueError(f"{what}: unsupported configuration")
+    raise RuntimeError(f"{what}: CUDA launch failed (status {status})")
+
+
+def is64(t) -> int:
+    if t.dtype == torch.int64:
+        return 1
+    if t.dtype == torch.int32:
+        return 0
+    raise ValueError(f"index tensors must be int32 or int64, got {t.dtype}")

@@ -1,0 +1,295 @@
+"""Drop + Reposition of a batch of requests on the GPU (C ABI ``akv_drop_compact``).
+
+The reference compiles every request's event program on the CPU
+(``compile_context_layout``, srt/context_system/ir.py:113-274, running the
+C++ sweep of kernels/ops/attention/context_plan.py:210-532), derives the
+decode view on the CPU (``ContextDecodeLayout.from_layout``,
+srt/context_system/occurrence.py:47-66), copies it to the device, and
+retires dropped slots through the scheduler (occurrence.py:711-714,
+936-964).  For the cache operation of an agent turn -- drop a set of spans,
+then Reposition at the end of the prompt -- ``DropCompactor`` computes all
+of it on the device in three stream-ordered launches:
+
+* keep mask and final positions of every token,
+* the compacted decode view (raw indices and positions of the kept tokens),
+* the Reposition transitions (source slot, destination slot, old and new
+  position), where a radix-shared source is copied to a fresh slot popped
+  from the device free ring (copy-on-write) and the request's
+  req_to_token entry is updated, while private sources rotate in place,
+* the freed slots of dropped private tokens, pushed onto the free ring.
+
+The transition vectors feed ``reposition_kv_layers`` directly, with the
+device-side count, so a whole Drop + Reposition runs without a host round
+trip.  Host input is the event program (token counts and drop ranges per
+request), validated on the CPU with the reference's rules before one packed
+host-to-device copy.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native
+
+TILE = int(_native.lib.akv_drop_compact_tile_tokens())
+
+
+class FreeSlotRing:
+    """Device-resident free list of KV slots.
+
+    ``ring`` holds slot ids; ``state`` = {head, tail} (int64, device).  Free
+    entries are ring[head % capacity .. tail % capacity).  Copy-on-write pops
+    from the head, freed slots are pushed at the tail, both on the device.
+    """
+
+    def __init__(self, free_slots, capacity=None, device=None):
+        free = torch.as_tensor(free_slots, dtype=torch.int32)
+        device = torch.device(device) if device is not None else free.device
+        capacity = int(capacity if capacity is not None else max(1, len(free)))
+        if len(free) > capacity:
+            raise ValueError("free slots exceed the ring capacity")
+        self.capacity = capacity
+        self.ring = torch.zeros(capacity, dtype=torch.int32, device=device)
+        self.ring[: len(free)] = free.to(device)
+        self.state = torch.tensor([0, len(free)], dtype=torch.int64, device=device)
+
+    def free_count(self) -> int:
+        """Number of free slots (reads the device state: synchronises)."""
+        head, tail = self.state.tolist()
+        return tail - head
+
+    def snapshot(self) -> np.ndarray:
+        """Free slot ids in ring order (reads the device: synchronises)."""
+        head, tail = self.state.tolist()
+        idx = torch.arange(head, tail, device=self.ring.device) % self.capacity
+        return self.ring[idx].cpu().numpy()
+
+
+@dataclass
+class DropResult:
+    """Device views of one call.  Counts live on the device in ``totals``
+    ({kept, moved, copy-on-write, freed}); the compacted vectors are valid
+    up to those counts and the per-request CSR offsets."""
+
+    keep_mask: torch.Tensor
+    positions: torch.Tensor
+    active_offsets: torch.Tensor
+    raw_indices: torch.Tensor
+    active_positions: torch.Tensor
+    next_position: torch.Tensor
+    transition_offsets: torch.Tensor
+    transition_source: torch.Tensor
+    transition_destination: torch.Tensor
+    transition_pairs: torch.Tensor
+    transition_raw: torch.Tensor
+    freed_offsets: torch.Tensor
+    freed_slots: torch.Tensor
+    totals: torch.Tensor
+    status: torch.Tensor
+
+    @property
+    def transition_count(self) -> torch.Tensor:
+        """One-element int32 device view: ``count_device`` for reposition."""
+        return self.totals[1:2]
+
+    def check(self) -> None:
+        """Read the device status (synchronises) and raise on failure."""
+        st = int(self.status.item())
+        if st == 0:
+            return
+        msgs = []
+        if st & _native.DROP_RING_UNDERFLOW:
+            msgs.append("not enough free KV slots for copy-on-write")
+        if st & _native.DROP_RING_OVERFLOW:
+            msgs.append("freed slots exceed the free ring capacity")
+        if st & _native.DROP_BAD_RANGE:
+            msgs.append("a drop range lies outside its request")
+        if st & _native.DROP_NO_ACTIVE:
+            msgs.append("Reposition of a request with no active tokens")
+        raise RuntimeError("drop_compact failed: " + "; ".join(msgs))
+
+
+def validate_program(token_counts, range_offsets, ranges, reposition=True):
+    """The reference compiler's rules for one drop event at the end of each
+    prompt (context_plan.py:362-411): ranges are half-open, ordered,
+    disjoint and inside the prompt; a Reposition needs an active token."""
+    token_counts = np.asarray(token_counts, np.int64)
+    range_offsets = np.asarray(range_offsets, np.int64)
+    ranges = np.asarray(ranges, np.int64).reshape(-1, 2)
+    if len(range_offsets) != len(token_counts) + 1 or range_offsets[0] != 0 or \
+            range_offsets[-1] != len(ranges) or np.any(np.diff(range_offsets) < 0):
+        raise ValueError("drop_range_offsets does not cover drop_ranges")
+    if np.any(token_counts < 0) or np.any(token_counts > np.iinfo(np.int32).max):
+        raise ValueError("token_count exceeds the int32 Reposition limit")
+    for r, t in enumerate(token_counts):
+        rr = ranges[range_offsets[r]: range_offsets[r + 1]]
+        if len(rr) == 0:
+            continue
+        starts, ends = rr[:, 0], rr[:, 1]
+        if np.any(starts < 0) or np.any(starts >= ends) or np.any(ends > t) or \
+                np.any(starts[1:] <= ends[:-1]):
+            raise ValueError("Drop ranges must be ordered, disjoint, and already materialized")
+        if reposition and t > 0 and int((ends - starts).sum()) == t:
+            raise ValueError(f"Reposition at raw boundary {int(t) - 1} has no active tokens.")
+
+
+class DropCompactor:
+    """Preallocated device buffers and pinned staging for ``akv_drop_compact``.
+
+    Capacities bound one call: total tokens, requests and ranges.  Outputs
+    are views into the buffers and are overwritten by the next call.
+    """
+
+    def __init__(self, max_tokens, max_requests, max_ranges, device):
+        self.device = torch.device(device)
+        self.max_tokens = int(max_tokens)
+        self.max_requests = int(max_requests)
+        self.max_ranges = int(max_ranges)
+        max_tiles = (self.max_tokens + TILE - 1) // TILE + self.max_requests
+        self.max_tiles = max_tiles
+        d, i32 = self.device, torch.int32
+        n, r = max(1, self.max_tokens), self.max_requests
+        self.keep_mask = torch.empty(n, dtype=torch.uint8, device=d)
+        self.positions = torch.empty(n, dtype=i32, device=d)
+        self.raw_indices = torch.empty(n, dtype=i32, device=d)
+        self.active_positions = torch.empty(n, dtype=i32, device=d)
+        self.transition_source = torch.empty(n, dtype=i32, device=d)
+        self.transition_destination = torch.empty(n, dtype=i32, device=d)
+        self.transition_pairs = torch.empty((n, 2), dtype=i32, device=d)
+        self.transition_raw = torch.empty(n, dtype=i32, device=d)
+        self.freed_slots = torch.empty(n, dtype=i32, device=d)
+        # per-request outputs + counters in one buffer
+        self.offsets = torch.empty((3, r + 1), dtype=i32, device=d)
+        self.next_position = torch.empty(max(1, r), dtype=i32, device=d)
+        self.counters = torch.empty(5, dtype=i32, device=d)  # totals[4], status
+        ws = int(_native.lib.akv_drop_compact_workspace_bytes(r, max_tiles))
+        self.workspace = torch.empty(ws + 256, dtype=torch.uint8, device=d)
+        # Packed program: token_offsets (int64) | row_ids (int64) |
+        # tile_offsets | range_offsets | shared_prefix | ranges (int32).
+        self._host = torch.empty(self._packed_bytes(), dtype=torch.uint8, pin_memory=True)
+        self._dev = torch.empty_like(self._host, device=d)
+        # The pinned staging buffer is rewritten by the next call only after
+        # the previous host-to-device copy has left it.
+        self._copied = torch.cuda.Event()
+        self._copied.record(torch.cuda.current_stream(d))
+
+    def _packed_bytes(self):
+        r, rr = self.max_requests, self.max_ranges
+        return 8 * (r + 1) + 8 * r + 4 * ((r + 1) * 2 + r + 2 * rr) + 64
+
+    def _layout(self, nreq, nranges):
+        off, views = 0, {}
+        for name, count, dtype, size in (
+            ("token_offsets", nreq + 1, torch.int64, 8),
+            ("row_ids", nreq, torch.int64, 8),
+            ("tile_offsets", nreq + 1, torch.int32, 4),
+            ("range_offsets", nreq + 1, torch.int32, 4),
+            ("shared_prefix", nreq, torch.int32, 4),
+            ("ranges", 2 * nranges, torch.int32, 4),
+        ):
+            off = (off + 7) // 8 * 8
+            views[name] = (off, count, dtype)
+            off += count * size
+        return views, off
+
+    def run(self, token_counts, range_offsets, ranges, req_to_token, row_ids, ring,
+            shared_prefix=None, reposition=True, validate=True) -> DropResult:
+        """Validate and stage the program (one packed host-to-device copy),
+        then launch: ``prepare`` followed by ``launch``."""
+        prepared = self.prepare(token_counts, range_offsets, ranges, row_ids,
+                                shared_prefix=shared_prefix, reposition=reposition,
+                                validate=validate)
+        return self.launch(prepared, req_to_token, ring)
+
+    def prepare(self, token_counts, range_offsets, ranges, row_ids, shared_prefix=None,
+                reposition=True, validate=True) -> dict:
+        """Host half: validation, packing and the host-to-device copy.  The
+        returned handle can be launched any number of times while the
+        staged program stays resident on the device."""
+        token_counts = np.asarray(token_counts, np.int64)
+        nreq = len(token_counts)
+        range_offsets = np.asarray(range_offsets, np.int64)
+        ranges = np.asarray(ranges, np.int64)
+        nranges = len(ranges) // 2
+        total = int(token_counts.sum())
+        if nreq > self.max_requests or nranges > self.max_ranges or total > self.max_tokens:
+            raise ValueError("drop program exceeds the compactor's capacity")
+        if validate:
+            validate_program(token_counts, range_offsets, ranges, reposition)
+        tiles = (token_counts + TILE - 1) // TILE
+        tile_offsets = np.concatenate(([0], np.cumsum(tiles)))
+        n_tiles = int(tile_offsets[-1])
+        views, used = self._layout(nreq, nranges)
+        host = self._host
+        self._copied.synchronize()
+        fields = {
+            "token_offsets": np.concatenate(([0], np.cumsum(token_counts))),
+            "row_ids": np.asarray(row_ids, np.int64),
+            "tile_offsets": tile_offsets,
+            "range_offsets": range_offsets,
+            "shared_prefix": np.zeros(nreq) if shared_prefix is None else shared_prefix,
+            "ranges": ranges,
+        }
+        for name, (off, count, dtype) in views.items():
+            size = 8 if dtype == torch.int64 else 4
+            host[off: off + count * size].view(dtype).copy_(
+                torch.from_numpy(np.asarray(fields[name]).astype(
+                    np.int64 if dtype == torch.int64 else np.int32)))
+        self._dev[:used].copy_(host[:used], non_blocking=True)
+        self._copied.record(torch.cuda.current_stream(self.device))
+        dev = {name: self._dev[off: off + count * (8 if dt == torch.int64 else 4)].view(dt)
+               for name, (off, count, dt) in views.items()}
+        return dict(dev=dev, nreq=nreq, n_tiles=n_tiles, total=total,
+                    shared=shared_prefix is not None, reposition=bool(reposition),
+                    h2d_bytes=used)
+
+    def launch(self, prepared, req_to_token, ring) -> DropResult:
+        """Device half: the three kernels of ``akv_drop_compact`` over a
+        staged program; no host work beyond the launch."""
+        if req_to_token.dtype != torch.int32 or req_to_token.device != self.device or \
+                req_to_token.ndim != 2 or req_to_token.stride(1) != 1:
+            raise ValueError("req_to_token must be a row-major int32 tensor on the device")
+        dev, nreq, n_tiles, total = (prepared["dev"], prepared["nreq"], prepared["n_tiles"],
+                                     prepared["total"])
+        ws = self.workspace
+        ws_aligned = ws[(-ws.data_ptr()) % 256:]
+        off3 = self.offsets
+        status = _native.lib.akv_drop_compact(
+            nreq, _native.ptr(dev["token_offsets"]), _native.ptr(dev["tile_offsets"]), n_tiles,
+            _native.ptr(dev["range_offsets"]), _native.ptr(dev["ranges"]),
+            _native.ptr(dev["shared_prefix"]) if prepared["shared"] else None,
+            _native.ptr(req_to_token), _native.ptr(dev["row_ids"]), req_to_token.stride(0),
+            int(prepared["reposition"]), _native.ptr(ring.ring), ring.capacity,
+            _native.ptr(ring.state), _native.ptr(self.keep_mask), _native.ptr(self.positions),
+            _native.ptr(off3[0]), _native.ptr(self.raw_indices),
+            _native.ptr(self.active_positions), _native.ptr(self.next_position),
+            _native.ptr(off3[1]), _native.ptr(self.transition_source),
+            _native.ptr(self.transition_destination), _native.ptr(self.transition_pairs),
+            _native.ptr(self.transition_raw), _native.ptr(off3[2]), _native.ptr(self.freed_slots),
+            _native.ptr(self.counters[:4]), _native.ptr(self.counters[4:]),
+            _native.ptr(ws_aligned), _native.stream_of(self.device),
+        )
+        _native.check(status, "drop_compact")
+        return DropResult(
+            keep_mask=self.keep_mask[:total], positions=self.positions[:total],
+            active_offsets=off3[0, : nreq + 1], raw_indices=self.raw_indices,
+            active_positions=self.active_positions, next_position=self.next_position[:nreq],
+            transition_offsets=off3[1, : nreq + 1], transition_source=self.transition_source,
+            transition_destination=self.transition_destination,
+            transition_pairs=self.transition_pairs, transition_raw=self.transition_raw,
+            freed_offsets=off3[2, : nreq + 1], freed_slots=self.freed_slots,
+            totals=self.counters[:4], status=self.counters[4:5],
+        )
+
+
+def drop_compact(token_counts, range_offsets, ranges, req_to_token, row_ids, ring,
+                 shared_prefix=None, reposition=True) -> DropResult:
+    """One-shot ``DropCompactor`` sized to this program."""
+    token_counts = np.asarray(token_counts, np.int64)
+    comp = DropCompactor(int(token_counts.sum()), len(token_counts),
+                         max(1, len(np.asarray(ranges)) // 2), req_to_token.device)
+    return comp.run(token_counts, range_offsets, ranges, req_to_token, row_ids, ring,
+                    shared_prefix=shared_prefix, reposition=reposition)

@@ -1,0 +1,103 @@
+// Shared device helpers for the akv_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "akv_b200.h"
+
+namespace akv {
+
+constexpr int kNumSMs = 148;
+
+// Grid sized for a persistent launch: `per_sm` resident blocks on every SM.
+inline int persistent_grid(int per_sm, long long work_blocks) {
+  int device = 0;
+  int sms = kNumSMs;
+  if (cudaGetDevice(&device) == cudaSuccess) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && v > 0)
+      sms = v;
+  }
+  long long cap = (long long)sms * per_sm;
+  long long g = work_blocks < cap ? work_blocks : cap;
+  return g < 1 ? 1 : (int)g;
+}
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
+
+// Load an index stored as int32 or int64 (dtype chosen at run time; the
+// branch is uniform across the grid).
+__device__ __forceinline__ int64_t ld_index(const void* p, int64_t i, int is64) {
+  return is64 ? __ldg(static_cast<const long long*>(p) + i)
+              : (int64_t)__ldg(static_cast<const int*>(p) + i);
+}
+
+__device__ __forceinline__ void st_index(void* p, int64_t i, int is64, int64_t v) {
+  if (is64)
+    static_cast<long long*>(p)[i] = (long long)v;
+  else
+    static_cast<int*>(p)[i] = (int)v;
+}
+
+// Element <-> fp32 conversions.  Loads are exact; stores round to nearest
+// even, as a GPU store of an fp32 value into a 16-bit tensor does.
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f32(float x) { return x; }
+  static __device__ __forceinline__ float from_f32(float x) { return x; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f32(float x) { return __float2bfloat16_rn(x); }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_f32(float x) { return __float2half_rn(x); }
+};
+
+// 16-byte vector of T.
+template <typename T> struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  union {
+    uint4 raw;
+    T e[N];
+  };
+};
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld16(const T* p) {
+  Vec16<T> v;
+  v.raw = *reinterpret_cast<const uint4*>(p);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void st16(T* p, const Vec16<T>& v) {
+  *reinterpret_cast<uint4*>(p) = v.raw;
+}
+
+// Streaming variants: the KV rows are touched once per call, keep them out
+// of L1 and mark them evict-first in L2.
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld16_stream(const T* p) {
+  Vec16<T> v;
+  asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.raw.x), "=r"(v.raw.y), "=r"(v.raw.z), "=r"(v.raw.w)
+               : "l"(p));
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void st16_stream(T* p, const Vec16<T>& v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.raw.x), "r"(v.raw.y),
+               "r"(v.raw.z), "r"(v.raw.w)
+               : "memory");
+}
+
+}  // namespace akv

@@ -1,0 +1,450 @@
+// Drop + Reposition of a batch of requests, computed on the device.
+//
+// For a program with one Drop event and one Reposition at the end of the
+// prompt, the reference's CPU event compiler
+// (akv/system/sglang/kernels/ops/attention/context_plan.py:210-532) walks a
+// linked list token by token.  Its result has a closed form that maps onto
+// one exclusive scan per request:
+//   keep(t)     = t is covered by no drop range
+//   rank(t)     = number of kept tokens before t (the scan)
+//   position(t) = rank(t) if kept (after the Reposition), else t
+//   moved(t)    = kept and rank(t) != t, i.e. t lies after the first drop
+// (tokens are born at positions 0..T-1; the first non-compact token of the
+// reference is the first kept token after the first dropped one, and from
+// there on every kept token moves -- context_plan.py:405-440).
+//
+// Three launches, no inter-block waiting:
+//   1. count   -- per 2048-token tile: keep mask from a difference array of
+//                 the request's drop ranges (shared-memory atomics + block
+//                 scan), four per-tile counters {kept, moved, cow, freed};
+//   2. plan    -- one block: exclusive scan of the tile counters, per-request
+//                 offsets, next_position, free-ring reservation;
+//   3. scatter -- per tile: block scan again, write positions, the compacted
+//                 decode view, transitions (with copy-on-write destinations
+//                 popped from the free ring) and freed slots (pushed on it).
+// Tiles never straddle requests (the host gives per-request tile offsets),
+// so a request's base is the scan value at its first tile.
+
+#include "common.cuh"
+
+namespace akv {
+namespace {
+
+constexpr int kTile = 2048;
+constexpr int kThreads = 256;
+constexpr int kPerThread = kTile / kThreads;  // 8 contiguous tokens per thread
+constexpr int kPlanThreads = 1024;
+constexpr int kFields = 4;  // kept, moved, cow, freed
+
+// Field packing for the block scan: 16 bits per counter (a tile holds at
+// most 2048 tokens, so no field overflows into the next).
+__device__ __forceinline__ unsigned long long pack4(int a, int b, int c, int d) {
+  return (unsigned long long)a | ((unsigned long long)b << 16) | ((unsigned long long)c << 32) |
+         ((unsigned long long)d << 48);
+}
+__device__ __forceinline__ int field(unsigned long long v, int f) {
+  return (int)((v >> (16 * f)) & 0xffffull);
+}
+
+// Block-wide exclusive scan built from warp shuffles.  Returns the
+// exclusive prefix of `v` and writes the block total to *total.
+template <typename U>
+__device__ U block_exclusive_scan(U v, U* total) {
+  __shared__ U warp_sums[32];
+  __shared__ U block_total;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  U inc = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    U o = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += o;
+  }
+  if (lane == 31) warp_sums[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    U w = lane < nwarps ? warp_sums[lane] : U(0);
+    U winc = w;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      U o = __shfl_up_sync(0xffffffffu, winc, d);
+      if (lane >= d) winc += o;
+    }
+    if (lane < nwarps) warp_sums[lane] = winc - w;  // exclusive base of each warp
+    if (lane == 31) block_total = winc;
+  }
+  __syncthreads();
+  const U base = warp_sums[warp];
+  *total = block_total;
+  __syncthreads();  // the next call may overwrite warp_sums
+  return base + inc - v;
+}
+
+struct Workspace {
+  int* tile_sums;   // [n_tiles][5]: four counters + bad-range flag
+  int* tile_base;   // [n_tiles][4]: exclusive scan of the counters
+  int* first_drop;  // [R]: smallest drop start of the request (INT_MAX if none)
+  long long* plan;  // {ring head, ring tail, status}
+};
+
+__host__ __device__ inline size_t align_up(size_t x) { return (x + 255) & ~size_t(255); }
+
+__host__ __device__ inline Workspace carve(void* base, int n_requests, int n_tiles) {
+  char* p = static_cast<char*>(base);
+  Workspace w;
+  w.tile_sums = reinterpret_cast<int*>(p);
+  p += align_up(sizeof(int) * 5 * (size_t)(n_tiles > 0 ? n_tiles : 1));
+  w.tile_base = reinterpret_cast<int*>(p);
+  p += align_up(sizeof(int) * 4 * (size_t)(n_tiles > 0 ? n_tiles : 1));
+  w.first_drop = reinterpret_cast<int*>(p);
+  p += align_up(sizeof(int) * (size_t)(n_requests > 0 ? n_requests : 1));
+  w.plan = reinterpret_cast<long long*>(p);
+  return w;
+}
+
+inline size_t workspace_bytes(int n_requests, int n_tiles) {
+  const size_t nt = n_tiles > 0 ? n_tiles : 1, nr = n_requests > 0 ? n_requests : 1;
+  return align_up(sizeof(int) * 5 * nt) + align_up(sizeof(int) * 4 * nt) +
+         align_up(sizeof(int) * nr) + align_up(sizeof(long long) * 4);
+}
+
+struct DropArgs {
+  int n_requests;
+  const int64_t* token_offsets;
+  const int32_t* tile_offsets;
+  int n_tiles;
+  const int32_t* range_offsets;
+  const int32_t* ranges;
+  const int32_t* shared_prefix;
+  int32_t* req_to_token;
+  const int64_t* row_ids;
+  int64_t row_stride;
+  int reposition;
+  int32_t* ring;
+  int64_t ring_capacity;
+  int64_t* ring_state;
+  uint8_t* keep_mask;
+  int32_t* positions;
+  int32_t* active_offsets;
+  int32_t* raw_indices;
+  int32_t* active_positions;
+  int32_t* next_position;
+  int32_t* transition_offsets;
+  int32_t* transition_source;
+  int32_t* transition_destination;
+  int32_t* transition_pairs;
+  int32_t* transition_raw;
+  int32_t* freed_offsets;
+  int32_t* freed_slots;
+  int32_t* totals;
+  int32_t* status;
+  Workspace ws;
+};
+
+// Request owning tile `tile`: the r with tile_offsets[r] <= tile < tile_offsets[r+1].
+__device__ int tile_request(const int32_t* tile_offsets, int n_requests, int tile) {
+  int lo = 0, hi = n_requests;  // search in [0, R]
+  while (lo < hi) {             // first r with tile_offsets[r] > tile
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(tile_offsets + mid) <= tile) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo - 1;
+}
+
+struct TileCtx {
+  int r, t0, n, T, P;
+  long long flat0;
+};
+
+__device__ TileCtx tile_context(const DropArgs& a, int tile) {
+  TileCtx c;
+  c.r = tile_request(a.tile_offsets, a.n_requests, tile);
+  const long long begin = a.token_offsets[c.r];
+  c.T = (int)(a.token_offsets[c.r + 1] - begin);
+  c.t0 = (tile - a.tile_offsets[c.r]) * kTile;
+  const int t1 = min(c.T, c.t0 + kTile);
+  c.n = t1 - c.t0;
+  c.P = a.shared_prefix ? a.shared_prefix[c.r] : 0;
+  c.flat0 = begin + c.t0;
+  return c;
+}
+
+__global__ void __launch_bounds__(kThreads) drop_count_kernel(const DropArgs a) {
+  __shared__ int diff[kTile + 1];
+  __shared__ int s_first, s_bad;
+  const int tile = blockIdx.x;
+  const TileCtx c = tile_context(a, tile);
+  for (int i = threadIdx.x; i <= kTile; i += blockDim.x) diff[i] = 0;
+  if (threadIdx.x == 0) {
+    s_first = INT_MAX;
+    s_bad = 0;
+  }
+  __syncthreads();
+  const int rb = a.range_offsets[c.r], re = a.range_offsets[c.r + 1];
+  int first = INT_MAX, bad = 0;
+  for (int i = rb + threadIdx.x; i < re; i += blockDim.x) {
+    const int s = a.ranges[2 * i], e = a.ranges[2 * i + 1];
+    if (s < 0 || e > c.T || s >= e) {
+      bad = 1;
+      continue;
+    }
+    first = min(first, s);
+    const int cs = max(s, c.t0), ce = min(e, c.t0 + c.n);
+    if (cs < ce) {
+      atomicAdd(&diff[cs - c.t0], 1);
+      atomicAdd(&diff[ce - c.t0], -1);
+    }
+  }
+  if (first != INT_MAX) atomicMin(&s_first, first);
+  if (bad) atomicOr(&s_bad, 1);
+  __syncthreads();
+
+  const int base = threadIdx.x * kPerThread;
+  int local = 0;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) local += diff[base + k];
+  int unused;
+  int cover = block_exclusive_scan<int>(local, &unused);
+  const int first_drop = s_first;
+  int kept = 0, moved = 0, cow = 0, freed = 0;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = base + k;
+    cover += diff[i];
+    if (i < c.n) {
+      const int t = c.t0 + i;
+      const bool keep = cover == 0;
+      const bool mv = a.reposition && keep && t > first_drop;
+      kept += keep;
+      moved += mv;
+      cow += mv && t < c.P;
+      freed += !keep && t >= c.P;
+      a.keep_mask[c.flat0 + i] = keep ? 1 : 0;
+    }
+  }
+  unsigned long long tot;
+  block_exclusive_scan<unsigned long long>(pack4(kept, moved, cow, freed), &tot);
+  if (threadIdx.x == 0) {
+    int* ts = a.ws.tile_sums + 5 * (size_t)tile;
+    for (int f = 0; f < kFields; ++f) ts[f] = field(tot, f);
+    ts[4] = s_bad;
+    if (c.t0 == 0) a.ws.first_drop[c.r] = first_drop;
+  }
+}
+
+__global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs a) {
+  __shared__ int s_bad;
+  __shared__ long long s_carry[kFields];
+  if (threadIdx.x == 0) {
+    s_bad = 0;
+    for (int f = 0; f < kFields; ++f) s_carry[f] = 0;
+  }
+  __syncthreads();
+  // Exclusive scan of the per-tile counters, 1024 tiles per round.
+  for (int t0 = 0; t0 < a.n_tiles; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    int v[kFields] = {0, 0, 0, 0};
+    if (t < a.n_tiles) {
+      const int* ts = a.ws.tile_sums + 5 * (size_t)t;
+      for (int f = 0; f < kFields; ++f) v[f] = ts[f];
+      if (ts[4]) atomicOr(&s_bad, 1);
+    }
+    for (int f = 0; f < kFields; ++f) {
+      int tot;
+      const int ex = block_exclusive_scan<int>(v[f], &tot);
+      if (t < a.n_tiles) a.ws.tile_base[4 * (size_t)t + f] = (int)(s_carry[f] + ex);
+      __syncthreads();
+      if (threadIdx.x == 0) s_carry[f] += tot;
+      __syncthreads();
+    }
+  }
+  const long long total_kept = s_carry[0], total_moved = s_carry[1], total_cow = s_carry[2],
+                  total_freed = s_carry[3];
+  __shared__ int s_no_active;
+  if (threadIdx.x == 0) s_no_active = 0;
+  __syncthreads();
+  auto base_at = [&](int tile, int f) -> int {
+    return tile < a.n_tiles ? a.ws.tile_base[4 * (size_t)tile + f] : (int)s_carry[f];
+  };
+  for (int r = threadIdx.x; r < a.n_requests; r += blockDim.x) {
+    const int tb = a.tile_offsets[r], te = a.tile_offsets[r + 1];
+    const int kb = base_at(tb, 0), ke = base_at(te, 0);
+    const int mb = base_at(tb, 1), me = base_at(te, 1);
+    const int T = (int)(a.token_offsets[r + 1] - a.token_offsets[r]);
+    a.active_offsets[r] = kb;
+    a.transition_offsets[r] = mb;
+    a.freed_offsets[r] = base_at(tb, 3);
+    const int active = ke - kb, moved = me - mb;
+    a.next_position[r] = (a.reposition && moved > 0) ? active : T;
+    if (a.reposition && T > 0 && active == 0) atomicOr(&s_no_active, 1);
+    if (te == tb) a.ws.first_drop[r] = INT_MAX;  // empty request: no tile wrote it
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    a.active_offsets[a.n_requests] = (int)total_kept;
+    a.transition_offsets[a.n_requests] = (int)total_moved;
+    a.freed_offsets[a.n_requests] = (int)total_freed;
+    a.totals[0] = (int)total_kept;
+    a.totals[1] = (int)total_moved;
+    a.totals[2] = (int)total_cow;
+    a.totals[3] = (int)total_freed;
+    int st = 0;
+    if (s_bad) st |= AKV_DROP_BAD_RANGE;
+    if (s_no_active) st |= AKV_DROP_NO_ACTIVE;
+    const long long head = a.ring_state[0], tail = a.ring_state[1];
+    if (total_cow > tail - head) st |= AKV_DROP_RING_UNDERFLOW;
+    else if (tail - head - total_cow + total_freed > a.ring_capacity) st |= AKV_DROP_RING_OVERFLOW;
+    a.ws.plan[0] = head;
+    a.ws.plan[1] = tail;
+    a.ws.plan[2] = st;
+    if (st == 0) {
+      a.ring_state[0] = head + total_cow;
+      a.ring_state[1] = tail + total_freed;
+    } else {
+      // All or nothing: no transition, copy-on-write or freed slot is
+      // emitted, so a failed call leaves the free ring and rows untouched.
+      a.totals[1] = 0;
+      a.totals[2] = 0;
+      a.totals[3] = 0;
+    }
+    *a.status = st;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a) {
+  if (a.ws.plan[2] != 0) return;
+  const int tile = blockIdx.x;
+  const TileCtx c = tile_context(a, tile);
+  const int first_drop = a.ws.first_drop[c.r];
+  const int base = threadIdx.x * kPerThread;
+  bool keep[kPerThread];
+  int kept = 0, moved = 0, cow = 0, freed = 0;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = base + k;
+    keep[k] = i < c.n && a.keep_mask[c.flat0 + i] != 0;
+    if (i < c.n) {
+      const int t = c.t0 + i;
+      const bool mv = a.reposition && keep[k] && t > first_drop;
+      kept += keep[k];
+      moved += mv;
+      cow += mv && t < c.P;
+      freed += !keep[k] && t >= c.P;
+    }
+  }
+  unsigned long long tot;
+  const unsigned long long ex =
+      block_exclusive_scan<unsigned long long>(pack4(kept, moved, cow, freed), &tot);
+  const int* tb = a.ws.tile_base + 4 * (size_t)tile;
+  int gk = tb[0] + field(ex, 0);
+  int gm = tb[1] + field(ex, 1);
+  int gc = tb[2] + field(ex, 2);
+  int gf = tb[3] + field(ex, 3);
+  const int req_kept_base = a.active_offsets[c.r];
+  int32_t* row = a.req_to_token + a.row_ids[c.r] * a.row_stride;
+  const long long head = a.ws.plan[0], tail = a.ws.plan[1];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = base + k;
+    if (i >= c.n) break;
+    const int t = c.t0 + i;
+    if (keep[k]) {
+      const int rank = gk - req_kept_base;
+      const int pos = a.reposition ? rank : t;
+      a.positions[c.flat0 + i] = pos;
+      a.raw_indices[gk] = t;
+      a.active_positions[gk] = pos;
+      ++gk;
+      if (a.reposition && t > first_drop) {
+        const int slot = row[t];
+        int dst = slot;
+        if (t < c.P) {
+          dst = a.ring[(head + gc) % a.ring_capacity];
+          row[t] = dst;
+          ++gc;
+        }
+        a.transition_source[gm] = slot;
+        a.transition_destination[gm] = dst;
+        a.transition_pairs[2 * (size_t)gm] = t;
+        a.transition_pairs[2 * (size_t)gm + 1] = rank;
+        a.transition_raw[gm] = t;
+        ++gm;
+      }
+    } else {
+      a.positions[c.flat0 + i] = t;
+      if (t >= c.P) {
+        const int slot = row[t];
+        a.freed_slots[gf] = slot;
+        a.ring[(tail + gf) % a.ring_capacity] = slot;
+        ++gf;
+      }
+    }
+  }
+}
+
+}  // namespace
+}  // namespace akv
+
+extern "C" int64_t akv_drop_compact_tile_tokens(void) { return akv::kTile; }
+
+extern "C" int64_t akv_drop_compact_workspace_bytes(int32_t n_requests, int32_t n_tiles) {
+  return (int64_t)akv::workspace_bytes(n_requests, n_tiles);
+}
+
+extern "C" int akv_drop_compact(
+    int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
+    int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
+    const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
+    int64_t row_stride, int32_t reposition, int32_t* ring, int64_t ring_capacity,
+    int64_t* ring_state, uint8_t* keep_mask, int32_t* positions, int32_t* active_offsets,
+    int32_t* raw_indices, int32_t* active_positions, int32_t* next_position,
+    int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
+    int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
+    int32_t* freed_slots, int32_t* totals, int32_t* status, void* workspace, void* stream) {
+  using namespace akv;
+  if (n_requests < 0 || n_tiles < 0 || ring_capacity <= 0 || !token_offsets || !tile_offsets ||
+      !range_offsets || !req_to_token || !row_ids || !ring || !ring_state || !keep_mask ||
+      !positions || !active_offsets || !raw_indices || !active_positions || !next_position ||
+      !transition_offsets || !transition_source || !transition_destination ||
+      !transition_pairs || !transition_raw || !freed_offsets || !freed_slots || !totals ||
+      !status || !workspace)
+    return AKV_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return AKV_ERR_INVALID;
+  DropArgs a;
+  a.n_requests = n_requests;
+  a.token_offsets = token_offsets;
+  a.tile_offsets = tile_offsets;
+  a.n_tiles = n_tiles;
+  a.range_offsets = range_offsets;
+  a.ranges = ranges;
+  a.shared_prefix = shared_prefix;
+  a.req_to_token = req_to_token;
+  a.row_ids = row_ids;
+  a.row_stride = row_stride;
+  a.reposition = reposition != 0;
+  a.ring = ring;
+  a.ring_capacity = ring_capacity;
+  a.ring_state = ring_state;
+  a.keep_mask = keep_mask;
+  a.positions = positions;
+  a.active_offsets = active_offsets;
+  a.raw_indices = raw_indices;
+  a.active_positions = active_positions;
+  a.next_position = next_position;
+  a.transition_offsets = transition_offsets;
+  a.transition_source = transition_source;
+  a.transition_destination = transition_destination;
+  a.transition_pairs = transition_pairs;
+  a.transition_raw = transition_raw;
+  a.freed_offsets = freed_offsets;
+  a.freed_slots = freed_slots;
+  a.totals = totals;
+  a.status = status;
+  a.ws = carve(workspace, n_requests, n_tiles);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n_tiles > 0) drop_count_kernel<<<n_tiles, kThreads, 0, s>>>(a);
+  drop_plan_kernel<<<1, kPlanThreads, 0, s>>>(a);
+  if (n_tiles > 0) drop_scatter_kernel<<<n_tiles, kThreads, 0, s>>>(a);
+  return launch_status();
+}

@@ -1,0 +1,247 @@
+// Decode page-table kernels over the compacted active-index view.
+//
+// Replace the reference's Triton kernels context_decode_indices and
+// context_window_lengths
+// (akv/system/sglang/kernels/ops/attention/context_page_table.py:7-76) and
+// write_row_slots (akv/system/sglang/kernels/ops/memory/context_rows.py:7-15).
+// The Triton decode-index kernel runs one program per request that walks
+// the request's whole length 256 indices at a time, so a 64K-token request
+// serialises on one SM.  Here each request is split over several blocks
+// (grid = splits x batch) that stride through it, so the batch's total
+// length is spread over every SM whatever the length distribution.
+
+#include "common.cuh"
+
+namespace akv {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Registry row: {raw_ids*, positions*, prompt_len, active, next_pos, row*}
+// (srt/layers/attention/context_backend.py:716-725).
+struct Entry {
+  const int32_t* raw_ids;
+  const int32_t* positions;
+  int32_t prompt;
+  int32_t active;
+  int32_t next_pos;
+  const int32_t* row;
+};
+
+__device__ __forceinline__ Entry load_entry(const int64_t* registry, int64_t row) {
+  const long long* e = reinterpret_cast<const long long*>(registry) + row * 6;
+  Entry x;
+  x.raw_ids = reinterpret_cast<const int32_t*>(e[0]);
+  x.positions = reinterpret_cast<const int32_t*>(e[1]);
+  x.prompt = (int32_t)e[2];
+  x.active = (int32_t)e[3];
+  x.next_pos = (int32_t)e[4];
+  x.row = reinterpret_cast<const int32_t*>(e[5]);
+  return x;
+}
+
+struct IndexArgs {
+  const int64_t* registry;
+  const int32_t* table;
+  int64_t row_stride;
+  const void* row_ids;
+  int row_ids_is64;
+  const void* lengths;
+  int lengths_is64;
+  const void* indptr;
+  int indptr_is64;
+  void* output;
+  int output_is64;
+  const void* starts;
+  int starts_is64;
+  const void* mapping;
+  int mapping_is64;
+  int64_t multiplier;
+};
+
+__global__ void __launch_bounds__(kThreads) decode_indices_kernel(const IndexArgs a) {
+  const int b = blockIdx.y;
+  const int64_t row = ld_index(a.row_ids, b, a.row_ids_is64);
+  const int64_t length = ld_index(a.lengths, b, a.lengths_is64);
+  const int64_t offset = ld_index(a.indptr, b, a.indptr_is64);
+  const int64_t start = a.starts ? ld_index(a.starts, b, a.starts_is64) : 0;
+  const Entry e = load_entry(a.registry, row);
+  const bool context = e.raw_ids != nullptr;
+  const int32_t* raw_row = e.row != nullptr ? e.row : a.table + row * a.row_stride;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < length; i += step) {
+    const int64_t logical = start + i;
+    int64_t raw = logical;
+    if (context)
+      raw = logical < e.active ? (int64_t)__ldg(e.raw_ids + logical)
+                               : (int64_t)e.prompt + logical - e.active;
+    int64_t slot = __ldg(raw_row + raw);
+    if (a.mapping) slot = ld_index(a.mapping, slot, a.mapping_is64) * a.multiplier;
+    st_index(a.output, offset + i, a.output_is64, slot);
+  }
+}
+
+__device__ __forceinline__ int64_t window_length(const Entry& e, int64_t length, int64_t window) {
+  if (e.raw_ids == nullptr) return length < window ? length : window;
+  const int64_t generated = length - e.active;
+  // The window is the inclusive distance q_pos - k_pos (context_page_table.py:19-20).
+  const int64_t lower = (int64_t)e.next_pos + generated - 1 - window;
+  int32_t lo = 0, hi = e.active;
+  while (lo < hi) {
+    const int32_t mid = (lo + hi) >> 1;
+    if ((int64_t)__ldg(e.positions + mid) < lower) lo = mid + 1;
+    else hi = mid;
+  }
+  const int64_t skipped = lower - e.next_pos > 0 ? lower - e.next_pos : 0;
+  return (int64_t)e.active - lo + generated - skipped;
+}
+
+__global__ void __launch_bounds__(kThreads) window_lengths_kernel(
+    const int64_t* registry, const void* row_ids, int row_ids_is64, const void* lengths,
+    int lengths_is64, void* output, int output_is64, int64_t window, int batch) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const Entry e = load_entry(registry, ld_index(row_ids, b, row_ids_is64));
+  st_index(output, b, output_is64, window_length(e, ld_index(lengths, b, lengths_is64), window));
+}
+
+// One block: lengths (windowed or not), their exclusive scan into kv_indptr,
+// and starts = seq_len - length.
+__global__ void __launch_bounds__(1024) decode_lengths_scan_kernel(
+    const int64_t* registry, const int64_t* row_ids, const int64_t* seq_lens, int64_t window,
+    int batch, int32_t* kv_indptr, int64_t* lengths_out, int64_t* starts_out) {
+  __shared__ long long warp_sums[32];
+  __shared__ long long carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int b0 = 0; b0 < batch; b0 += blockDim.x) {
+    const int b = b0 + threadIdx.x;
+    long long len = 0, seq = 0;
+    if (b < batch) {
+      seq = seq_lens[b];
+      len = seq;
+      if (window >= 0) len = window_length(load_entry(registry, row_ids[b]), seq, window);
+    }
+    long long inc = len;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const long long o = __shfl_up_sync(0xffffffffu, inc, d);
+      if (lane >= d) inc += o;
+    }
+    if (lane == 31) warp_sums[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+      const long long w = warp_sums[lane];
+      long long winc = w;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const long long o = __shfl_up_sync(0xffffffffu, winc, d);
+        if (lane >= d) winc += o;
+      }
+      warp_sums[lane] = winc - w;
+    }
+    __syncthreads();
+    const long long excl = carry + warp_sums[warp] + inc - len;
+    if (b < batch) {
+      kv_indptr[b] = (int32_t)excl;
+      if (lengths_out) lengths_out[b] = len;
+      if (starts_out) starts_out[b] = seq - len;
+      if (b == batch - 1) kv_indptr[batch] = (int32_t)(excl + len);
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = excl + len;
+    __syncthreads();
+  }
+  if (batch == 0 && threadIdx.x == 0) kv_indptr[0] = 0;
+}
+
+__global__ void write_row_slots_kernel(const int64_t* pointers, const void* rows, int rows_is64,
+                                       const void* cols, int cols_is64, const void* values,
+                                       int values_is64, int64_t n) {
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    int32_t* row = reinterpret_cast<int32_t*>(pointers[ld_index(rows, i, rows_is64)]);
+    row[ld_index(cols, i, cols_is64)] = (int32_t)ld_index(values, i, values_is64);
+  }
+}
+
+int split_count(int batch) {
+  // About 8 resident blocks per SM in total, at most 256 per request.
+  long long want = (long long)kNumSMs * 8 / (batch > 0 ? batch : 1);
+  if (want < 1) want = 1;
+  if (want > 256) want = 256;
+  return (int)want;
+}
+
+}  // namespace
+}  // namespace akv
+
+extern "C" int akv_context_decode_indices(
+    const int64_t* registry, const int32_t* req_to_token, int64_t row_stride,
+    const void* row_ids, int32_t row_ids_is64, const void* lengths, int32_t lengths_is64,
+    const void* indptr, int32_t indptr_is64, void* output, int32_t output_is64,
+    const void* starts, int32_t starts_is64, const void* mapping, int32_t mapping_is64,
+    int64_t multiplier, int32_t batch, void* stream) {
+  using namespace akv;
+  if (batch < 0 || batch > 65535 || !registry || !req_to_token || !row_ids || !lengths ||
+      !indptr || !output)
+    return AKV_ERR_INVALID;
+  if (batch == 0) return AKV_OK;
+  IndexArgs a{registry, req_to_token, row_stride, row_ids, row_ids_is64, lengths, lengths_is64,
+              indptr, indptr_is64, output, output_is64, starts, starts_is64, mapping,
+              mapping_is64, multiplier};
+  dim3 grid(split_count(batch), batch);
+  decode_indices_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status();
+}
+
+extern "C" int akv_context_window_lengths(
+    const int64_t* registry, const void* row_ids, int32_t row_ids_is64, const void* lengths,
+    int32_t lengths_is64, void* output, int32_t output_is64, int64_t window, int32_t batch,
+    void* stream) {
+  using namespace akv;
+  if (batch < 0 || !registry || !row_ids || !lengths || !output) return AKV_ERR_INVALID;
+  if (batch == 0) return AKV_OK;
+  window_lengths_kernel<<<(batch + kThreads - 1) / kThreads, kThreads, 0,
+                          static_cast<cudaStream_t>(stream)>>>(
+      registry, row_ids, row_ids_is64, lengths, lengths_is64, output, output_is64, window, batch);
+  return launch_status();
+}
+
+extern "C" int akv_build_decode_metadata(
+    const int64_t* registry, const int32_t* req_to_token, int64_t row_stride,
+    const int64_t* row_ids, const int64_t* seq_lens, int64_t window, const int64_t* mapping,
+    int64_t multiplier, int32_t batch, int32_t* kv_indptr, int64_t* lengths_out,
+    int64_t* starts_out, int32_t* kv_indices, void* stream) {
+  using namespace akv;
+  if (batch < 0 || batch > 65535 || !registry || !req_to_token || !row_ids || !seq_lens ||
+      !kv_indptr || !kv_indices)
+    return AKV_ERR_INVALID;
+  if (window >= 0 && (!lengths_out || !starts_out)) return AKV_ERR_INVALID;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  decode_lengths_scan_kernel<<<1, 1024, 0, s>>>(registry, row_ids, seq_lens, window, batch,
+                                                 kv_indptr, lengths_out, starts_out);
+  if (batch == 0) return launch_status();
+  IndexArgs a{registry, req_to_token, row_stride, row_ids, 1,
+              window >= 0 ? (const void*)lengths_out : (const void*)seq_lens, 1, kv_indptr, 0,
+              kv_indices, 0, window >= 0 ? starts_out : nullptr, 1, mapping, 1, multiplier};
+  dim3 grid(split_count(batch), batch);
+  decode_indices_kernel<<<grid, kThreads, 0, s>>>(a);
+  return launch_status();
+}
+
+extern "C" int akv_write_row_slots(const int64_t* pointers, const void* rows, int32_t rows_is64,
+                                   const void* columns, int32_t columns_is64, const void* values,
+                                   int32_t values_is64, int64_t n, void* stream) {
+  using namespace akv;
+  if (n < 0 || (n > 0 && (!pointers || !rows || !columns || !values))) return AKV_ERR_INVALID;
+  if (n == 0) return AKV_OK;
+  const int blocks = (int)((n + kThreads - 1) / kThreads < 1024 ? (n + kThreads - 1) / kThreads
+                                                                 : 1024);
+  write_row_slots_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      pointers, rows, rows_is64, columns, columns_is64, values, values_is64, n);
+  return launch_status();
+}
+
+extern "C" const char* akv_version(void) { return "akv_b200 0.1 (sm_100a)"; }

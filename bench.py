@@ -1,0 +1,480 @@
+#!/usr/bin/env python
+"""Benchmark of the AKV cache-operation hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c1|c5]
+
+Metric: reposition+drop retained-KV GB/s (algorithmic bytes / time).  At
+N = 1 the workload is c2, the GPT-OSS-120B-shaped cache: one 65536-token
+request, 36 layers, 8 KV heads, head_dim 64, bf16, about 40 % dropped in
+20 spans, Reposition with YaRN RoPE.  One step = one Drop + Reposition:
+``DropCompactor`` (keep mask, scan, decode view, transitions, freed slots on
+the device; three launches) followed by one ``reposition_kv_layers`` launch
+over all 36 layers driven by the device-side transition count.  Moved
+tokens are private to the request, so they are rotated in place.
+
+Algorithmic bytes per step (per GPU): reposition, in place: per moved token,
+layer and local head 2 * rotary_dim * 2 bytes (read + write the rotary
+part); drop: T (keep mask) + 4 T (slot row) + 8 A (decode view) + 4 (T - A)
+(freed slots) + 12 per transition.  KV inputs (2.4 GB of K) exceed the
+126 MB L2, so no flush is needed between steps.
+
+Multi-GPU: one process per GPU (torchrun); KV heads are split 8 / N per
+rank as in SGLang tensor parallelism and every rank computes the same drop
+metadata (the scheduler state is replicated per TP rank); no collective on
+the data path, a barrier around the timed region and a MAX all-reduce of
+the timings afterwards.  The workload is fixed as N grows (strong
+scaling); the aggregate counts every rank's bytes.
+
+``--impl reference``: the reference's CPU implementation of the path on the
+host cores (rank 0 only): its own C++ event compiler (oracle/_ref, built
+from the reference sources) + the decode view in numpy + the CPU
+restatement of its reposition kernel (the reference has no CPU reposition),
+each step a bounded sample of the reposition scaled to the full step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "reposition+drop retained-KV GB/s"
+UNIT = "GB/s"
+
+WORKLOADS = {
+    # name: (layers, kv heads, head_dim, rope)
+    "c1": (1, 8, 64, "rope10000"),
+    "c2": (36, 8, 64, "yarn"),
+    "c5": (80, 8, 128, "rope500000"),
+}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    return p.parse_args()
+
+
+def program_for(name):
+    from akv_b200 import workloads
+
+    if name == "c1":
+        return workloads.c1_program()
+    if name == "c2":
+        return workloads.c2_program()
+    if name == "c5":
+        return workloads.c5_program(requests=1)
+    raise ValueError(name)
+
+
+def cos_sin(name, dim, max_pos):
+    from akv_b200.rope import rope_cos_sin_cache, yarn_cos_sin_cache
+
+    rope = WORKLOADS[name][3]
+    if rope == "yarn":
+        return yarn_cos_sin_cache(max_pos, dim, 150000.0, 32.0, 4096)
+    return rope_cos_sin_cache(max_pos, dim, float(rope[4:]))
+
+
+def plan_stats(prog):
+    """Host-side closed form of the single-stage program: kept tokens and
+    moved tokens per request (what the kernels will produce)."""
+    kept, moved = 0, 0
+    for r in range(prog.requests):
+        keep = prog.keep_mask(r)
+        kept += int(keep.sum())
+        dropped = np.flatnonzero(~keep)
+        if len(dropped):
+            moved += int((keep & (np.arange(len(keep)) > dropped[0])).sum())
+    return prog.total_tokens, kept, moved
+
+
+def algorithmic_bytes(prog, heads_local, layers, dim, rot, elem=2):
+    t, a, n = plan_stats(prog)
+    reposition = n * layers * heads_local * 2 * rot * elem
+    drop = t + 4 * t + 8 * a + 4 * (t - a) + 12 * n
+    return reposition, drop
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic(workload):
+    """Per-launch DRAM bytes of the reposition kernel from the committed ncu
+    summary (profiles/), scaled to this workload; None if not captured."""
+    path = os.path.join(ROOT, "profiles", f"reposition_{workload}.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during a timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.out = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            ident = str(device_index)
+        self.ident = ident
+
+    def start(self):
+        try:
+            self.out = open(os.devnull, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.ident],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            text, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            text = ""
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in text.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[2:6]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def dist_max(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dist_barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng, threads):
+    """One step of the reference's CPU path: its C++ event compiler
+    (oracle/_ref) + numpy decode view + the reposition restatement over a
+    sample of the moved tokens.  Returns (seconds scaled to the full step,
+    sample size)."""
+    from oracle import oracle, reference
+
+    t0 = time.perf_counter()
+    lays = []
+    for r in range(prog.requests):
+        t = int(prog.token_counts[r])
+        rr = prog.request_ranges(r)
+        has = len(rr) > 0
+        comp = reference.compile_context_layout if reference.available() else \
+            oracle.compile_layout
+        lay = comp(np.zeros(t, np.int32), [t] if has else [], [0, len(rr) // 2] if has else [0],
+                   rr, [t - 1], [t])
+        raw = np.flatnonzero(lay["keep_mask"]).astype(np.int32)
+        _ = lay["positions"][raw]
+        lays.append(lay)
+    t_drop = time.perf_counter() - t0
+    lay = lays[0]
+    moved = lay["transition_raw_tokens"]
+    n = len(moved)
+    m = min(sample, n)
+    pick = rng.choice(n, size=m, replace=False) if m < n else np.arange(n)
+    slots = rows[0][moved[pick]].astype(np.int32)
+    pairs = np.stack((lay["transition_old_positions"][pick],
+                      lay["transition_new_positions"][pick]), 1).astype(np.int32)
+    # K rows of the sampled tokens, all layers, as bf16 bit patterns; the
+    # in-place rotation reads and writes exactly these rows.
+    k = [np.random.default_rng(l).integers(0, 1 << 16, size=(m, heads, dim), dtype=np.uint16)
+         & 0x7F7F for l in range(layers)]
+    idx = np.arange(m, dtype=np.int32)
+    t1 = time.perf_counter()
+    oracle.reposition(k, k, idx, idx, pairs, cache_np, bf16=True, threads=threads)
+    t_rep = time.perf_counter() - t1
+    del slots
+    return t_drop + t_rep * (n / max(1, m)), m, n
+
+
+def run_reference(args):
+    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    if rank != 0:
+        return 0
+    from akv_b200 import workloads
+
+    layers, heads, dim, _ = WORKLOADS[args.workload]
+    prog = program_for(args.workload)
+    rows, _ = workloads.slot_rows(np.random.default_rng(0), prog)
+    cache_np = cos_sin(args.workload, dim, 131072).numpy()
+    threads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(0)
+    rep_bytes, drop_bytes = algorithmic_bytes(prog, heads, layers, dim, dim)
+    sample = 4000
+    for _ in range(args.warmup):
+        cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng, threads)
+    times = []
+    for _ in range(args.steps):
+        s, m, n = cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng,
+                                     threads)
+        times.append(s)
+    sec = sum(times)
+    value = (rep_bytes + drop_bytes) * args.steps / sec / 1e9
+    from oracle import reference
+
+    kind = "reference" if reference.available() else "port"
+    desc = (f"{args.workload}: event compiler over all {prog.total_tokens} tokens "
+            f"({'reference C++ from oracle/_ref' if kind == 'reference' else 'oracle port'}) + "
+            f"decode view; reposition restatement on {m} of {n} moved tokens x {layers} layers "
+            f"x {heads} heads per step, time scaled to all {n}")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * sec / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": args.workload, "layers": layers, "kv_heads": heads, "head_dim": dim,
+                   "tokens": prog.total_tokens},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": desc},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from akv_b200 import workloads
+    from akv_b200.context_drop import DropCompactor, FreeSlotRing
+    from akv_b200.context_reposition import layer_pointer_table, reposition_kv_layers
+
+    layers, heads_total, dim, _ = WORKLOADS[args.workload]
+    if heads_total % world:
+        raise SystemExit(f"{heads_total} KV heads do not split over {world} GPUs")
+    heads = heads_total // world
+    prog = program_for(args.workload)
+    rows, nslots = workloads.slot_rows(np.random.default_rng(0), prog)
+    total, kept, moved = plan_stats(prog)
+    freed_per_step = total - kept
+
+    # KV pools of this rank's heads, [slot, head, dim] per layer.
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    k_pools = [torch.randn(nslots, heads, dim, device=dev, generator=g).to(torch.bfloat16)
+               for _ in range(layers)]
+    v_pools = [torch.empty(nslots, heads, dim, device=dev, dtype=torch.bfloat16)
+               for _ in range(layers)]
+    k_ptrs, v_ptrs = layer_pointer_table(k_pools), layer_pointer_table(v_pools)
+    cache = cos_sin(args.workload, dim, 131072).to(dev)
+    table = np.zeros((prog.requests + 1, int(prog.token_counts.max())), np.int32)
+    for r in range(prog.requests):
+        table[r + 1, : len(rows[r])] = rows[r]
+    req_to_token = torch.from_numpy(table).to(dev)
+    row_ids = np.arange(1, prog.requests + 1)
+    steps_total = args.warmup + 2 * args.steps + 4
+    ring = FreeSlotRing(torch.zeros(0, dtype=torch.int32),
+                        capacity=freed_per_step * steps_total + 16, device=dev)
+    comp = DropCompactor(total, prog.requests, max(1, len(prog.ranges) // 2), dev)
+    stream = torch.cuda.current_stream(dev)
+
+    prepared = comp.prepare(prog.token_counts, prog.range_offsets, prog.ranges, row_ids)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+
+    def step(i=None):
+        if i is not None:
+            ev[i][0].record(stream)
+        res = comp.launch(prepared, req_to_token, ring)
+        if i is not None:
+            ev[i][1].record(stream)
+        reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
+                             res.transition_destination, res.transition_pairs, cache,
+                             count_device=res.transition_count)
+        if i is not None:
+            ev[i][2].record(stream)
+        return res
+
+    for _ in range(args.warmup):
+        res = step()
+    torch.cuda.synchronize()
+    res.check()
+    assert int(res.totals[1].item()) == moved
+
+    clocks = ClockSampler(local)
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    clock_info = clocks.stop()
+    ms = t_start.elapsed_time(t_end)
+    drop_ms = [a.elapsed_time(b) for a, b, _ in ev]
+    rep_ms = [b.elapsed_time(c) for _, b, c in ev]
+    ms = dist_max(ms, world)
+
+    # e2e: through the public API with the program in host memory: validate,
+    # stage (one pinned H2D copy), launch, and read the decode view back.
+    a_host = torch.empty(2 * kept + prog.requests + 5, dtype=torch.int32, pin_memory=True)
+    d2h = 4 * (2 * kept + prog.requests + 5)
+    h2d = prepared["h2d_bytes"]
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    w0 = time.perf_counter()
+    for i in range(args.steps):
+        res = comp.run(prog.token_counts, prog.range_offsets, prog.ranges, req_to_token,
+                       row_ids, ring)
+        reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
+                             res.transition_destination, res.transition_pairs, cache,
+                             count_device=res.transition_count)
+        a_host[:kept].copy_(res.raw_indices[:kept], non_blocking=True)
+        a_host[kept: 2 * kept].copy_(res.active_positions[:kept], non_blocking=True)
+        a_host[2 * kept: 2 * kept + prog.requests].copy_(res.next_position, non_blocking=True)
+        a_host[2 * kept + prog.requests: 2 * kept + prog.requests + 5].copy_(comp.counters,
+                                                                            non_blocking=True)
+        stream.synchronize()
+        if int(a_host[-1]) != 0:
+            raise RuntimeError("drop_compact status in the e2e loop")
+    e2e_s = dist_max(time.perf_counter() - w0, world)
+    dist_barrier(world)
+
+    rep_bytes, drop_bytes = algorithmic_bytes(prog, heads, layers, dim, dim)
+    step_bytes = (rep_bytes + drop_bytes) * world
+    value = step_bytes * args.steps / (ms / 1e3) / 1e9
+    e2e_value = step_bytes * args.steps / e2e_s / 1e9
+    rep_mean = statistics.mean(rep_ms)
+    peak, peak_kind = measured_peak()
+    achieved = rep_bytes / (rep_mean / 1e3) / 1e9
+    traffic = ncu_traffic(args.workload) if world == 1 else None
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cache_np = cache.cpu().numpy()
+        threads = len(os.sched_getaffinity(0))
+        sec, m, n = cpu_reference_step(prog, rows, layers, heads, dim, cache_np, 4000,
+                                       np.random.default_rng(0), threads)
+        from oracle import reference
+
+        kind = "reference" if reference.available() else "port"
+        cpu = {"value": round((rep_bytes + drop_bytes) / sec / 1e9, 3), "unit": UNIT,
+               "cores": threads, "kind": kind,
+               "sample": f"event compiler ({'reference C++, oracle/_ref' if kind == 'reference' else 'oracle port'}) "
+                         f"over all {total} tokens + numpy decode view; reposition restatement "
+                         f"(the reference has no CPU reposition) on {m} of {n} moved tokens x "
+                         f"{layers} layers x {heads} heads, time scaled to all {n}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "layers": layers, "kv_heads": heads_total,
+                       "kv_heads_per_gpu": heads, "head_dim": dim, "tokens": total,
+                       "moved_tokens": moved, "dropped_tokens": total - kept,
+                       "reposition": "in place", "rope": WORKLOADS[args.workload][3],
+                       "parallelism": f"kv-head tp{world}",
+                       "l2": "inputs larger than L2 (K pools 2.4 GB per 36 layers), no flush"},
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "kernel": "reposition_kernel",
+                         "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": rep_bytes,
+                         "ms_per_launch": round(rep_mean, 4)},
+            "breakdown_ms": {"drop_compact": round(statistics.mean(drop_ms), 4),
+                             "reposition": round(rep_mean, 4)},
+            "gpu_launches": 4 * args.steps,
+            "cpu_baseline": cpu,
+            "clocks": clock_info,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,198 @@
+/*
+ * akv_b200.h -- C ABI of the B200 (sm_100a) cache-operation kernels.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, sizes and strides (strides in elements),
+ *     and a cudaStream_t passed as `void*` (NULL = legacy default stream);
+ *   - is stream-ordered: it enqueues work and returns, with no host
+ *     synchronisation, no device-to-host copy and no allocation, so it can
+ *     be captured in a CUDA graph;
+ *   - returns an AKV_* status.  A non-zero status means nothing was
+ *     enqueued (argument errors) or the launch failed (AKV_ERR_CUDA).
+ *
+ * Reference interfaces are cited as file:line relative to the reference
+ * project root (thu-nics/AKV).
+ */
+#ifndef AKV_B200_H_
+#define AKV_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define AKV_OK 0
+#define AKV_ERR_INVALID 1     /* bad argument (shape, dtype, stride, count) */
+#define AKV_ERR_CUDA 2        /* the CUDA launch failed                      */
+#define AKV_ERR_UNSUPPORTED 3 /* valid but not supported by this build       */
+
+/* Device-side status bits written by akv_drop_compact into `status`. */
+#define AKV_DROP_RING_UNDERFLOW 1 /* not enough free slots for copy-on-write */
+#define AKV_DROP_RING_OVERFLOW 2  /* freed slots exceed the ring capacity    */
+#define AKV_DROP_BAD_RANGE 4      /* a drop range lies outside its request   */
+#define AKV_DROP_NO_ACTIVE 8      /* Reposition of a request with no token   */
+
+/* Element types. */
+#define AKV_F16 0
+#define AKV_BF16 1
+#define AKV_F32 2
+
+/* Library identification: returns a static string. */
+const char* akv_version(void);
+
+/*
+ * Reposition: rotate retained K rows from their old to their new RoPE
+ * position and move them (and V) from source to destination slots, for
+ * every layer in the pointer tables, in one launch.
+ *
+ * Replaces reposition_kv_layers / _reposition_layers_kernel
+ * (akv/system/sglang/kernels/ops/attention/context_reposition.py:126-236,
+ * :28-123).  Same arithmetic: explicit fp32 inverse rotation by the old
+ * angle with IEEE division by cos^2+sin^2, forward rotation by the new one,
+ * no FMA contraction, bit copy when the two positions are equal; the K
+ * dims [rotary_dim, head_dim) and all of V are copied.
+ *
+ * k_data_ptrs / v_data_ptrs: DEVICE arrays of n_layers 64-bit base
+ *   addresses of [slots, heads, head_dim] NHD pools (stride(-1) == 1).
+ * source_slots / destination_slots: int32 [count]; position_pairs: int32
+ *   [count, position_stride] holding (old, new) in columns 0 and 1.
+ * cos_sin_cache: [max_position, rotary_dim] rows of (cos | sin), element
+ *   type cache_dtype, row stride cache_stride.
+ * count_device: optional DEVICE int32 holding the number of transitions to
+ *   process; when non-NULL the kernel processes min(count, *count_device),
+ *   so a count produced on the device needs no host round trip.
+ *
+ * num_slots / max_position (0 = unchecked) bound the slots and positions a
+ * transition may name; a transition outside them is skipped and, when
+ * error_flag (DEVICE int32, may be NULL) is given, 1 is stored there.
+ *
+ * A transition whose source equals its destination is rotated in place:
+ * every (token, layer, head) row is read completely before it is written,
+ * and the K tail and V (copies onto themselves) are skipped.  Results are
+ * the same as the reference's for such rows.
+ */
+int akv_reposition_kv_layers(
+    const void* k_data_ptrs, const void* v_data_ptrs, int32_t n_layers, int32_t kv_dtype,
+    int32_t num_heads, int32_t head_dim, int32_t rotary_dim, int64_t k_stride_slot,
+    int64_t k_stride_head, int64_t v_stride_slot, int64_t v_stride_head,
+    const int32_t* source_slots, const int32_t* destination_slots,
+    const int32_t* position_pairs, int64_t position_stride, int64_t count,
+    const int32_t* count_device, const void* cos_sin_cache, int32_t cache_dtype,
+    int64_t cache_stride, int32_t is_neox_style, int32_t skip_unmapped, int64_t num_slots,
+    int64_t max_position, int32_t* error_flag, void* stream);
+
+/*
+ * Drop + Reposition of a batch of requests, on the device.
+ *
+ * Replaces, for programs with one Drop event and one Reposition at the end
+ * of the prompt, the CPU event compiler compile_radix_reposition_layout
+ * (akv/system/sglang/kernels/ops/attention/context_plan.py:210-532, via
+ * srt/context_system/ir.py:113-274: keep mask, final positions, transitions
+ * (raw, old, new), next_position), the decode view
+ * ContextDecodeLayout.from_layout (srt/context_system/occurrence.py:47-66:
+ * raw = flatnonzero(keep), positions[raw]) and the slot retirement of
+ * OccurrenceState.advance / free_context_slots (occurrence.py:711-714,
+ * 936-964), with copy-on-write for radix-shared slots.
+ *
+ * Request r owns tokens [token_offsets[r], token_offsets[r+1]) of the flat
+ * per-token outputs, born at positions 0..T_r-1; its drop ranges are the
+ * request-local half-open pairs ranges[2*range_offsets[r] .. 2*range_offsets[r+1]).
+ * Its req_to_token row is req_to_token + row_ids[r] * row_stride (int32).
+ * Tokens below shared_prefix[r] (NULL = none) are borrowed radix slots: one
+ * that moves is copied to a fresh slot popped from the free ring and its row
+ * entry is updated; one that is dropped is not freed.  Other moved tokens
+ * are repositioned in place (source == destination).  Dropped private
+ * tokens' slots are pushed onto the free ring (and listed in freed_slots).
+ *
+ * Free ring: ring[capacity] int32 slot ids; ring_state = {head, tail} int64
+ * on the device (free entries are ring[head % capacity .. tail % capacity)).
+ *
+ * Outputs (device): keep_mask (uint8) and positions (int32) per flat token;
+ * active_offsets[R+1], raw_indices, active_positions (compacted decode view);
+ * next_position[R]; transition_offsets[R+1], transition_source,
+ * transition_destination, transition_pairs [N,2], transition_raw;
+ * freed_offsets[R+1], freed_slots; totals[4] = {active, transitions, cow,
+ * freed}; status (AKV_DROP_* bits, 0 = ok).  Per-request counts are on the
+ * device only: totals[1] can be handed to akv_reposition_kv_layers as
+ * count_device without a host round trip.
+ *
+ * tile_offsets[R+1]: prefix sum over requests of ceil(T_r / tile_tokens),
+ * n_tiles its last entry (the host knows the request lengths).
+ * workspace: akv_drop_compact_workspace_bytes(n_requests, n_tiles) bytes of
+ * device scratch, no initial contents required.
+ */
+int64_t akv_drop_compact_tile_tokens(void);
+int64_t akv_drop_compact_workspace_bytes(int32_t n_requests, int32_t n_tiles);
+int akv_drop_compact(
+    int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
+    int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
+    const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
+    int64_t row_stride, int32_t reposition, int32_t* ring, int64_t ring_capacity,
+    int64_t* ring_state, uint8_t* keep_mask, int32_t* positions, int32_t* active_offsets,
+    int32_t* raw_indices, int32_t* active_positions, int32_t* next_position,
+    int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
+    int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
+    int32_t* freed_slots, int32_t* totals, int32_t* status, void* workspace, void* stream);
+
+/*
+ * Decode read indices.  Replaces the Triton kernel context_decode_indices
+ * (akv/system/sglang/kernels/ops/attention/context_page_table.py:34-76),
+ * same contract: registry rows of six int64 cells {raw_ids*, positions*,
+ * prompt_len, active, next_pos, row*}
+ * (srt/layers/attention/context_backend.py:716-725); for request b and
+ * i < lengths[b], logical = starts[b] + i; raw = raw_ids[logical] if the
+ * row has context and logical < active, else prompt + logical - active (or
+ * logical without context); slot = row[raw] (row* or req_to_token row);
+ * slot = mapping[slot] * multiplier if mapping != NULL; stored at
+ * output[indptr[b] + i].  The *_is64 flags give each index vector's width.
+ */
+int akv_context_decode_indices(
+    const int64_t* registry, const int32_t* req_to_token, int64_t row_stride,
+    const void* row_ids, int32_t row_ids_is64, const void* lengths, int32_t lengths_is64,
+    const void* indptr, int32_t indptr_is64, void* output, int32_t output_is64,
+    const void* starts, int32_t starts_is64, const void* mapping, int32_t mapping_is64,
+    int64_t multiplier, int32_t batch, void* stream);
+
+/*
+ * Sliding-window visible lengths.  Replaces the Triton kernel
+ * context_window_lengths
+ * (akv/system/sglang/kernels/ops/attention/context_page_table.py:7-31):
+ * rows without context get min(length, window); context rows count the
+ * active keys with position >= q_pos - window (binary search over the
+ * row's positions) plus the visible generated tokens.
+ */
+int akv_context_window_lengths(
+    const int64_t* registry, const void* row_ids, int32_t row_ids_is64, const void* lengths,
+    int32_t lengths_is64, void* output, int32_t output_is64, int64_t window, int32_t batch,
+    void* stream);
+
+/*
+ * Ragged decode metadata in one call: optional window lengths (window >= 0),
+ * kv_indptr (exclusive scan of the lengths), starts = seq_lens - lengths and
+ * the decode indices.  Replaces ContextDecodeRegistry.fill_window / fill
+ * (srt/layers/attention/context_backend.py:754-809), whose torch cumsum and
+ * subtraction run as separate kernels.  kv_indptr: int32 [batch+1];
+ * lengths_out, starts_out: int64 [batch] (may be NULL); kv_indices: int32.
+ */
+int akv_build_decode_metadata(
+    const int64_t* registry, const int32_t* req_to_token, int64_t row_stride,
+    const int64_t* row_ids, const int64_t* seq_lens, int64_t window, const int64_t* mapping,
+    int64_t multiplier, int32_t batch, int32_t* kv_indptr, int64_t* lengths_out,
+    int64_t* starts_out, int32_t* kv_indices, void* stream);
+
+/*
+ * Overflow-row slot scatter.  Replaces the Triton kernel write_row_slots
+ * (akv/system/sglang/kernels/ops/memory/context_rows.py:7-15):
+ * ((int32*)pointers[rows[i]])[columns[i]] = values[i] for i < n.
+ */
+int akv_write_row_slots(const int64_t* pointers, const void* rows, int32_t rows_is64,
+                        const void* columns, int32_t columns_is64, const void* values,
+                        int32_t values_is64, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AKV_B200_H_ */

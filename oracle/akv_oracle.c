@@ -328,6 +328,9 @@ int akvo_reposition(
                     store_elem(kb, kd + i1, dtype, same ? x1 : y1);
                     store_elem(kb, kd + i2, dtype, same ? x2 : y2);
                 }
+                /* In place (src == dst) these copies write every element
+                 * onto itself; skipping them leaves the same bytes. */
+                if (src == dst) continue;
                 for (int32_t j = rotary_dim; j < head_dim; ++j) copy_elem(kb, kb, kd + j, ks + j, dtype);
                 int64_t vs = src * v_stride_slot + h * v_stride_head;
                 int64_t vd = dst * v_stride_slot + h * v_stride_head;

@@ -1,0 +1,68 @@
+"""The C-ABI library loads on the CPU host and exports every symbol that
+include/*.h declares (no compute call is made without a GPU)."""
+
+import ctypes
+import glob
+import os
+import re
+
+from conftest import ROOT
+
+
+def declared_symbols():
+    names = set()
+    for header in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(header).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"\b(akv_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for required in ("akv_reposition_kv_layers", "akv_drop_compact", "akv_context_decode_indices",
+                     "akv_context_window_lengths", "akv_write_row_slots",
+                     "akv_build_decode_metadata"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from akv_b200 import _native
+
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    missing = [n for n in sorted(declared_symbols()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol():
+    from akv_b200 import _native
+
+    assert declared_symbols() == set(_native.SIGNATURES)
+
+
+def test_host_only_entry_points():
+    from akv_b200 import _native
+
+    assert _native.lib.akv_version().startswith(b"akv_b200")
+    assert _native.lib.akv_drop_compact_tile_tokens() == 2048
+    assert _native.lib.akv_drop_compact_workspace_bytes(64, 700) > 0
+
+
+def test_argument_errors_are_reported_before_any_launch():
+    """Bad sizes are rejected on the host: AKV_ERR_INVALID, nothing enqueued."""
+    from akv_b200 import _native
+
+    lib = _native.lib
+    # rotary_dim odd
+    assert lib.akv_reposition_kv_layers(
+        None, None, 1, 1, 8, 64, 63, 512, 64, 512, 64, None, None, None, 2, 5, None, None,
+        2, 64, 1, 0, 0, 0, None, None) == _native.AKV_ERR_INVALID
+    # zero transitions: nothing to do, OK without a GPU
+    assert lib.akv_reposition_kv_layers(
+        None, None, 1, 1, 8, 64, 64, 512, 64, 512, 64, None, None, None, 2, 0, None, None,
+        2, 64, 1, 0, 0, 0, None, None) == _native.AKV_OK
+    assert lib.akv_context_decode_indices(
+        None, None, 0, None, 0, None, 0, None, 0, None, 0, None, 0, None, 0, 1, 4,
+        None) == _native.AKV_ERR_INVALID
+    assert lib.akv_write_row_slots(None, None, 0, None, 0, None, 0, 0, None) == _native.AKV_OK

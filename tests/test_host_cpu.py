@@ -1,0 +1,99 @@
+"""Host-side logic that needs no GPU: program validation, workload
+generators, the closed form the drop kernels implement, RoPE tables."""
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+
+def test_validate_program_follows_reference_rules():
+    from akv_b200.context_drop import validate_program
+
+    validate_program([10, 0, 5], [0, 2, 2, 3], [1, 3, 5, 7, 0, 2])
+    with pytest.raises(ValueError, match="ordered, disjoint"):
+        validate_program([10], [0, 2], [1, 5, 4, 7])  # overlapping
+    with pytest.raises(ValueError, match="ordered, disjoint"):
+        validate_program([10], [0, 1], [3, 3])  # empty range
+    with pytest.raises(ValueError, match="does not cover"):
+        validate_program([10], [0, 2], [1, 3])
+    with pytest.raises(ValueError, match="ordered, disjoint"):
+        validate_program([4], [0, 2], [0, 2, 2, 4])  # adjacent: previous_end < start fails
+    with pytest.raises(ValueError, match="no active tokens"):
+        validate_program([4], [0, 1], [0, 4])
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_single_stage_closed_form_matches_compiler(seed):
+    """The formulas the drop kernels evaluate (keep = not covered, rank =
+    kept tokens before, moved = kept after the first drop) equal the
+    reference-pinned compiler's output for one drop event + one Reposition."""
+    from akv_b200 import workloads
+
+    prog = workloads.c3_program(requests=3, max_len=6000, seed=seed)
+    for r in range(prog.requests):
+        t = int(prog.token_counts[r])
+        rr = prog.request_ranges(r)
+        lay = oracle.compile_layout(np.zeros(t), [t], [0, len(rr) // 2], rr, [t - 1], [t])
+        keep = prog.keep_mask(r)
+        rank = np.cumsum(keep) - keep
+        first = np.flatnonzero(~keep)[0]
+        moved = keep & (np.arange(t) > first)
+        np.testing.assert_array_equal(lay["keep_mask"], keep)
+        np.testing.assert_array_equal(lay["positions"], np.where(keep, rank, np.arange(t)))
+        np.testing.assert_array_equal(lay["transition_raw_tokens"], np.flatnonzero(moved))
+        np.testing.assert_array_equal(lay["transition_new_positions"], rank[moved])
+        assert lay["next_position"] == (int(keep.sum()) if moved.any() else t)
+
+
+def test_workloads_match_configuration():
+    from akv_b200 import workloads
+
+    c2 = workloads.c2_program()
+    keep = c2.keep_mask(0)
+    assert c2.total_tokens == 65536 and len(c2.ranges) == 40
+    assert int((~keep).sum()) == 26425  # about 40 % dropped
+    lengths = np.diff(c2.ranges.reshape(-1, 2), axis=1)
+    assert lengths.min() >= 256 and lengths.max() <= 4096
+    c3 = workloads.c3_program()
+    assert c3.requests == 64 and 1024 <= c3.meta["prefix"] <= 4096
+    for r in range(c3.requests):
+        rr = c3.request_ranges(r)
+        assert rr[0] < c3.meta["prefix"] // 2  # first span inside the shared prefix
+    c4 = workloads.c4_lengths()
+    assert len(c4) == 128 and c4.max() <= 65536 and abs(np.median(c4) - 8192) < 2500
+    c5 = workloads.c5_program(requests=2)
+    assert abs(int((~c5.keep_mask(0)).sum()) / 131072 - 0.3) < 0.02
+
+
+def test_yarn_table_magnitude():
+    from akv_b200.rope import rope_cos_sin_cache, yarn_cos_sin_cache
+
+    t = yarn_cos_sin_cache(1024, 64, 150000.0, 32.0, 4096).numpy()
+    mag = t[:, :32] ** 2 + t[:, 32:] ** 2
+    want = (0.1 * np.log(32.0) + 1.0) ** 2
+    np.testing.assert_allclose(mag, want, rtol=1e-5)
+    p = rope_cos_sin_cache(16, 8, 10000.0).numpy()
+    np.testing.assert_allclose(p[:, :4] ** 2 + p[:, 4:] ** 2, 1.0, rtol=1e-6)
+    np.testing.assert_allclose(p[3, 0], np.cos(3.0), rtol=1e-6)
+
+
+def test_reference_compiler_matches_oracle_at_c2_size():
+    """When the reference's own compiler is built (oracle/_ref), it agrees
+    with the oracle on the full GPT-OSS-shaped program."""
+    from oracle import reference
+    from akv_b200 import workloads
+
+    if not reference.available():
+        pytest.skip("reference compiler not built here")
+    prog = workloads.c2_program()
+    t = prog.total_tokens
+    rr = prog.request_ranges(0)
+    args = (np.arange(t) % 1000, [t], [0, len(rr) // 2], rr, [t - 1], [t])
+    a = reference.compile_context_layout(*args)
+    b = oracle.compile_layout(*args)
+    for k in ("positions", "keep_mask", "transition_raw_tokens", "transition_old_positions",
+              "transition_new_positions", "records", "birth_positions", "materialized_stage"):
+        np.testing.assert_array_equal(np.asarray(a[k]).astype(np.int64),
+                                      np.asarray(b[k]).astype(np.int64), err_msg=k)
+    assert a["next_position"] == b["next_position"]

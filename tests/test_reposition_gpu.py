@@ -1,0 +1,287 @@
+"""Reposition kernel (C ABI akv_reposition_kv_layers) against the reference.
+
+* golden cases: outputs of the reference's Triton kernel
+  (context_reposition.py:28-123) run by tests/golden/make_golden.py -- fp32
+  storage bit for bit, bf16 storage as the round-to-nearest-even of the
+  reference's fp32 values (what a GPU store does);
+* random and benchmark-shaped cases against the pinned CPU oracle, bit for
+  bit, for bf16 / fp16 / fp32 storage, NEOX and GPT-J styles, partial
+  rotary_dim, copy-on-write and in-place transitions.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+RP = golden("reposition")
+RP_CASES = sorted({k.split("/")[0] for k in RP.files})
+
+
+def _rp():
+    from akv_b200.context_reposition import reposition_kv_layers, layer_pointer_table
+
+    return reposition_kv_layers, layer_pointer_table
+
+
+def _bits_to_f32(bits):
+    return (bits.astype(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def _f32_to_bf16_bits(x):
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+
+
+def _golden_layers(case, storage):
+    n, layers, heads, dim, rot, neox, pad, skip = (int(x) for x in RP[f"{case}/spec"])
+    k_bits, v_bits = RP[f"{case}/k_in"], RP[f"{case}/v_in"]
+    dev = torch.device("cuda")
+    if storage == "f32":
+        ks = [torch.from_numpy(_bits_to_f32(k_bits[i])).to(dev) for i in range(layers)]
+        vs = [torch.from_numpy(_bits_to_f32(v_bits[i])).to(dev) for i in range(layers)]
+    else:
+        ks = [torch.from_numpy(k_bits[i].copy()).to(dev).view(torch.bfloat16) for i in range(layers)]
+        vs = [torch.from_numpy(v_bits[i].copy()).to(dev).view(torch.bfloat16) for i in range(layers)]
+    return (n, layers, heads, dim, rot, neox, pad, skip), ks, vs
+
+
+@pytest.mark.parametrize("storage", ["f32", "bf16"])
+@pytest.mark.parametrize("case", RP_CASES)
+def test_reposition_matches_reference_golden(case, storage):
+    reposition_kv_layers, table = _rp()
+    (n, layers, heads, dim, rot, neox, pad, skip), k_full, v_full = _golden_layers(case, storage)
+    ks = [k[..., :dim] for k in k_full]
+    vs = [v[..., :dim] for v in v_full]
+    dev = ks[0].device
+    cache = torch.from_numpy(RP[f"{case}/cache"]).to(dev)
+    src = torch.from_numpy(RP[f"{case}/src"]).to(dev)
+    dst = torch.from_numpy(RP[f"{case}/dst"]).to(dev)
+    pairs = torch.from_numpy(RP[f"{case}/pairs"]).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    reposition_kv_layers(table(ks), table(vs), ks[0], vs[0], src, dst, pairs, cache,
+                         is_neox_style=bool(neox), skip_unmapped=bool(skip), rotary_dim=rot,
+                         error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    rows = np.clip(RP[f"{case}/dst"].astype(np.int64), 0, None)
+    for layer in range(layers):
+        got_k = k_full[layer].cpu()
+        got_v = v_full[layer].cpu()
+        want_k, want_v = RP[f"{case}/k_out_dst"][layer], RP[f"{case}/v_out_dst"][layer]
+        if storage == "f32":
+            np.testing.assert_array_equal(got_k.numpy()[rows], want_k)
+            np.testing.assert_array_equal(got_v.numpy()[rows], want_v)
+        else:
+            np.testing.assert_array_equal(got_k.view(torch.int16).numpy().view(np.uint16)[rows],
+                                          _f32_to_bf16_bits(want_k))
+            np.testing.assert_array_equal(got_v.view(torch.int16).numpy().view(np.uint16)[rows],
+                                          _f32_to_bf16_bits(want_v))
+        # rows that are not destinations are untouched (padding included)
+        mask = np.ones(got_k.shape[0], bool)
+        mask[rows] = False
+        k_in = RP[f"{case}/k_in"][layer]
+        if storage == "f32":
+            np.testing.assert_array_equal(got_k.numpy()[mask], _bits_to_f32(k_in)[mask])
+        else:
+            np.testing.assert_array_equal(got_k.view(torch.int16).numpy()[mask], k_in[mask])
+
+
+def _random_case(rng, *, dtype, layers, heads, dim, rot, neox, n, slots, in_place, pad=0,
+                 cache_dtype=torch.float32, max_pos=4096, yarn=False):
+    from oracle import oracle
+    from akv_b200.rope import rope_cos_sin_cache, yarn_cos_sin_cache
+
+    reposition_kv_layers, table = _rp()
+    width = dim + pad
+    k_full = [torch.randn(slots, heads, width).to(dtype) for _ in range(layers)]
+    v_full = [torch.randn(slots, heads, width).to(dtype) for _ in range(layers)]
+    perm = rng.permutation(np.arange(1, slots))
+    src = perm[:n].astype(np.int32)
+    dst = src.copy() if in_place else perm[n: 2 * n].astype(np.int32)
+    old = rng.integers(0, max_pos, size=n)
+    new = rng.integers(0, max_pos, size=n)
+    new[::9] = old[::9]
+    pairs = np.stack((old, new), 1).astype(np.int32)
+    if yarn:
+        cache = yarn_cos_sin_cache(max_pos, rot, 150000.0, 32.0, 4096)
+    else:
+        cache = rope_cos_sin_cache(max_pos, rot, 10000.0)
+    cache = cache.to(cache_dtype)
+
+    # oracle on host copies
+    def host(t):
+        if t.dtype == torch.bfloat16:
+            return t.view(torch.int16).numpy().view(np.uint16).copy()
+        return t.numpy().copy()
+
+    hk = [host(k) for k in k_full]
+    hv = [host(v) for v in v_full]
+    cache_host = host(cache)
+    oracle.reposition([a[..., :dim] for a in hk], [a[..., :dim] for a in hv], src, dst, pairs,
+                      cache_host, is_neox_style=neox, rotary_dim=rot,
+                      bf16=dtype == torch.bfloat16, cache_bf16=cache_dtype == torch.bfloat16,
+                      threads=4)
+    dev = torch.device("cuda")
+    dk = [k.to(dev) for k in k_full]
+    dv = [v.to(dev) for v in v_full]
+    ks = [k[..., :dim] for k in dk]
+    vs = [v[..., :dim] for v in dv]
+    reposition_kv_layers(table(ks), table(vs), ks[0], vs[0], torch.from_numpy(src).to(dev),
+                         torch.from_numpy(dst).to(dev), torch.from_numpy(pairs).to(dev),
+                         cache.to(dev), is_neox_style=neox, rotary_dim=rot)
+    torch.cuda.synchronize()
+    for layer in range(layers):
+        np.testing.assert_array_equal(host(dk[layer].cpu()), hk[layer])
+        np.testing.assert_array_equal(host(dv[layer].cpu()), hv[layer])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("neox", [True, False])
+@pytest.mark.parametrize("in_place", [True, False])
+def test_reposition_random_matches_oracle(dtype, neox, in_place):
+    rng = np.random.default_rng(1)
+    _random_case(rng, dtype=dtype, layers=3, heads=8, dim=64, rot=64, neox=neox, n=300,
+                 slots=1000, in_place=in_place, yarn=True)
+
+
+@pytest.mark.parametrize(
+    "heads,dim,rot,pad,cache_dtype",
+    [(4, 128, 128, 0, torch.float32), (2, 128, 64, 0, torch.bfloat16), (3, 96, 32, 8,
+                                                                           torch.float32),
+     (1, 40, 24, 0, torch.float16), (8, 64, 64, 4, torch.float32), (5, 80, 80, 0, torch.float32)],
+)
+def test_reposition_shapes_match_oracle(heads, dim, rot, pad, cache_dtype):
+    rng = np.random.default_rng(heads * 1000 + dim)
+    for in_place in (True, False):
+        _random_case(rng, dtype=torch.bfloat16, layers=5, heads=heads, dim=dim, rot=rot,
+                     neox=True, n=257, slots=800, in_place=in_place, pad=pad,
+                     cache_dtype=cache_dtype)
+
+
+def test_reposition_misaligned_layer_matches_oracle():
+    """A layer whose base address is not 16-byte aligned takes the element path."""
+    from oracle import oracle
+    from akv_b200.rope import rope_cos_sin_cache
+
+    reposition_kv_layers, table = _rp()
+    rng = np.random.default_rng(5)
+    dev = torch.device("cuda")
+    slots, heads, dim = 300, 8, 64
+    base = torch.randn(slots * heads * dim + 8).to(torch.bfloat16)
+    k0 = base[4: 4 + slots * heads * dim].view(slots, heads, dim)  # 8-byte offset
+    k1 = torch.randn(slots, heads, dim).to(torch.bfloat16)
+    v0 = torch.randn(slots, heads, dim).to(torch.bfloat16)
+    v1 = torch.randn(slots, heads, dim).to(torch.bfloat16)
+    n = 100
+    perm = rng.permutation(np.arange(1, slots))
+    src, dst = perm[:n].astype(np.int32), perm[n: 2 * n].astype(np.int32)
+    pairs = rng.integers(0, 1000, size=(n, 2)).astype(np.int32)
+    cache = rope_cos_sin_cache(1000, dim, 10000.0)
+    host = [t.view(torch.int16).numpy().view(np.uint16).copy() for t in (k0, k1, v0, v1)]
+    oracle.reposition(host[:2], host[2:], src, dst, pairs, cache.numpy(), bf16=True)
+    dbase = base.to(dev)
+    dk0 = dbase[4: 4 + slots * heads * dim].view(slots, heads, dim)
+    dk1, dv0, dv1 = k1.to(dev), v0.to(dev), v1.to(dev)
+    reposition_kv_layers(table([dk0, dk1]), table([dv0, dv1]), dk1, dv1,
+                         torch.from_numpy(src).to(dev), torch.from_numpy(dst).to(dev),
+                         torch.from_numpy(pairs).to(dev), cache.to(dev))
+    torch.cuda.synchronize()
+    for got, want in zip((dk0, dk1, dv0, dv1), host):
+        np.testing.assert_array_equal(got.cpu().view(torch.int16).numpy().view(np.uint16), want)
+
+
+def test_reposition_count_device_and_bounds():
+    from akv_b200.rope import rope_cos_sin_cache
+
+    reposition_kv_layers, table = _rp()
+    dev = torch.device("cuda")
+    k = torch.randn(64, 2, 64, device=dev).to(torch.bfloat16)
+    v = torch.randn(64, 2, 64, device=dev).to(torch.bfloat16)
+    k0, v0 = k.clone(), v.clone()
+    src = torch.tensor([1, 2, 3, 4], dtype=torch.int32, device=dev)
+    dst = torch.tensor([11, 12, 13, 999], dtype=torch.int32, device=dev)  # 999 out of range
+    pairs = torch.tensor([[5, 1], [6, 2], [7, 3], [8, 4]], dtype=torch.int32, device=dev)
+    cache = rope_cos_sin_cache(16, 64, 10000.0).to(dev)
+    count = torch.tensor([2], dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    reposition_kv_layers(table([k]), table([v]), k, v, src, dst, pairs, cache, count_device=count,
+                         error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert not torch.equal(k[11], k0[11]) and torch.equal(v[12], v0[2])
+    assert torch.equal(k[13], k0[13])  # beyond the device count: untouched
+    count.fill_(4)
+    reposition_kv_layers(table([k]), table([v]), k, v, src, dst, pairs, cache, count_device=count,
+                         error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1  # the out-of-range destination was skipped and reported
+    assert torch.equal(v[13], v0[3])
+
+
+def test_reposition_validation_errors():
+    reposition_kv_layers, table = _rp()
+    dev = torch.device("cuda")
+    k = torch.zeros(8, 2, 64, device=dev, dtype=torch.bfloat16)
+    ptrs = table([k])
+    s = torch.zeros(1, dtype=torch.int32, device=dev)
+    pairs = torch.zeros(1, 2, dtype=torch.int32, device=dev)
+    cache = torch.zeros(4, 64, device=dev)
+    with pytest.raises(ValueError, match="page_size=1"):
+        reposition_kv_layers(ptrs, ptrs, k, k, s, s, pairs, cache, page_size=16)
+    with pytest.raises(ValueError, match="int32 slot vectors"):
+        reposition_kv_layers(ptrs, ptrs, k, k, s.long(), s, pairs, cache)
+    with pytest.raises(ValueError, match="cos/sin cache"):
+        reposition_kv_layers(ptrs, ptrs, k, k, s, s, pairs, cache[:, :32])
+    with pytest.raises(ValueError, match="cos/sin cache"):
+        reposition_kv_layers(ptrs, ptrs, k, k, s, s, pairs, cache, rotary_dim=63)
+    with pytest.raises(ValueError, match="one CUDA device"):
+        reposition_kv_layers(ptrs, ptrs, k, k, s.cpu(), s, pairs, cache)
+    # empty transition list: no launch, no error
+    e = torch.zeros(0, dtype=torch.int32, device=dev)
+    reposition_kv_layers(ptrs, ptrs, k, k, e, e, e.view(0, 2), cache)
+
+
+def test_reposition_c2_shape_sampled_rows_match_oracle():
+    """Full GPT-OSS-shaped launch (36 layers, 8 heads, head_dim 64, YaRN,
+    38.9K transitions in place); every row depends only on its own input, so
+    a sample of transitions checked on the CPU is an exact check of them."""
+    from oracle import oracle
+    from akv_b200 import workloads
+    from akv_b200.rope import yarn_cos_sin_cache
+
+    reposition_kv_layers, table = _rp()
+    dev = torch.device("cuda")
+    prog = workloads.c2_program()
+    T = int(prog.token_counts[0])
+    keep = prog.keep_mask(0)
+    rank = np.cumsum(keep) - 1
+    moved = np.flatnonzero(keep & (np.arange(T) > np.flatnonzero(~keep)[0]))
+    rng = np.random.default_rng(0)
+    row = rng.permutation(T).astype(np.int32) + 1
+    src = row[moved]
+    pairs = np.stack((moved, rank[moved]), 1).astype(np.int32)
+    layers, heads, dim = 36, 8, 64
+    g = torch.Generator(device=dev).manual_seed(0)
+    ks = [torch.randn(T + 1, heads, dim, device=dev, generator=g).to(torch.bfloat16)
+          for _ in range(layers)]
+    vs = [torch.empty(T + 1, heads, dim, device=dev, dtype=torch.bfloat16) for _ in range(layers)]
+    cache = yarn_cos_sin_cache(131072, dim, 150000.0, 32.0, 4096)
+    sample = rng.choice(len(moved), size=2000, replace=False)
+    before = [k[torch.from_numpy(src[sample].astype(np.int64)).to(dev)].cpu() for k in ks]
+    s = torch.from_numpy(src).to(dev)
+    reposition_kv_layers(table(ks), table(vs), ks[0], vs[0], s, s,
+                         torch.from_numpy(pairs).to(dev), cache.to(dev))
+    torch.cuda.synchronize()
+    hk = [b.view(torch.int16).numpy().view(np.uint16).copy() for b in before]
+    hv = [np.zeros_like(a) for a in hk]
+    idx = np.arange(len(sample), dtype=np.int32)
+    oracle.reposition(hk, hv, idx, idx, pairs[sample], cache.numpy(), bf16=True, threads=4)
+    for layer in range(layers):
+        got = ks[layer][torch.from_numpy(src[sample].astype(np.int64)).to(dev)].cpu()
+        np.testing.assert_array_equal(got.view(torch.int16).numpy().view(np.uint16), hk[layer])
