@@ -31,6 +31,7 @@ SIGNATURES = {
         _P, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64,
         _P, _P, _I32, _I64, _I32, _I32, _I64, _I64, _P, _P,
     ],
+    "akv_reposition_divide": [_P, _P, _P, _I64, _I32, _P],
     "akv_drop_compact_tile_tokens": [],
     "akv_drop_compact_workspace_bytes": [_I32, _I32],
     "akv_drop_compact": [
@@ -46,6 +47,10 @@ SIGNATURES = {
         _P, _P, _I64, _P, _P, _I64, _P, _I64, _I32, _P, _P, _P, _P, _P,
     ],
     "akv_write_row_slots": [_P, _P, _I32, _P, _I32, _P, _I32, _I64, _P],
+    "akv_decode_attention": [
+        _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, ctypes.c_float, _I32,
+        _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P, _I64, _I64, _P, _P, _P,
+    ],
 }
 RESTYPES = {
     "akv_version": ctypes.c_char_p,

@@ -144,7 +144,10 @@ class DropCompactor:
     """
 
     def __init__(self, max_tokens, max_requests, max_ranges, device):
-        self.device = torch.device(device)
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = device
         self.max_tokens = int(max_tokens)
         self.max_requests = int(max_requests)
         self.max_ranges = int(max_ranges)

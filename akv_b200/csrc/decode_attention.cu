@@ -1,0 +1,421 @@
+// Paged GQA decode attention over the compacted cache, with learned sinks.
+//
+// Replaces the native decode kernels the reference calls over the registry's
+// kv_indptr / kv_indices (FlashInfer BatchDecodeWithPagedKVCacheWrapper and
+// FA3 flash_attn_with_kvcache, not vendored), together with AKV's sink
+// correction o *= sigmoid(lse - sink) (akv/system/sglang.patch:2170-2183,
+// srt/layers/attention/context_backend.py:254-272), which here is folded into
+// the softmax denominator: out = sum_k e^{s_k} v_k / (sum_k e^{s_k} + e^{sink}).
+// Sliding-window layers read only the window the metadata builder selected
+// (context_page_table.py:7-31), so this kernel needs no position mask.
+//
+// Decode attention reads every key once (8 flop per byte for a GQA group of
+// 8) -- an HBM-bound stream.  Layout of the work:
+//  * one CTA = one (request, key range) work item, all KV heads of the
+//    request; warp w owns KV head w and its GROUP = 8 query heads;
+//  * a key's K row (and V row) for all local heads is one contiguous
+//    Hkv*D*2-byte run in the [slot, head, dim] pool; NSTAGE stages of TK keys
+//    are gathered into shared memory with 16-byte cp.async (zero-filled
+//    past the range end), XOR-swizzled by key so ldmatrix is conflict-free;
+//  * tensor cores (mma.sync m16n8k16 bf16, fp32 accumulate) with KEYS as the
+//    M dimension: S^T[16 keys x 8 heads] = K[16 x D] . Q^T[D x 8], so the
+//    8-head group fills N = 8 exactly and no MMA row is padding; then
+//    O^T[D x 8] += V^T[D x 16] . P^T[16 x 8], with P^T produced from the S^T
+//    accumulator fragment by movmatrix (an in-register 8x8 transpose);
+//  * fp32 online softmax in base 2; per-head state lives in the lanes that
+//    hold that head's O^T columns, so rescaling is thread-local;
+//  * long requests are split into several items whose partial (m, l, acc)
+//    a second kernel combines; single-item requests write bf16 directly.
+
+#include "common.cuh"
+
+namespace akv {
+namespace {
+
+constexpr int kGroup = 8;  // query heads per KV head (the MMA N)
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct AttnParams {
+  const __nv_bfloat16* q;
+  long long q_sb, q_sh;  // strides of q [batch, q_heads, D] in elements
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  long long k_ss, k_sh, v_ss, v_sh;
+  long long num_slots;
+  const int* kv_indices;
+  const float* sinks;  // [q_heads] natural-log logits, or null
+  float scale_log2;    // sm_scale * log2(e)
+  const int4* work;    // {request, kv_begin, kv_end, partial or -1}
+  float* part_acc;     // [partials, q_heads, D]
+  float* part_ml;      // [partials, q_heads, 2] (max in base 2, sum)
+  __nv_bfloat16* out;
+  long long o_sb, o_sh;
+  float* lse;          // [batch, q_heads] natural log, or null
+  int num_q_heads;
+  int* error_flag;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                            uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                                  uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D, int HKV, int TK, int NSTAGE>
+struct Cfg {
+  static constexpr int kThreads = 32 * HKV;
+  static constexpr int kCph = D / 8;               // 16-byte chunks per head row
+  static constexpr int kChunks = HKV * kCph;       // chunks per key row
+  static constexpr int kRowBytes = kChunks * 16;
+  static constexpr int kTileBytes = TK * kRowBytes;
+  static constexpr int kStageBytes = 2 * kTileBytes;  // K then V
+  static constexpr int kSmem = NSTAGE * kStageBytes;
+};
+
+template <int D, int HKV, int TK, int NSTAGE>
+__global__ void __launch_bounds__(32 * HKV)
+decode_attention_kernel(const AttnParams p) {
+  using C = Cfg<D, HKV, TK, NSTAGE>;
+  static_assert(D % 16 == 0 && D >= 64, "head_dim must be a multiple of 16, at least 64");
+  static_assert(TK % 16 == 0, "key tile is a whole number of 16-key MMA blocks");
+  extern __shared__ __align__(128) unsigned char smem[];
+
+  const int4 w = p.work[blockIdx.x];
+  const int b = w.x, kv_begin = w.y, kv_end = w.z, partial = w.w;
+  const int n_keys = kv_end - kv_begin;
+  const int n_tiles = (n_keys + TK - 1) / TK;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+
+  // Gather one tile of K and V rows into stage `s`.
+  auto load_tile = [&](int tile, int s) {
+    const uint32_t kbase = smem_u32(smem + s * C::kStageBytes);
+    const uint32_t vbase = kbase + C::kTileBytes;
+    for (int i = tid; i < TK * C::kChunks; i += C::kThreads) {
+      const int j = i / C::kChunks;  // key within the tile
+      const int c = i - j * C::kChunks;
+      const int head = c / C::kCph, cc = c - head * C::kCph;
+      const int kk = kv_begin + tile * TK + j;
+      const bool valid = kk < kv_end;
+      long long slot = valid ? (long long)__ldg(p.kv_indices + kk) : 0;
+      if (slot < 0 || slot >= p.num_slots) {  // never touch memory outside the pools
+        if (valid && p.error_flag) *p.error_flag = 1;
+        slot = 0;
+      }
+      const int phys = head * C::kCph + (cc ^ (j & 7));
+      const uint32_t off = j * C::kRowBytes + phys * 16;
+      cp_async16(kbase + off, p.k + slot * p.k_ss + head * p.k_sh + cc * 8, valid ? 16 : 0);
+      cp_async16(vbase + off, p.v + slot * p.v_ss + head * p.v_sh + cc * 8, valid ? 16 : 0);
+    }
+  };
+
+#pragma unroll
+  for (int s = 0; s < NSTAGE - 1; ++s) {
+    if (s < n_tiles) load_tile(s, s);
+    cp_async_commit();
+  }
+
+  // Q^T fragments of this warp's 8 query heads (B operand, k = dims).
+  const int qh0 = warp * kGroup;
+  uint32_t qf[D / 16][2];
+  {
+    const __nv_bfloat16* qrow = p.q + (long long)b * p.q_sb + (long long)(qh0 + g) * p.q_sh;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      qf[ks][0] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * t);
+      qf[ks][1] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * t);
+    }
+  }
+
+  float m[2] = {-INFINITY, -INFINITY};  // running max (base 2) of heads 2t, 2t+1
+  float l[2] = {0.f, 0.f};              // this lane's share of the running sum
+  float acc[D / 16][4];
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) acc[mt][r] = 0.f;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int nt = tile + NSTAGE - 1;
+    if (nt < n_tiles) load_tile(nt, nt % NSTAGE);
+    cp_async_commit();
+    cp_async_wait<NSTAGE - 1>();
+    __syncthreads();
+
+    const unsigned char* stage = smem + (tile % NSTAGE) * C::kStageBytes;
+    const uint32_t kb = smem_u32(stage);
+    const uint32_t vb = kb + C::kTileBytes;
+    const int key0 = tile * TK;
+
+#pragma unroll
+    for (int blk = 0; blk < TK / 16; ++blk) {
+      // ---- S^T = K . Q^T for 16 keys ----
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        const int key = blk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const int cc = ks * 2 + (lane >> 4);
+          const uint32_t addr =
+              kb + key * C::kRowBytes + (warp * C::kCph + (cc ^ (key & 7))) * 16;
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4(addr, a0, a1, a2, a3);
+          mma_bf16(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+        }
+      }
+      // keys g and g + 8 of this block; mask past the item's end
+      const int kg0 = key0 + blk * 16 + g, kg1 = kg0 + 8;
+      s[0] = kg0 < n_keys ? s[0] * p.scale_log2 : -INFINITY;
+      s[1] = kg0 < n_keys ? s[1] * p.scale_log2 : -INFINITY;
+      s[2] = kg1 < n_keys ? s[2] * p.scale_log2 : -INFINITY;
+      s[3] = kg1 < n_keys ? s[3] * p.scale_log2 : -INFINITY;
+
+      // ---- online softmax, heads 2t (s0, s2) and 2t+1 (s1, s3) ----
+      float bm0 = fmaxf(s[0], s[2]), bm1 = fmaxf(s[1], s[3]);
+#pragma unroll
+      for (int x = 4; x < 32; x <<= 1) {
+        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, x));
+        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, x));
+      }
+      const float mn0 = fmaxf(m[0], bm0), mn1 = fmaxf(m[1], bm1);
+      const float base0 = mn0 == -INFINITY ? 0.f : mn0;
+      const float base1 = mn1 == -INFINITY ? 0.f : mn1;
+      const float al0 = fast_exp2(m[0] - base0), al1 = fast_exp2(m[1] - base1);
+      m[0] = mn0;
+      m[1] = mn1;
+      const float p0 = fast_exp2(s[0] - base0), p1 = fast_exp2(s[1] - base1);
+      const float p2 = fast_exp2(s[2] - base0), p3 = fast_exp2(s[3] - base1);
+      l[0] = l[0] * al0 + p0 + p2;
+      l[1] = l[1] * al1 + p1 + p3;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        acc[mt][0] *= al0;
+        acc[mt][1] *= al1;
+        acc[mt][2] *= al0;
+        acc[mt][3] *= al1;
+      }
+
+      // ---- O^T += V^T . P^T ----
+      const uint32_t pb0 = movmatrix_trans(pack_bf16(p0, p1));  // keys 0-7
+      const uint32_t pb1 = movmatrix_trans(pack_bf16(p2, p3));  // keys 8-15
+      {
+        const int mj = lane >> 3;
+        const int key = blk * 16 + (lane & 7) + ((mj >> 1) & 1) * 8;
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          const int cc = mt * 2 + (mj & 1);
+          const uint32_t addr =
+              vb + key * C::kRowBytes + (warp * C::kCph + (cc ^ (key & 7))) * 16;
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(addr, a0, a1, a2, a3);
+          mma_bf16(acc[mt], a0, a1, a2, a3, pb0, pb1);
+        }
+      }
+    }
+    __syncthreads();  // the stage is refilled NSTAGE - 1 tiles later
+  }
+  cp_async_wait<0>();
+
+  // ---- epilogue ----
+#pragma unroll
+  for (int x = 4; x < 32; x <<= 1) {
+    l[0] += __shfl_xor_sync(0xffffffffu, l[0], x);
+    l[1] += __shfl_xor_sync(0xffffffffu, l[1], x);
+  }
+  const int h0 = qh0 + 2 * t, h1 = h0 + 1;
+  if (partial >= 0) {
+    float* pa = p.part_acc + (long long)partial * p.num_q_heads * D;
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      const int d0 = mt * 16 + g, d1 = d0 + 8;
+      pa[(long long)h0 * D + d0] = acc[mt][0];
+      pa[(long long)h1 * D + d0] = acc[mt][1];
+      pa[(long long)h0 * D + d1] = acc[mt][2];
+      pa[(long long)h1 * D + d1] = acc[mt][3];
+    }
+    if (g == 0) {
+      float* pm = p.part_ml + (long long)partial * p.num_q_heads * 2;
+      pm[2 * h0] = m[0];
+      pm[2 * h0 + 1] = l[0];
+      pm[2 * h1] = m[1];
+      pm[2 * h1 + 1] = l[1];
+    }
+    return;
+  }
+  float den0 = l[0], den1 = l[1];
+  const float mb0 = m[0] == -INFINITY ? 0.f : m[0];
+  const float mb1 = m[1] == -INFINITY ? 0.f : m[1];
+  if (p.sinks) {
+    den0 += fast_exp2(p.sinks[h0] * kLog2e - mb0);
+    den1 += fast_exp2(p.sinks[h1] * kLog2e - mb1);
+  }
+  const float inv0 = den0 > 0.f ? 1.f / den0 : 0.f;
+  const float inv1 = den1 > 0.f ? 1.f / den1 : 0.f;
+  __nv_bfloat16* o = p.out + (long long)b * p.o_sb;
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt) {
+    const int d0 = mt * 16 + g, d1 = d0 + 8;
+    o[(long long)h0 * p.o_sh + d0] = __float2bfloat16_rn(acc[mt][0] * inv0);
+    o[(long long)h1 * p.o_sh + d0] = __float2bfloat16_rn(acc[mt][1] * inv1);
+    o[(long long)h0 * p.o_sh + d1] = __float2bfloat16_rn(acc[mt][2] * inv0);
+    o[(long long)h1 * p.o_sh + d1] = __float2bfloat16_rn(acc[mt][3] * inv1);
+  }
+  if (p.lse && g == 0) {
+    // natural-log LSE of [scores | sink] (the sink-corrected value,
+    // context_backend.py:269-271); -inf for an empty key set without sink.
+    p.lse[(long long)b * p.num_q_heads + h0] = den0 > 0.f ? (mb0 + log2f(den0)) * kLn2 : -INFINITY;
+    p.lse[(long long)b * p.num_q_heads + h1] = den1 > 0.f ? (mb1 + log2f(den1)) * kLn2 : -INFINITY;
+  }
+}
+
+// Combine the partial results of split requests: one block per request,
+// one thread per (head, dim).
+template <int D>
+__global__ void decode_combine_kernel(const AttnParams p, const int2* merge, int batch) {
+  const int b = blockIdx.x;
+  const int2 mg = merge[b];  // {first partial, count}; count 0 = written directly
+  if (mg.y == 0) return;
+  for (int i = threadIdx.x; i < p.num_q_heads * D; i += blockDim.x) {
+    const int h = i / D, d = i - h * D;
+    float mx = -INFINITY;
+    for (int s = 0; s < mg.y; ++s)
+      mx = fmaxf(mx, p.part_ml[((long long)(mg.x + s) * p.num_q_heads + h) * 2]);
+    const float base = mx == -INFINITY ? 0.f : mx;
+    float den = 0.f, num = 0.f;
+    for (int s = 0; s < mg.y; ++s) {
+      const long long q = (long long)(mg.x + s) * p.num_q_heads + h;
+      const float f = fast_exp2(p.part_ml[2 * q] - base);
+      den += p.part_ml[2 * q + 1] * f;
+      num += p.part_acc[q * D + d] * f;
+    }
+    if (p.sinks) den += fast_exp2(p.sinks[h] * kLog2e - base);
+    p.out[(long long)b * p.o_sb + (long long)h * p.o_sh + d] =
+        __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+    if (p.lse && d == 0)
+      p.lse[(long long)b * p.num_q_heads + h] =
+          den > 0.f ? (base + log2f(den)) * kLn2 : -INFINITY;
+  }
+}
+
+template <int D, int HKV>
+int launch_attention(const AttnParams& p, int n_items, const int2* merge, int batch,
+                     cudaStream_t s) {
+  constexpr int TK = (HKV * D <= 512) ? 32 : 16;
+  constexpr int NSTAGE = (HKV * D <= 256) ? 4 : 3;
+  using C = Cfg<D, HKV, TK, NSTAGE>;
+  auto kernel = decode_attention_kernel<D, HKV, TK, NSTAGE>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+      cudaSuccess)
+    return AKV_ERR_CUDA;
+  if (n_items > 0) kernel<<<n_items, C::kThreads, C::kSmem, s>>>(p);
+  if (merge != nullptr && batch > 0) decode_combine_kernel<D><<<batch, 256, 0, s>>>(p, merge, batch);
+  return launch_status();
+}
+
+template <int D>
+int dispatch_heads(const AttnParams& p, int hkv, int n_items, const int2* merge, int batch,
+                   cudaStream_t s) {
+  switch (hkv) {
+    case 1: return launch_attention<D, 1>(p, n_items, merge, batch, s);
+    case 2: return launch_attention<D, 2>(p, n_items, merge, batch, s);
+    case 4: return launch_attention<D, 4>(p, n_items, merge, batch, s);
+    case 8: return launch_attention<D, 8>(p, n_items, merge, batch, s);
+  }
+  return AKV_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+}  // namespace akv
+
+extern "C" int akv_decode_attention(
+    const void* q, int64_t q_stride_batch, int64_t q_stride_head, const void* k_pool,
+    const void* v_pool, int64_t k_stride_slot, int64_t k_stride_head, int64_t v_stride_slot,
+    int64_t v_stride_head, int64_t num_slots, const int32_t* kv_indices, const float* sinks,
+    float sm_scale, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    const int32_t* work, int32_t n_items, const int32_t* merge, float* partial_acc,
+    float* partial_ml, void* out, int64_t out_stride_batch, int64_t out_stride_head, float* lse,
+    int32_t* error_flag, void* stream) {
+  using namespace akv;
+  if (batch < 0 || n_items < 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads * kGroup ||
+      !q || !k_pool || !v_pool || !kv_indices || !work || !out || num_slots <= 0)
+    return AKV_ERR_INVALID;
+  if ((q_stride_head % 2) || (reinterpret_cast<uintptr_t>(q) & 3) ||
+      (reinterpret_cast<uintptr_t>(k_pool) & 15) || (reinterpret_cast<uintptr_t>(v_pool) & 15) ||
+      (k_stride_slot % 8) || (k_stride_head % 8) || (v_stride_slot % 8) || (v_stride_head % 8))
+    return AKV_ERR_INVALID;  // 16-byte cp.async rows and 4-byte q pairs
+  AttnParams p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.q_sb = q_stride_batch;
+  p.q_sh = q_stride_head;
+  p.k = static_cast<const __nv_bfloat16*>(k_pool);
+  p.v = static_cast<const __nv_bfloat16*>(v_pool);
+  p.k_ss = k_stride_slot;
+  p.k_sh = k_stride_head;
+  p.v_ss = v_stride_slot;
+  p.v_sh = v_stride_head;
+  p.num_slots = num_slots;
+  p.kv_indices = kv_indices;
+  p.sinks = sinks;
+  p.scale_log2 = sm_scale * kLog2e;
+  p.work = reinterpret_cast<const int4*>(work);
+  p.part_acc = partial_acc;
+  p.part_ml = partial_ml;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_sb = out_stride_batch;
+  p.o_sh = out_stride_head;
+  p.lse = lse;
+  p.num_q_heads = num_q_heads;
+  p.error_flag = error_flag;
+  const int2* mg = reinterpret_cast<const int2*>(merge);
+  if (mg != nullptr && (!partial_acc || !partial_ml)) return AKV_ERR_INVALID;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (head_dim) {
+    case 64: return dispatch_heads<64>(p, num_kv_heads, n_items, mg, batch, s);
+    case 128: return dispatch_heads<128>(p, num_kv_heads, n_items, mg, batch, s);
+  }
+  return AKV_ERR_UNSUPPORTED;
+}

@@ -102,12 +102,63 @@ __device__ __forceinline__ float cache_at(const void* base, long long idx) {
   return Elem<C>::to_f32(static_cast<const C*>(base)[idx]);
 }
 
+// Correctly rounded n / s for both numerators of a pair, given
+// y = RN(1/s) (computed once per token and pair with __frcp_rn and reused
+// across every layer and head).
+//
+// Method: Markstein's FMA correction (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990; "IA-64 and Elementary Functions", 2000): if y is within
+// half an ulp of 1/s and q within one ulp of n/s, then r = n - s*q is exact
+// in one FMA and RN(q + r*y) is the correctly rounded quotient.  q0 = RN(n*y)
+// can be up to about 1.5 ulp away, so one correction step first brings it
+// within (0.5 + 2^-23) ulp and a second one, under the theorem, gives
+// RN(n/s) -- the value IEEE division (__fdiv_rn, the reference's tl.div_rn)
+// returns.  The theorem needs no underflow or overflow in the remainders:
+// the fast path is taken only when s lies in [2^-60, 2^60] (checked once per
+// token) and |n| in [2^-100, 2^100]; anything else, zeros (whose sign the
+// FMA chain would not keep) and non-finite values included, uses __fdiv_rn.
+// tests/test_reposition_gpu.py compares the two over adversarial inputs.
+constexpr float kDivMin = 0x1p-60f, kDivMax = 0x1p60f;
+constexpr float kNumMin = 0x1p-100f, kNumMax = 0x1p100f;
+
+__device__ __forceinline__ float markstein_div(float n, float s, float y) {
+  float q = __fmul_rn(n, y);
+  float r = __fmaf_rn(-s, q, n);
+  q = __fmaf_rn(r, y, q);
+  r = __fmaf_rn(-s, q, n);
+  return __fmaf_rn(r, y, q);
+}
+
+__device__ __forceinline__ void div2_rn(float n1, float n2, float s, float y, bool s_ok,
+                                        float& u1, float& u2) {
+  const float a1 = fabsf(n1), a2 = fabsf(n2);
+  if (s_ok && a1 >= kNumMin && a1 <= kNumMax && a2 >= kNumMin && a2 <= kNumMax) {
+    u1 = markstein_div(n1, s, y);
+    u2 = markstein_div(n2, s, y);
+  } else {
+    u1 = __fdiv_rn(n1, s);
+    u2 = __fdiv_rn(n2, s);
+  }
+}
+
 // Layers loaded before any is rotated, so that 2 * LU independent 16-byte
 // loads are in flight per thread.
-template <typename T> struct Unroll { static constexpr int value = 2; };
+#ifndef AKV_REPOSITION_UNROLL
+#define AKV_REPOSITION_UNROLL 2
+#endif
+// Bytes per vector access (16 or 8) and resident blocks per SM the register
+// budget is sized for.
+#ifndef AKV_REPOSITION_VECTOR_BYTES
+#define AKV_REPOSITION_VECTOR_BYTES 16
+#endif
+#ifndef AKV_REPOSITION_MIN_BLOCKS
+#define AKV_REPOSITION_MIN_BLOCKS 2
+#endif
+template <typename T> struct Unroll { static constexpr int value = AKV_REPOSITION_UNROLL; };
 
 template <typename T, typename C, bool NEOX, int V>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, AKV_REPOSITION_MIN_BLOCKS)
 reposition_kernel(const RepositionParams p) {
   constexpr int LU = Unroll<T>::value;
   __shared__ unsigned long long s_k[kMaxLayers];
@@ -116,7 +167,7 @@ reposition_kernel(const RepositionParams p) {
   for (int i = threadIdx.x; i < p.n_layers; i += blockDim.x) {
     s_k[i] = p.k_ptrs[i];
     s_v[i] = p.v_ptrs[i];
-    s_vec[i] = ((s_k[i] | s_v[i]) & 15) == 0;
+    s_vec[i] = ((s_k[i] | s_v[i]) & (V * sizeof(T) - 1)) == 0;
   }
   __syncthreads();
 
@@ -156,7 +207,8 @@ reposition_kernel(const RepositionParams p) {
     const int o1 = NEOX ? j : 2 * j;
     const int o2 = NEOX ? p.half + j : 2 * j + V;
 
-    float oc[V], os[V], nc[V], ns[V], sc[V];
+    float oc[V], os[V], nc[V], ns[V], sc[V], rc[V];
+    bool scale_ok = true;
     {
       const long long ro = po * p.cache_stride, rn = pn * p.cache_stride;
 #pragma unroll
@@ -166,6 +218,8 @@ reposition_kernel(const RepositionParams p) {
         nc[i] = cache_at<C>(p.cache, rn + j + i);
         ns[i] = cache_at<C>(p.cache, rn + p.half + j + i);
         sc[i] = __fadd_rn(__fmul_rn(oc[i], oc[i]), __fmul_rn(os[i], os[i]));
+        rc[i] = __frcp_rn(sc[i]);
+        scale_ok = scale_ok && sc[i] >= kDivMin && sc[i] <= kDivMax;
       }
     }
     const long long ks = src * p.k_ss + head * p.k_sh;
@@ -193,19 +247,25 @@ reposition_kernel(const RepositionParams p) {
             x[V + i] = Elem<T>::to_f32(b[q].e[i]);
           }
           float y[2 * V];
+          if (same) {
+            // Old == new position: the reference stores the source values.
 #pragma unroll
-          for (int i = 0; i < V; ++i) {
-            // NEOX pairs (i, half + i) -> (x[i], x[V + i]); GPT-J pairs
-            // (2i, 2i + 1) of the 2V contiguous elements.
-            const int i1 = NEOX ? i : 2 * i;
-            const int i2 = NEOX ? V + i : 2 * i + 1;
-            const float x1 = x[i1], x2 = x[i2];
-            const float u1 = __fdiv_rn(__fadd_rn(__fmul_rn(x1, oc[i]), __fmul_rn(x2, os[i])), sc[i]);
-            const float u2 = __fdiv_rn(__fsub_rn(__fmul_rn(x2, oc[i]), __fmul_rn(x1, os[i])), sc[i]);
-            const float y1 = __fsub_rn(__fmul_rn(u1, nc[i]), __fmul_rn(u2, ns[i]));
-            const float y2 = __fadd_rn(__fmul_rn(u2, nc[i]), __fmul_rn(u1, ns[i]));
-            y[i1] = same ? x1 : y1;
-            y[i2] = same ? x2 : y2;
+            for (int i = 0; i < 2 * V; ++i) y[i] = x[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+              // NEOX pairs (i, half + i) -> (x[i], x[V + i]); GPT-J pairs
+              // (2i, 2i + 1) of the 2V contiguous elements.
+              const int i1 = NEOX ? i : 2 * i;
+              const int i2 = NEOX ? V + i : 2 * i + 1;
+              const float x1 = x[i1], x2 = x[i2];
+              const float n1 = __fadd_rn(__fmul_rn(x1, oc[i]), __fmul_rn(x2, os[i]));
+              const float n2 = __fsub_rn(__fmul_rn(x2, oc[i]), __fmul_rn(x1, os[i]));
+              float u1, u2;
+              div2_rn(n1, n2, sc[i], rc[i], scale_ok, u1, u2);
+              y[i1] = __fsub_rn(__fmul_rn(u1, nc[i]), __fmul_rn(u2, ns[i]));
+              y[i2] = __fadd_rn(__fmul_rn(u2, nc[i]), __fmul_rn(u1, ns[i]));
+            }
           }
           Chunk<T, V> ra, rb;
 #pragma unroll
@@ -269,7 +329,7 @@ int launch(const RepositionParams& p, cudaStream_t stream) {
 
 template <typename T, typename C>
 int dispatch_style(const RepositionParams& p, bool neox, bool vec, cudaStream_t s) {
-  constexpr int VV = 16 / sizeof(T);
+  constexpr int VV = AKV_REPOSITION_VECTOR_BYTES / sizeof(T);
   if (vec) return neox ? launch<T, C, true, VV>(p, s) : launch<T, C, false, VV>(p, s);
   return neox ? launch<T, C, true, 1>(p, s) : launch<T, C, false, 1>(p, s);
 }
@@ -332,8 +392,8 @@ extern "C" int akv_reposition_kv_layers(
   p.error_flag = error_flag;
 
   const int esize = kv_dtype == AKV_F32 ? 4 : 2;
-  const int V = 16 / esize;
-  // The 16-byte path needs every vector to start on a 16-byte boundary:
+  const int V = AKV_REPOSITION_VECTOR_BYTES / esize;
+  // The vector path needs every vector to start on a vector boundary:
   // shapes and strides are checked here, each layer's base address in the
   // kernel (a misaligned layer falls back to element accesses).
   const bool vec = (p.half % V == 0) && (head_dim % V == 0) && (rotary_dim % V == 0) &&
@@ -347,4 +407,40 @@ extern "C" int akv_reposition_kv_layers(
     case AKV_F16: return dispatch_cache<__half>(p, cache_dtype, neox, vec, s);
   }
   return AKV_ERR_INVALID;
+}
+
+namespace akv {
+namespace {
+
+__global__ void divide_kernel(const float* n, const float* s, float* q, int64_t count,
+                              int method) {
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += step) {
+    const float d = s[i];
+    if (method == 0) {
+      q[i] = __fdiv_rn(n[i], d);
+    } else {
+      const bool d_ok = d >= kDivMin && d <= kDivMax;
+      float u1, u2;
+      div2_rn(n[i], n[i], d, __frcp_rn(d), d_ok, u1, u2);
+      q[i] = u1;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace akv
+
+extern "C" int akv_reposition_divide(const float* numerators, const float* denominators,
+                                     float* quotients, int64_t count, int32_t method,
+                                     void* stream) {
+  using namespace akv;
+  if (count < 0 || (method != 0 && method != 1) ||
+      (count > 0 && (!numerators || !denominators || !quotients)))
+    return AKV_ERR_INVALID;
+  if (count == 0) return AKV_OK;
+  const int blocks = (int)((count + 255) / 256 < 4096 ? (count + 255) / 256 : 4096);
+  divide_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      numerators, denominators, quotients, count, method);
+  return launch_status();
 }

@@ -63,8 +63,8 @@ WORKLOADS = {
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     return p.parse_args()
@@ -134,59 +134,70 @@ def ncu_traffic(workload):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during a timed region."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU,
+    sampled through NVML (read-only queries) every 50 ms on a thread during
+    a timed region.  Samples taken while the GPU is busy count as under
+    load."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device_index):
-        self.proc = None
-        self.out = None
+        self.handle = None
+        self.samples = []
+        self._stop = None
+        self._thread = None
         try:
+            import pynvml
+
+            pynvml.nvmlInit()
             uuid = str(torch.cuda.get_device_properties(device_index).uuid)
-            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
-        except Exception:
-            ident = str(device_index)
-        self.ident = ident
+            uuid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # no NVML: report the clocks as unknown
+            self.error = f"{type(exc).__name__}: {exc}"
+
+    def _run(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                reasons = get_reasons(self.handle)
+                util = nv.nvmlDeviceGetUtilizationRates(self.handle).gpu
+                self.samples.append((sm, reasons, util))
+            except Exception:
+                pass
+            self._stop.wait(0.05)
 
     def start(self):
-        try:
-            self.out = open(os.devnull, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", self.ident],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+        if self.handle is None:
+            return
+        import threading
+
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self.handle is None:
+            return {"error": getattr(self, "error", "NVML unavailable")}
+        self._stop.set()
+        self._thread.join(timeout=2)
+        if not self.samples:
             return None
-        self.proc.terminate()
-        try:
-            text, _ = self.proc.communicate(timeout=5)
-        except Exception:
-            self.proc.kill()
-            text = ""
-        sm, smax, reasons = [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in text.strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 6:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                smax.append(float(parts[1]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[2:6]):
-                if flag.lower() == "active":
+        loaded = [s for s in self.samples if s[2] > 0] or self.samples
+        reasons = set()
+        for _, bits, _ in loaded:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
                     reasons.add(name)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(s[0] for s in loaded), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples),
+                "samples_under_load": len(loaded)}
 
 
 def dist_setup():

@@ -84,6 +84,18 @@ int akv_reposition_kv_layers(
     int64_t max_position, int32_t* error_flag, void* stream);
 
 /*
+ * The correctly rounded fp32 division the reposition kernel uses, exported
+ * so a caller can check it against IEEE division on its own GPU: method 0
+ * is IEEE division (__fdiv_rn, the reference's tl.div_rn), method 1 the
+ * kernel's path (Markstein's FMA correction over a per-token reciprocal,
+ * with an IEEE fallback outside its safe range).  quotients[i] =
+ * numerators[i] / denominators[i] for i < count, all DEVICE fp32.  No
+ * reference counterpart: a self-check of this build's arithmetic.
+ */
+int akv_reposition_divide(const float* numerators, const float* denominators,
+                          float* quotients, int64_t count, int32_t method, void* stream);
+
+/*
  * Drop + Reposition of a batch of requests, on the device.
  *
  * Replaces, for programs with one Drop event and one Reposition at the end
@@ -181,6 +193,40 @@ int akv_build_decode_metadata(
     const int64_t* row_ids, const int64_t* seq_lens, int64_t window, const int64_t* mapping,
     int64_t multiplier, int32_t batch, int32_t* kv_indptr, int64_t* lengths_out,
     int64_t* starts_out, int32_t* kv_indices, void* stream);
+
+/*
+ * Paged GQA decode attention with learned sinks over a compacted index
+ * list.  Replaces the native decode kernels the reference runs over the
+ * registry's kv_indptr / kv_indices (FlashInfer decode wrapper / FA3
+ * flash_attn_with_kvcache, upstream, not vendored; AKV glue at
+ * akv/system/sglang.patch:2170-2183) and AKV's sink correction
+ * o *= sigmoid(lse - sink) (srt/layers/attention/context_backend.py:254-272),
+ * computed here as out = sum e^s v / (sum e^s + e^sink).
+ *
+ * q: bf16 [batch, num_q_heads, head_dim] (strides in elements); K / V pools:
+ * bf16 [slots, num_kv_heads, head_dim] with the given strides (16-byte
+ * aligned rows); kv_indices: int32 slots.  num_q_heads = 8 * num_kv_heads,
+ * num_kv_heads in {1, 2, 4, 8}, head_dim in {64, 128}.  sinks: fp32
+ * [num_q_heads] natural-log logits or NULL.  sm_scale multiplies q.k.
+ * work: DEVICE int32 [n_items, 4] rows {request, kv_begin, kv_end, partial}
+ * (kv_begin/kv_end index kv_indices; partial = -1 writes the request's
+ * output directly, else the item's slot in partial_acc [P, q_heads, D] and
+ * partial_ml [P, q_heads, 2]); merge: DEVICE int32 [batch, 2] rows
+ * {first partial, count} (count 0 = written directly) or NULL when no item
+ * is split.  out: bf16 [batch, q_heads, head_dim]; lse: fp32 [batch, q_heads]
+ * natural-log LSE including the sink, or NULL.  A slot outside [0, num_slots)
+ * is read as slot 0 and sets *error_flag (DEVICE int32, may be NULL).
+ * The host side (akv_b200/context_attention.py) builds work/merge from
+ * host-known lengths, as FlashInfer's plan() does.
+ */
+int akv_decode_attention(
+    const void* q, int64_t q_stride_batch, int64_t q_stride_head, const void* k_pool,
+    const void* v_pool, int64_t k_stride_slot, int64_t k_stride_head, int64_t v_stride_slot,
+    int64_t v_stride_head, int64_t num_slots, const int32_t* kv_indices, const float* sinks,
+    float sm_scale, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    const int32_t* work, int32_t n_items, const int32_t* merge, float* partial_acc,
+    float* partial_ml, void* out, int64_t out_stride_batch, int64_t out_stride_head, float* lse,
+    int32_t* error_flag, void* stream);
 
 /*
  * Overflow-row slot scatter.  Replaces the Triton kernel write_row_slots

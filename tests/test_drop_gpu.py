@@ -25,7 +25,8 @@ def _run(program, rows, ring_free, ring_capacity=None, reposition=True, max_slot
         table[row_ids[r], : len(rows[r])] = rows[r]
     req_to_token = torch.from_numpy(table).to(dev)
     ring = FreeSlotRing(torch.from_numpy(np.asarray(ring_free, np.int32)),
-                        capacity=ring_capacity, device=dev)
+                        capacity=ring_capacity or len(ring_free) + program.total_tokens + 1,
+                        device=dev)
     comp = DropCompactor(program.total_tokens, nreq, max(1, len(program.ranges) // 2), dev)
     res = comp.run(program.token_counts, program.range_offsets, program.ranges, req_to_token,
                    row_ids, ring, shared_prefix=program.shared_prefix if

@@ -285,3 +285,60 @@ def test_reposition_c2_shape_sampled_rows_match_oracle():
     for layer in range(layers):
         got = ks[layer][torch.from_numpy(src[sample].astype(np.int64)).to(dev)].cpu()
         np.testing.assert_array_equal(got.view(torch.int16).numpy().view(np.uint16), hk[layer])
+
+
+def _random_floats(rng, n, lo_exp, hi_exp):
+    """fp32 values with uniformly random exponents and mantissas, both signs."""
+    exp = rng.integers(lo_exp + 127, hi_exp + 127 + 1, size=n).astype(np.uint32)
+    mant = rng.integers(0, 1 << 23, size=n, dtype=np.uint32)
+    sign = rng.integers(0, 2, size=n, dtype=np.uint32) << 31
+    return (sign | (np.clip(exp, 0, 254) << 23) | mant).view(np.float32)
+
+
+def test_reposition_division_matches_ieee():
+    """The kernel's division (Markstein correction over a per-token
+    reciprocal, IEEE fallback outside its range) returns exactly what IEEE
+    division returns, over 48M quotients: realistic RoPE scales (plain ~1,
+    YaRN ~1.81, bf16 tables), log-uniform denominators across the fast-path
+    bounds, numerators over every binade, and special values."""
+    from akv_b200 import _native
+
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(2024)
+    n = 1 << 24
+    cases = []
+    # 1. realistic: numerators ~ products of N(0,1) K values with cos/sin
+    num = (rng.standard_normal(n) * rng.standard_normal(n)).astype(np.float32)
+    den = np.where(rng.random(n) < 0.5, 1.0 + (rng.random(n) - 0.5) * 2e-7,
+                   (0.1 * np.log(32) + 1) ** 2 * (1 + (rng.random(n) - 0.5) * 1e-6))
+    cases.append((num, den.astype(np.float32)))
+    # 2. every binade of the numerator, denominators across and beyond the bounds
+    cases.append((_random_floats(rng, n, -149, 127), np.abs(_random_floats(rng, n, -80, 80))))
+    # 3. numerators near the fast-path edges, random denominators near 1
+    edge = np.concatenate([_random_floats(rng, n // 4, -102, -98),
+                           _random_floats(rng, n // 4, 98, 102),
+                           _random_floats(rng, n // 2, -30, 30)])
+    cases.append((edge, np.abs(_random_floats(rng, n, -2, 2))))
+    special = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e-45, -1e-45, 1e-38, 3.4e38,
+                        -3.4e38, 1.0, -1.0], np.float32)
+    sp_n, sp_d = np.meshgrid(special, np.abs(special))
+    cases.append((sp_n.reshape(-1), sp_d.reshape(-1).astype(np.float32)))
+    for num, den in cases:
+        a = torch.from_numpy(np.ascontiguousarray(num, np.float32)).to(dev)
+        b = torch.from_numpy(np.ascontiguousarray(den, np.float32)).to(dev)
+        q0 = torch.empty_like(a)
+        q1 = torch.empty_like(a)
+        stream = _native.stream_of(dev)
+        _native.check(_native.lib.akv_reposition_divide(_native.ptr(a), _native.ptr(b),
+                                                         _native.ptr(q0), a.numel(), 0, stream),
+                      "divide")
+        _native.check(_native.lib.akv_reposition_divide(_native.ptr(a), _native.ptr(b),
+                                                         _native.ptr(q1), a.numel(), 1, stream),
+                      "divide")
+        torch.cuda.synchronize()
+        x0, x1 = q0.view(torch.int32), q1.view(torch.int32)
+        both_nan = torch.isnan(q0) & torch.isnan(q1)
+        bad = (x0 != x1) & ~both_nan
+        assert int(bad.sum().item()) == 0, (
+            f"{int(bad.sum())} quotients differ, e.g. "
+            f"{a[bad][:4].tolist()} / {b[bad][:4].tolist()}")
