@@ -6,16 +6,24 @@
 // :126-236).  The reference launches one 4-warp program per
 // (token, layer, head) that moves a single 128-byte row.  Here one thread
 // ("unit") owns V consecutive rotary pairs of one (token, head) -- two
-// 16-byte vectors -- and walks all layers, so the token's slots, positions
-// and cos/sin values are loaded once and reused across layers, and every
-// warp moves whole contiguous [heads x head_dim] rows with 16-byte accesses.
+// 16-byte vectors per layer -- and walks all layers: the token's slots,
+// positions and cos/sin values are loaded once and reused across layers,
+// and a warp moves whole contiguous [heads x head_dim] rows.
+//
+// Memory pipeline: a unit's rows for the next S-1 layers are in flight
+// while it rotates the current one.  They are fetched with per-thread
+// cp.async into the thread's own shared-memory slots (no registers held,
+// no barrier: a thread only reads what it fetched), so the loads of up to
+// eight layers overlap the arithmetic of the current layer.  Results are
+// stored straight back with streaming (evict-first) 16-byte stores.
 //
 // Arithmetic is the reference's, operation for operation, with explicitly
 // rounded intrinsics (no FMA contraction):
 //   s  = oc*oc + os*os
 //   u1 = (x1*oc + x2*os) / s         u2 = (x2*oc - x1*os) / s
 //   y1 = u1*nc - u2*ns               y2 = u2*nc + u1*ns
-// and the source values are stored unchanged when old == new position.
+// the divisions correctly rounded (div2_rn below), and the source values
+// stored unchanged when old == new position.
 
 #include "common.cuh"
 
@@ -24,6 +32,14 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxLayers = 512;
+// 16-byte staging slots per thread: 8 layers of a K pair in flight for an
+// in-place unit, 4 layers of (K pair + 2 copied vectors) for copy-on-write.
+constexpr int kSlots = 16;
+constexpr int kStageBytes = kSlots * kThreads * 16;  // 64 KiB per block
+
+#ifndef AKV_REPOSITION_MIN_BLOCKS
+#define AKV_REPOSITION_MIN_BLOCKS 2
+#endif
 
 struct RepositionParams {
   const unsigned long long* k_ptrs;
@@ -48,12 +64,10 @@ struct RepositionParams {
   int* error_flag;
 };
 
-// V consecutive elements of T, moved with one 16- or 8-byte access when
-// V * sizeof(T) is 16 or 8 bytes, element by element otherwise.
-template <typename T, int V> struct alignas(V * sizeof(T) >= 16 ? 16 : 8) Chunk {
+// V consecutive elements of T, moved with one 16-byte access when
+// V * sizeof(T) is 16 and the layer is aligned, element by element otherwise.
+template <typename T, int V> struct alignas(V * sizeof(T) >= 16 ? 16 : alignof(T)) Chunk {
   T e[V];
-  // `vec` is false for a layer whose base address is not 16-byte aligned;
-  // the branch is uniform across the grid for a given layer.
   __device__ __forceinline__ void load(const T* p, bool vec) {
     if constexpr (V * sizeof(T) == 16) {
       if (vec) {
@@ -62,13 +76,6 @@ template <typename T, int V> struct alignas(V * sizeof(T) >= 16 ? 16 : 8) Chunk 
                      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                      : "l"(p));
         *reinterpret_cast<uint4*>(e) = r;
-        return;
-      }
-    } else if constexpr (V * sizeof(T) == 8) {
-      if (vec) {
-        uint2 r;
-        asm volatile("ld.global.cs.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-        *reinterpret_cast<uint2*>(e) = r;
         return;
       }
     }
@@ -84,18 +91,27 @@ template <typename T, int V> struct alignas(V * sizeof(T) >= 16 ? 16 : 8) Chunk 
                      : "memory");
         return;
       }
-    } else if constexpr (V * sizeof(T) == 8) {
-      if (vec) {
-        const uint2 r = *reinterpret_cast<const uint2*>(e);
-        asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(r.x), "r"(r.y)
-                     : "memory");
-        return;
-      }
     }
 #pragma unroll
     for (int i = 0; i < V; ++i) p[i] = e[i];
   }
+  __device__ __forceinline__ void load_shared(uint32_t addr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "r"(addr));
+    *reinterpret_cast<uint4*>(e) = r;
+  }
 };
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 template <typename C>
 __device__ __forceinline__ float cache_at(const void* base, long long idx) {
@@ -104,7 +120,7 @@ __device__ __forceinline__ float cache_at(const void* base, long long idx) {
 
 // Correctly rounded n / s for both numerators of a pair, given
 // y = RN(1/s) (computed once per token and pair with __frcp_rn and reused
-// across every layer and head).
+// across every layer).
 //
 // Method: Markstein's FMA correction (P. Markstein, "Computation of
 // elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
@@ -114,13 +130,14 @@ __device__ __forceinline__ float cache_at(const void* base, long long idx) {
 // can be up to about 1.5 ulp away, so one correction step first brings it
 // within (0.5 + 2^-23) ulp and a second one, under the theorem, gives
 // RN(n/s) -- the value IEEE division (__fdiv_rn, the reference's tl.div_rn)
-// returns.  The theorem needs no underflow or overflow in the remainders:
-// the fast path is taken only when s lies in [2^-60, 2^60] (checked once per
-// token) and |n| in [2^-100, 2^100]; anything else, zeros (whose sign the
-// FMA chain would not keep) and non-finite values included, uses __fdiv_rn.
+// returns.  The theorem needs the quotient and remainders clear of overflow
+// and underflow: the fast path is taken only when s lies in [2^-30, 2^30]
+// (checked once per token) and |n| in [2^-60, 2^60], so the quotient stays
+// within [2^-90, 2^90]; anything else, zeros (whose sign the FMA chain would
+// not keep) and non-finite values included, uses __fdiv_rn.
 // tests/test_reposition_gpu.py compares the two over adversarial inputs.
-constexpr float kDivMin = 0x1p-60f, kDivMax = 0x1p60f;
-constexpr float kNumMin = 0x1p-100f, kNumMax = 0x1p100f;
+constexpr float kDivMin = 0x1p-30f, kDivMax = 0x1p30f;
+constexpr float kNumMin = 0x1p-60f, kNumMax = 0x1p60f;
 
 __device__ __forceinline__ float markstein_div(float n, float s, float y) {
   float q = __fmul_rn(n, y);
@@ -142,53 +159,204 @@ __device__ __forceinline__ void div2_rn(float n1, float n2, float s, float y, bo
   }
 }
 
-// Layers loaded before any is rotated, so that 2 * LU independent 16-byte
-// loads are in flight per thread.
-#ifndef AKV_REPOSITION_UNROLL
-#define AKV_REPOSITION_UNROLL 2
-#endif
-// Bytes per vector access (16 or 8) and resident blocks per SM the register
-// budget is sized for.
-#ifndef AKV_REPOSITION_VECTOR_BYTES
-#define AKV_REPOSITION_VECTOR_BYTES 16
-#endif
-#ifndef AKV_REPOSITION_MIN_BLOCKS
-#define AKV_REPOSITION_MIN_BLOCKS 2
-#endif
-template <typename T> struct Unroll { static constexpr int value = AKV_REPOSITION_UNROLL; };
+// Per-unit constants: the V pairs' old/new cos and sin, s = cos^2+sin^2 of
+// the old angle and its reciprocal.
+template <int V> struct Trig {
+  float oc[V], os[V], nc[V], ns[V], sc[V], rc[V];
+  bool scale_ok;
+};
+
+template <typename C, int V>
+__device__ __forceinline__ void load_trig(const RepositionParams& p, long long po, long long pn,
+                                          int j, Trig<V>& tr) {
+  const long long ro = po * p.cache_stride, rn = pn * p.cache_stride;
+  tr.scale_ok = true;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    tr.oc[i] = cache_at<C>(p.cache, ro + j + i);
+    tr.os[i] = cache_at<C>(p.cache, ro + p.half + j + i);
+    tr.nc[i] = cache_at<C>(p.cache, rn + j + i);
+    tr.ns[i] = cache_at<C>(p.cache, rn + p.half + j + i);
+    tr.sc[i] = __fadd_rn(__fmul_rn(tr.oc[i], tr.oc[i]), __fmul_rn(tr.os[i], tr.os[i]));
+    tr.rc[i] = __frcp_rn(tr.sc[i]);
+    tr.scale_ok = tr.scale_ok && tr.sc[i] >= kDivMin && tr.sc[i] <= kDivMax;
+  }
+}
+
+// Rotate one unit's two chunks (a: first V elements, b: second) in place.
+template <typename T, bool NEOX, int V>
+__device__ __forceinline__ void rotate(Chunk<T, V>& a, Chunk<T, V>& b, const Trig<V>& tr,
+                                       bool same) {
+  if (same) return;  // old == new position: the reference stores the source values
+  float x[2 * V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    x[i] = Elem<T>::to_f32(a.e[i]);
+    x[V + i] = Elem<T>::to_f32(b.e[i]);
+  }
+  float y[2 * V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    // NEOX pairs (i, half + i) -> (x[i], x[V + i]); GPT-J pairs (2i, 2i + 1)
+    // of the 2V contiguous elements.
+    const int i1 = NEOX ? i : 2 * i;
+    const int i2 = NEOX ? V + i : 2 * i + 1;
+    const float x1 = x[i1], x2 = x[i2];
+    const float n1 = __fadd_rn(__fmul_rn(x1, tr.oc[i]), __fmul_rn(x2, tr.os[i]));
+    const float n2 = __fsub_rn(__fmul_rn(x2, tr.oc[i]), __fmul_rn(x1, tr.os[i]));
+    float u1, u2;
+    div2_rn(n1, n2, tr.sc[i], tr.rc[i], tr.scale_ok, u1, u2);
+    y[i1] = __fsub_rn(__fmul_rn(u1, tr.nc[i]), __fmul_rn(u2, tr.ns[i]));
+    y[i2] = __fadd_rn(__fmul_rn(u2, tr.nc[i]), __fmul_rn(u1, tr.ns[i]));
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    a.e[i] = Elem<T>::from_f32(y[i]);
+    b.e[i] = Elem<T>::from_f32(y[V + i]);
+  }
+}
+
+struct UnitGeom {
+  long long ks, kd, vs, vd;  // element offsets of the (slot, head) rows
+  int o1, o2;                // offsets of the unit's two chunks in the head row
+  int chunk, chunks, tail_vecs, copy_vecs;
+  bool in_place, same;
+};
+
+// Element offset of copy vector c (K tail first, then V) and its table.
+__device__ __forceinline__ long long copy_src(const UnitGeom& g, int c, int rot, int V) {
+  return c < g.tail_vecs ? g.ks + rot + (long long)c * V : g.vs + (long long)(c - g.tail_vecs) * V;
+}
+__device__ __forceinline__ long long copy_dst(const UnitGeom& g, int c, int rot, int V) {
+  return c < g.tail_vecs ? g.kd + rot + (long long)c * V : g.vd + (long long)(c - g.tail_vecs) * V;
+}
+
+// Unpipelined walk over the layers (element path, misaligned layers, or a
+// copy-on-write that moves more than two vectors per unit and layer).
+template <typename T, bool NEOX, int V>
+__device__ void unit_direct(const RepositionParams& p, const unsigned long long* s_k,
+                            const unsigned long long* s_v, const bool* s_vec, const UnitGeom& g,
+                            const Trig<V>& tr) {
+  for (int l = 0; l < p.n_layers; ++l) {
+    T* kb = reinterpret_cast<T*>(s_k[l]);
+    Chunk<T, V> a, b;
+    a.load(kb + g.ks + g.o1, s_vec[l]);
+    b.load(kb + g.ks + g.o2, s_vec[l]);
+    rotate<T, NEOX, V>(a, b, tr, g.same);
+    a.store(kb + g.kd + g.o1, s_vec[l]);
+    b.store(kb + g.kd + g.o2, s_vec[l]);
+    if (!g.in_place) {
+      T* vb = reinterpret_cast<T*>(s_v[l]);
+      for (int c = g.chunk; c < g.copy_vecs; c += g.chunks) {
+        T* base = c < g.tail_vecs ? kb : vb;
+        Chunk<T, V> t;
+        t.load(base + copy_src(g, c, p.rotary_dim, V), s_vec[l]);
+        t.store(base + copy_dst(g, c, p.rotary_dim, V), s_vec[l]);
+      }
+    }
+  }
+}
+
+// Pipelined walk: S layers in flight, NV staged 16-byte vectors per layer
+// (2 = the K pair; 4 = the K pair plus two copy vectors).
+template <typename T, bool NEOX, int V, int S, int NV>
+__device__ void unit_pipelined(const RepositionParams& p, const unsigned long long* s_k,
+                               const unsigned long long* s_v, uint32_t stage, const UnitGeom& g,
+                               const Trig<V>& tr) {
+  static_assert(S * NV <= kSlots, "staging slots");
+  constexpr uint32_t kSlotStride = kThreads * 16;
+  const int c0 = g.chunk, c1 = g.chunk + g.chunks;
+  auto issue = [&](int l) {
+    const T* kb = reinterpret_cast<const T*>(s_k[l]);
+    const uint32_t base = stage + (uint32_t)((l % S) * NV) * kSlotStride;
+    cp_async16(base, kb + g.ks + g.o1);
+    cp_async16(base + kSlotStride, kb + g.ks + g.o2);
+    if constexpr (NV == 4) {
+      const T* vb = reinterpret_cast<const T*>(s_v[l]);
+      if (c0 < g.copy_vecs)
+        cp_async16(base + 2 * kSlotStride,
+                   (c0 < g.tail_vecs ? kb : vb) + copy_src(g, c0, p.rotary_dim, V));
+      if (c1 < g.copy_vecs)
+        cp_async16(base + 3 * kSlotStride,
+                   (c1 < g.tail_vecs ? kb : vb) + copy_src(g, c1, p.rotary_dim, V));
+    }
+  };
+#pragma unroll
+  for (int l = 0; l < S - 1; ++l) {
+    if (l < p.n_layers) issue(l);
+    cp_async_commit();
+  }
+  for (int l = 0; l < p.n_layers; ++l) {
+    if (l + S - 1 < p.n_layers) issue(l + S - 1);
+    cp_async_commit();
+    cp_async_wait<S - 1>();
+    const uint32_t base = stage + (uint32_t)((l % S) * NV) * kSlotStride;
+    Chunk<T, V> a, b;
+    a.load_shared(base);
+    b.load_shared(base + kSlotStride);
+    rotate<T, NEOX, V>(a, b, tr, g.same);
+    T* kb = reinterpret_cast<T*>(s_k[l]);
+    a.store(kb + g.kd + g.o1, true);
+    b.store(kb + g.kd + g.o2, true);
+    if constexpr (NV == 4) {
+      T* vb = reinterpret_cast<T*>(s_v[l]);
+      if (c0 < g.copy_vecs) {
+        Chunk<T, V> t;
+        t.load_shared(base + 2 * kSlotStride);
+        t.store((c0 < g.tail_vecs ? kb : vb) + copy_dst(g, c0, p.rotary_dim, V), true);
+      }
+      if (c1 < g.copy_vecs) {
+        Chunk<T, V> t;
+        t.load_shared(base + 3 * kSlotStride);
+        t.store((c1 < g.tail_vecs ? kb : vb) + copy_dst(g, c1, p.rotary_dim, V), true);
+      }
+    }
+  }
+  cp_async_wait<0>();
+}
 
 template <typename T, typename C, bool NEOX, int V>
 __global__ void __launch_bounds__(kThreads, AKV_REPOSITION_MIN_BLOCKS)
 reposition_kernel(const RepositionParams p) {
-  constexpr int LU = Unroll<T>::value;
+  constexpr bool kVector = V * sizeof(T) == 16;
+  extern __shared__ __align__(16) unsigned char stage_smem[];
   __shared__ unsigned long long s_k[kMaxLayers];
   __shared__ unsigned long long s_v[kMaxLayers];
   __shared__ bool s_vec[kMaxLayers];
+  __shared__ int s_all_vec;
+  if (threadIdx.x == 0) s_all_vec = 1;
+  __syncthreads();
   for (int i = threadIdx.x; i < p.n_layers; i += blockDim.x) {
     s_k[i] = p.k_ptrs[i];
     s_v[i] = p.v_ptrs[i];
     s_vec[i] = ((s_k[i] | s_v[i]) & (V * sizeof(T) - 1)) == 0;
+    if (!s_vec[i]) s_all_vec = 0;
   }
   __syncthreads();
+  const bool all_vec = kVector && s_all_vec;
+  const uint32_t stage =
+      static_cast<uint32_t>(__cvta_generic_to_shared(stage_smem)) + threadIdx.x * 16;
 
   long long count = p.count;
   if (p.count_dev != nullptr) {
     const long long c = *p.count_dev;
     count = c < count ? c : count;
   }
-  const int chunks = p.half / V;             // units per head
-  const int upt = p.num_heads * chunks;      // units per token
+  UnitGeom g;
+  g.chunks = p.half / V;  // units per head
+  const int upt = p.num_heads * g.chunks;
   const long long total = count * upt;
   // Vectors of V elements per head that a copy moves: K tail then all of V.
-  const int tail_vecs = (p.head_dim - p.rotary_dim) / V;
-  const int copy_vecs = tail_vecs + p.head_dim / V;
+  g.tail_vecs = (p.head_dim - p.rotary_dim) / V;
+  g.copy_vecs = g.tail_vecs + p.head_dim / V;
+  const bool cow_pipelined = g.copy_vecs <= 2 * g.chunks;
   const long long stride = (long long)gridDim.x * blockDim.x;
 
   for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += stride) {
     const long long tok = u / upt;
     const int rem = (int)(u - tok * upt);
-    const int head = rem / chunks;
-    const int chunk = rem - head * chunks;
+    const int head = rem / g.chunks;
+    g.chunk = rem - head * g.chunks;
     const long long src = __ldg(p.src + tok);
     const long long dst = __ldg(p.dst + tok);
     if (p.skip_unmapped && (src <= 0 || dst <= 0)) continue;
@@ -199,137 +367,56 @@ reposition_kernel(const RepositionParams p) {
       if (p.error_flag != nullptr) *p.error_flag = 1;
       continue;
     }
-    const bool same = po == pn;
-    const bool in_place = src == dst;
-    if (same && in_place) continue;  // rewriting identical bits: nothing to do
+    g.same = po == pn;
+    g.in_place = src == dst;
+    if (g.same && g.in_place) continue;  // rewriting identical bits: nothing to do
 
-    const int j = chunk * V;  // first pair of this unit
-    const int o1 = NEOX ? j : 2 * j;
-    const int o2 = NEOX ? p.half + j : 2 * j + V;
+    const int j = g.chunk * V;  // first pair of this unit
+    g.o1 = NEOX ? j : 2 * j;
+    g.o2 = NEOX ? p.half + j : 2 * j + V;
+    g.ks = src * p.k_ss + head * p.k_sh;
+    g.kd = dst * p.k_ss + head * p.k_sh;
+    g.vs = src * p.v_ss + head * p.v_sh;
+    g.vd = dst * p.v_ss + head * p.v_sh;
+    Trig<V> tr;
+    load_trig<C, V>(p, po, pn, j, tr);
 
-    float oc[V], os[V], nc[V], ns[V], sc[V], rc[V];
-    bool scale_ok = true;
-    {
-      const long long ro = po * p.cache_stride, rn = pn * p.cache_stride;
-#pragma unroll
-      for (int i = 0; i < V; ++i) {
-        oc[i] = cache_at<C>(p.cache, ro + j + i);
-        os[i] = cache_at<C>(p.cache, ro + p.half + j + i);
-        nc[i] = cache_at<C>(p.cache, rn + j + i);
-        ns[i] = cache_at<C>(p.cache, rn + p.half + j + i);
-        sc[i] = __fadd_rn(__fmul_rn(oc[i], oc[i]), __fmul_rn(os[i], os[i]));
-        rc[i] = __frcp_rn(sc[i]);
-        scale_ok = scale_ok && sc[i] >= kDivMin && sc[i] <= kDivMax;
+    if constexpr (kVector) {
+      if (all_vec && g.in_place) {
+        unit_pipelined<T, NEOX, V, 8, 2>(p, s_k, s_v, stage, g, tr);
+        continue;
+      }
+      if (all_vec && cow_pipelined) {
+        unit_pipelined<T, NEOX, V, 4, 4>(p, s_k, s_v, stage, g, tr);
+        continue;
       }
     }
-    const long long ks = src * p.k_ss + head * p.k_sh;
-    const long long kd = dst * p.k_ss + head * p.k_sh;
-    const long long vs = src * p.v_ss + head * p.v_sh;
-    const long long vd = dst * p.v_ss + head * p.v_sh;
-
-    for (int l0 = 0; l0 < p.n_layers; l0 += LU) {
-      Chunk<T, V> a[LU], b[LU];
-#pragma unroll
-      for (int q = 0; q < LU; ++q) {
-        if (l0 + q < p.n_layers) {
-          const T* kb = reinterpret_cast<const T*>(s_k[l0 + q]);
-          a[q].load(kb + ks + o1, s_vec[l0 + q]);
-          b[q].load(kb + ks + o2, s_vec[l0 + q]);
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < LU; ++q) {
-        if (l0 + q < p.n_layers) {
-          float x[2 * V];
-#pragma unroll
-          for (int i = 0; i < V; ++i) {
-            x[i] = Elem<T>::to_f32(a[q].e[i]);
-            x[V + i] = Elem<T>::to_f32(b[q].e[i]);
-          }
-          float y[2 * V];
-          if (same) {
-            // Old == new position: the reference stores the source values.
-#pragma unroll
-            for (int i = 0; i < 2 * V; ++i) y[i] = x[i];
-          } else {
-#pragma unroll
-            for (int i = 0; i < V; ++i) {
-              // NEOX pairs (i, half + i) -> (x[i], x[V + i]); GPT-J pairs
-              // (2i, 2i + 1) of the 2V contiguous elements.
-              const int i1 = NEOX ? i : 2 * i;
-              const int i2 = NEOX ? V + i : 2 * i + 1;
-              const float x1 = x[i1], x2 = x[i2];
-              const float n1 = __fadd_rn(__fmul_rn(x1, oc[i]), __fmul_rn(x2, os[i]));
-              const float n2 = __fsub_rn(__fmul_rn(x2, oc[i]), __fmul_rn(x1, os[i]));
-              float u1, u2;
-              div2_rn(n1, n2, sc[i], rc[i], scale_ok, u1, u2);
-              y[i1] = __fsub_rn(__fmul_rn(u1, nc[i]), __fmul_rn(u2, ns[i]));
-              y[i2] = __fadd_rn(__fmul_rn(u2, nc[i]), __fmul_rn(u1, ns[i]));
-            }
-          }
-          Chunk<T, V> ra, rb;
-#pragma unroll
-          for (int i = 0; i < V; ++i) {
-            ra.e[i] = Elem<T>::from_f32(y[i]);
-            rb.e[i] = Elem<T>::from_f32(y[V + i]);
-          }
-          T* kb = reinterpret_cast<T*>(s_k[l0 + q]);
-          ra.store(kb + kd + o1, s_vec[l0 + q]);
-          rb.store(kb + kd + o2, s_vec[l0 + q]);
-        }
-      }
-      if (!in_place) {
-        // Copy-on-write: this unit moves vectors chunk, chunk + chunks, ...
-        // of the head's K tail followed by its V row.
-        for (int c = chunk; c < copy_vecs; c += chunks) {
-          Chunk<T, V> t[LU];
-#pragma unroll
-          for (int q = 0; q < LU; ++q) {
-            if (l0 + q < p.n_layers) {
-              if (c < tail_vecs) {
-                t[q].load(reinterpret_cast<const T*>(s_k[l0 + q]) + ks + p.rotary_dim + c * V,
-                          s_vec[l0 + q]);
-              } else {
-                t[q].load(reinterpret_cast<const T*>(s_v[l0 + q]) + vs + (c - tail_vecs) * V,
-                          s_vec[l0 + q]);
-              }
-            }
-          }
-#pragma unroll
-          for (int q = 0; q < LU; ++q) {
-            if (l0 + q < p.n_layers) {
-              if (c < tail_vecs) {
-                t[q].store(reinterpret_cast<T*>(s_k[l0 + q]) + kd + p.rotary_dim + c * V,
-                           s_vec[l0 + q]);
-              } else {
-                t[q].store(reinterpret_cast<T*>(s_v[l0 + q]) + vd + (c - tail_vecs) * V,
-                           s_vec[l0 + q]);
-              }
-            }
-          }
-        }
-      }
-    }
+    unit_direct<T, NEOX, V>(p, s_k, s_v, s_vec, g, tr);
   }
 }
 
 template <typename T, typename C, bool NEOX, int V>
 int launch(const RepositionParams& p, cudaStream_t stream) {
   auto kernel = reposition_kernel<T, C, NEOX, V>;
+  constexpr int smem = (V * sizeof(T) == 16) ? kStageBytes : 0;  // element path stages nothing
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return AKV_ERR_CUDA;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) !=
+          cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
   const long long units = p.count * (long long)p.num_heads * (p.half / V);
   const long long blocks = (units + kThreads - 1) / kThreads;
   const int grid = persistent_grid(per_sm, blocks);
-  kernel<<<grid, kThreads, 0, stream>>>(p);
+  kernel<<<grid, kThreads, smem, stream>>>(p);
   return launch_status();
 }
 
 template <typename T, typename C>
 int dispatch_style(const RepositionParams& p, bool neox, bool vec, cudaStream_t s) {
-  constexpr int VV = AKV_REPOSITION_VECTOR_BYTES / sizeof(T);
+  constexpr int VV = 16 / sizeof(T);
   if (vec) return neox ? launch<T, C, true, VV>(p, s) : launch<T, C, false, VV>(p, s);
   return neox ? launch<T, C, true, 1>(p, s) : launch<T, C, false, 1>(p, s);
 }
@@ -345,6 +432,21 @@ int dispatch_cache(const RepositionParams& p, int cache_dtype, bool neox, bool v
   return AKV_ERR_INVALID;
 }
 
+__global__ void divide_kernel(const float* n, const float* s, float* q, int64_t count,
+                              int method) {
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += step) {
+    const float d = s[i];
+    if (method == 0) {
+      q[i] = __fdiv_rn(n[i], d);
+    } else {
+      const bool d_ok = d >= kDivMin && d <= kDivMax;
+      float u1, u2;
+      div2_rn(n[i], n[i], d, __frcp_rn(d), d_ok, u1, u2);
+      q[i] = u1;
+    }
+  }
+}
 
 }  // namespace
 }  // namespace akv
@@ -392,10 +494,10 @@ extern "C" int akv_reposition_kv_layers(
   p.error_flag = error_flag;
 
   const int esize = kv_dtype == AKV_F32 ? 4 : 2;
-  const int V = AKV_REPOSITION_VECTOR_BYTES / esize;
-  // The vector path needs every vector to start on a vector boundary:
+  const int V = 16 / esize;
+  // The 16-byte path needs every vector to start on a 16-byte boundary:
   // shapes and strides are checked here, each layer's base address in the
-  // kernel (a misaligned layer falls back to element accesses).
+  // kernel (a misaligned layer sends the launch to element accesses).
   const bool vec = (p.half % V == 0) && (head_dim % V == 0) && (rotary_dim % V == 0) &&
                    (k_stride_slot % V == 0) && (k_stride_head % V == 0) &&
                    (v_stride_slot % V == 0) && (v_stride_head % V == 0);
@@ -408,28 +510,6 @@ extern "C" int akv_reposition_kv_layers(
   }
   return AKV_ERR_INVALID;
 }
-
-namespace akv {
-namespace {
-
-__global__ void divide_kernel(const float* n, const float* s, float* q, int64_t count,
-                              int method) {
-  const int64_t step = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += step) {
-    const float d = s[i];
-    if (method == 0) {
-      q[i] = __fdiv_rn(n[i], d);
-    } else {
-      const bool d_ok = d >= kDivMin && d <= kDivMax;
-      float u1, u2;
-      div2_rn(n[i], n[i], d, __frcp_rn(d), d_ok, u1, u2);
-      q[i] = u1;
-    }
-  }
-}
-
-}  // namespace
-}  // namespace akv
 
 extern "C" int akv_reposition_divide(const float* numerators, const float* denominators,
                                      float* quotients, int64_t count, int32_t method,
