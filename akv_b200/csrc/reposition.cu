@@ -25,6 +25,8 @@
 // the divisions correctly rounded (div2_rn below), and the source values
 // stored unchanged when old == new position.
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace akv {
@@ -62,6 +64,7 @@ struct RepositionParams {
   long long num_slots;     // 0 = unchecked
   long long max_position;  // 0 = unchecked
   int* error_flag;
+  float one;  // 1.0f, passed at run time (see the packed sums in rotate)
 };
 
 // V consecutive elements of T, moved with one 16-byte access when
@@ -164,6 +167,7 @@ __device__ __forceinline__ void div2_rn(float n1, float n2, float s, float y, bo
 template <int V> struct Trig {
   float oc[V], os[V], nc[V], ns[V], sc[V], rc[V];
   bool scale_ok;
+  float one;
 };
 
 template <typename C, int V>
@@ -171,6 +175,7 @@ __device__ __forceinline__ void load_trig(const RepositionParams& p, long long p
                                           int j, Trig<V>& tr) {
   const long long ro = po * p.cache_stride, rn = pn * p.cache_stride;
   tr.scale_ok = true;
+  tr.one = p.one;
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     tr.oc[i] = cache_at<C>(p.cache, ro + j + i);
@@ -183,11 +188,139 @@ __device__ __forceinline__ void load_trig(const RepositionParams& p, long long p
   }
 }
 
+// Packed fp32 pairs: Blackwell's f32x2 add / sub / mul / fma (PTX ISA 8.6,
+// sm_100a) round each lane exactly like the scalar .rn instruction, so two
+// rotary pairs go through the reference's operation sequence per
+// instruction with bit-identical results.
+using f2 = unsigned long long;
+__device__ __forceinline__ f2 pk(float lo, float hi) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk(f2 r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// Markstein division (see markstein_div) on two lanes at once; ns = -s.
+__device__ __forceinline__ f2 markstein_div2(f2 n, f2 ns, f2 y) {
+  f2 q = mul2(n, y);
+  f2 r = fma2(ns, q, n);
+  q = fma2(r, y, q);
+  r = fma2(ns, q, n);
+  return fma2(r, y, q);
+}
+
+__device__ __forceinline__ bool num_ok(float n) {
+  const float a = fabsf(n);
+  return a >= kNumMin && a <= kNumMax;
+}
+
+// Two adjacent elements of a chunk pair as fp32 (word w of the 2V elements
+// a ++ b) and back, rounding to nearest even on the way back.
+template <typename T, int V>
+__device__ __forceinline__ void get2(const Chunk<T, V>& a, const Chunk<T, V>& b, int w, float& lo,
+                                     float& hi) {
+  const Chunk<T, V>& c = w < V / 2 ? a : b;
+  const int i = 2 * (w < V / 2 ? w : w - V / 2);
+  lo = Elem<T>::to_f32(c.e[i]);
+  hi = Elem<T>::to_f32(c.e[i + 1]);
+}
+template <typename T, int V>
+__device__ __forceinline__ void put2(Chunk<T, V>& a, Chunk<T, V>& b, int w, float lo, float hi) {
+  Chunk<T, V>& c = w < V / 2 ? a : b;
+  const int i = 2 * (w < V / 2 ? w : w - V / 2);
+  if constexpr (sizeof(T) == 2) {
+    uint32_t packed;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value)
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
+    else
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
+    *reinterpret_cast<uint32_t*>(&c.e[i]) = packed;
+  } else {
+    c.e[i] = Elem<T>::from_f32(lo);
+    c.e[i + 1] = Elem<T>::from_f32(hi);
+  }
+}
+
 // Rotate one unit's two chunks (a: first V elements, b: second) in place.
 template <typename T, bool NEOX, int V>
 __device__ __forceinline__ void rotate(Chunk<T, V>& a, Chunk<T, V>& b, const Trig<V>& tr,
                                        bool same) {
   if (same) return;  // old == new position: the reference stores the source values
+  if constexpr (V % 2 == 0) {
+#pragma unroll
+    for (int k = 0; k < V / 2; ++k) {
+      // Pairs 2k and 2k + 1 of the unit.  NEOX: x1 are elements 2k, 2k+1 of
+      // a and x2 the same of b.  GPT-J: the pairs are elements (4k, 4k+1)
+      // and (4k+2, 4k+3) of a ++ b.
+      float x1l, x1h, x2l, x2h;
+      if constexpr (NEOX) {
+        get2(a, b, k, x1l, x1h);
+        get2(a, b, V / 2 + k, x2l, x2h);
+      } else {
+        get2(a, b, 2 * k, x1l, x2l);
+        get2(a, b, 2 * k + 1, x1h, x2h);
+      }
+      const int i = 2 * k;
+      const f2 x1 = pk(x1l, x1h), x2 = pk(x2l, x2h);
+      const f2 oc = pk(tr.oc[i], tr.oc[i + 1]), os = pk(tr.os[i], tr.os[i + 1]);
+      // Sums of two rounded products are formed as fma(p, +-1, q) with the
+      // 1 known only at run time: RN(p * 1 + q) is exactly RN(p + q), and
+      // the assembler cannot fold a single-use packed product into an FMA
+      // with the other product, which it otherwise does for f32x2 add/sub
+      // despite the .rn modifier (the fused result differs in the last bit).
+      const f2 one = pk(tr.one, tr.one), mone = pk(-tr.one, -tr.one);
+      const f2 n1 = fma2(mul2(x1, oc), one, mul2(x2, os));
+      const f2 n2 = fma2(mul2(x1, os), mone, mul2(x2, oc));
+      float n1l, n1h, n2l, n2h;
+      upk(n1, n1l, n1h);
+      upk(n2, n2l, n2h);
+      f2 u1, u2;
+      if (tr.scale_ok && num_ok(n1l) && num_ok(n1h) && num_ok(n2l) && num_ok(n2h)) {
+        const f2 ns = pk(-tr.sc[i], -tr.sc[i + 1]), y = pk(tr.rc[i], tr.rc[i + 1]);
+        u1 = markstein_div2(n1, ns, y);
+        u2 = markstein_div2(n2, ns, y);
+      } else {
+        u1 = pk(__fdiv_rn(n1l, tr.sc[i]), __fdiv_rn(n1h, tr.sc[i + 1]));
+        u2 = pk(__fdiv_rn(n2l, tr.sc[i]), __fdiv_rn(n2h, tr.sc[i + 1]));
+      }
+      const f2 nc = pk(tr.nc[i], tr.nc[i + 1]), nsn = pk(tr.ns[i], tr.ns[i + 1]);
+      const f2 y1 = fma2(mul2(u2, nsn), mone, mul2(u1, nc));
+      const f2 y2 = fma2(mul2(u2, nc), one, mul2(u1, nsn));
+      float y1l, y1h, y2l, y2h;
+      upk(y1, y1l, y1h);
+      upk(y2, y2l, y2h);
+      if constexpr (NEOX) {
+        put2(a, b, k, y1l, y1h);
+        put2(a, b, V / 2 + k, y2l, y2h);
+      } else {
+        put2(a, b, 2 * k, y1l, y2l);
+        put2(a, b, 2 * k + 1, y1h, y2h);
+      }
+    }
+    return;
+  }
   float x[2 * V];
 #pragma unroll
   for (int i = 0; i < V; ++i) {
@@ -492,6 +625,7 @@ extern "C" int akv_reposition_kv_layers(
   p.num_slots = num_slots;
   p.max_position = max_position;
   p.error_flag = error_flag;
+  p.one = 1.0f;
 
   const int esize = kv_dtype == AKV_F32 ? 4 : 2;
   const int V = 16 / esize;
