@@ -67,6 +67,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    p.add_argument("--layers", type=int, default=None,
+                   help="override the workload's layer count (a smaller cut for ncu captures)")
     return p.parse_args()
 
 
@@ -280,6 +282,7 @@ def run_reference(args):
     from akv_b200 import workloads
 
     layers, heads, dim, _ = WORKLOADS[args.workload]
+    layers = args.layers or layers
     prog = program_for(args.workload)
     rows, _ = workloads.slot_rows(np.random.default_rng(0), prog)
     cache_np = cos_sin(args.workload, dim, 131072).numpy()
@@ -328,6 +331,7 @@ def run_ours(args):
     from akv_b200.context_reposition import layer_pointer_table, reposition_kv_layers
 
     layers, heads_total, dim, _ = WORKLOADS[args.workload]
+    layers = args.layers or layers
     if heads_total % world:
         raise SystemExit(f"{heads_total} KV heads do not split over {world} GPUs")
     heads = heads_total // world
