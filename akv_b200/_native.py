@@ -38,6 +38,12 @@ SIGNATURES = {
         _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P,
         _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
     ],
+    "akv_drop_compact_static_max_requests": [],
+    "akv_drop_compact_static_max_tiles": [],
+    "akv_drop_compact_static": [
+        _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P,
+        _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+    ],
     "akv_context_decode_indices": [
         _P, _P, _I64, _P, _I32, _P, _I32, _P, _I32, _P, _I32, _P, _I32, _P, _I32, _I64, _I32,
         _P,
@@ -56,6 +62,8 @@ RESTYPES = {
     "akv_version": ctypes.c_char_p,
     "akv_drop_compact_tile_tokens": _I64,
     "akv_drop_compact_workspace_bytes": _I64,
+    "akv_drop_compact_static_max_requests": _I64,
+    "akv_drop_compact_static_max_tiles": _I64,
 }
 
 

@@ -288,6 +288,52 @@ class DropCompactor:
         )
 
 
+def launch_static(compactor, prepared, req_to_token, ring) -> DropResult:
+    """``DropCompactor.launch`` through ``akv_drop_compact_static``: same
+    kernels and outputs, but the scratch lives in the library's own device
+    array instead of ``compactor.workspace`` -- the entry point for callers
+    that cannot allocate device memory for a workspace.  At most
+    ``akv_drop_compact_static_max_requests()`` requests and
+    ``akv_drop_compact_static_max_tiles()`` tiles per call; calls whose
+    kernels overlap on the GPU share the array and must be serialised."""
+    c = compactor
+    if req_to_token.dtype != torch.int32 or req_to_token.device != c.device or \
+            req_to_token.ndim != 2 or req_to_token.stride(1) != 1:
+        raise ValueError("req_to_token must be a row-major int32 tensor on the device")
+    dev, nreq, n_tiles, total = (prepared["dev"], prepared["nreq"], prepared["n_tiles"],
+                                 prepared["total"])
+    off3 = c.offsets
+    status = _native.lib.akv_drop_compact_static(
+        nreq, _native.ptr(dev["token_offsets"]), _native.ptr(dev["tile_offsets"]), n_tiles,
+        _native.ptr(dev["range_offsets"]), _native.ptr(dev["ranges"]),
+        _native.ptr(dev["shared_prefix"]) if prepared["shared"] else None,
+        _native.ptr(req_to_token), _native.ptr(dev["row_ids"]), req_to_token.stride(0),
+        int(prepared["reposition"]), _native.ptr(ring.ring), ring.capacity,
+        _native.ptr(ring.state), _native.ptr(c.keep_mask), _native.ptr(c.positions),
+        _native.ptr(off3[0]), _native.ptr(c.raw_indices), _native.ptr(c.active_positions),
+        _native.ptr(c.next_position), _native.ptr(off3[1]), _native.ptr(c.transition_source),
+        _native.ptr(c.transition_destination), _native.ptr(c.transition_pairs),
+        _native.ptr(c.transition_raw), _native.ptr(off3[2]), _native.ptr(c.freed_slots),
+        _native.ptr(c.counters[:4]), _native.ptr(c.counters[4:]), _native.stream_of(c.device),
+    )
+    if status == _native.AKV_ERR_INVALID:
+        raise ValueError(
+            "drop_compact_static: the program exceeds the static scratch "
+            f"({int(_native.lib.akv_drop_compact_static_max_requests())} requests, "
+            f"{int(_native.lib.akv_drop_compact_static_max_tiles())} tiles of {TILE} tokens)")
+    _native.check(status, "drop_compact_static")
+    return DropResult(
+        keep_mask=c.keep_mask[:total], positions=c.positions[:total],
+        active_offsets=off3[0, : nreq + 1], raw_indices=c.raw_indices,
+        active_positions=c.active_positions, next_position=c.next_position[:nreq],
+        transition_offsets=off3[1, : nreq + 1], transition_source=c.transition_source,
+        transition_destination=c.transition_destination,
+        transition_pairs=c.transition_pairs, transition_raw=c.transition_raw,
+        freed_offsets=off3[2, : nreq + 1], freed_slots=c.freed_slots,
+        totals=c.counters[:4], status=c.counters[4:5],
+    )
+
+
 def drop_compact(token_counts, range_offsets, ranges, req_to_token, row_ids, ring,
                  shared_prefix=None, reposition=True) -> DropResult:
     """One-shot ``DropCompactor`` sized to this program."""

@@ -25,6 +25,8 @@
 // Tiles never straddle requests (the host gives per-request tile offsets),
 // so a request's base is the scan value at its first tile.
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace akv {
@@ -447,4 +449,94 @@ extern "C" int akv_drop_compact(
   drop_plan_kernel<<<1, kPlanThreads, 0, s>>>(a);
   if (n_tiles > 0) drop_scatter_kernel<<<n_tiles, kThreads, 0, s>>>(a);
   return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot hand this library a workspace: a serving runtime that
+// has reserved every byte of device memory for its KV pool up front, a
+// caller running inside a CUDA-graph capture or a custom allocator that
+// forbids cudaMalloc on its hot path, or a plain C/FFI caller with no device
+// allocator of its own.  For them the drop compaction keeps its scratch
+// (per-tile counters, their scan, per-request first-drop positions and the
+// ring plan) in one file-scope device array instead.  Every GPU that loads
+// this library holds the array until the process exits.
+//
+// Limits: at most kStaticMaxRequests requests and kStaticMaxTiles tiles
+// (kStaticMaxTiles * 2048 = 32M tokens) per call; larger calls are refused
+// with AKV_ERR_INVALID before anything is launched.  No part of the scratch
+// needs to start at zero -- each call writes every entry before reading it --
+// so nothing is cleared between calls.  All calls on a device share the one
+// array: two calls whose kernels overlap on the GPU (different streams
+// without ordering between them) race on it and must be serialised by the
+// caller.
+namespace akv {
+namespace {
+constexpr int kStaticMaxRequests = 4096;
+constexpr int kStaticMaxTiles = 16384;
+constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// The workspace layout of carve() at the maximum sizes (about 0.6 MB).
+constexpr size_t kStaticScratchBytes =
+    align256(sizeof(int) * 5 * kStaticMaxTiles) + align256(sizeof(int) * 4 * kStaticMaxTiles) +
+    align256(sizeof(int) * kStaticMaxRequests) + align256(sizeof(long long) * 4);
+}  // namespace
+}  // namespace akv
+
+static __device__ __align__(256) unsigned char g_drop_scratch[akv::kStaticScratchBytes];
+
+namespace akv {
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_drop_scratch on the current device, looked up once
+// per device (cudaGetSymbolAddress; the host-side name is only a stand-in).
+int static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AKV_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_drop_scratch) != cudaSuccess || p == nullptr)
+      return AKV_ERR_CUDA;
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return AKV_OK;
+}
+}  // namespace
+}  // namespace akv
+
+extern "C" int64_t akv_drop_compact_static_max_requests(void) {
+  return akv::kStaticMaxRequests;
+}
+extern "C" int64_t akv_drop_compact_static_max_tiles(void) { return akv::kStaticMaxTiles; }
+
+extern "C" int akv_drop_compact_static(
+    int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
+    int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
+    const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
+    int64_t row_stride, int32_t reposition, int32_t* ring, int64_t ring_capacity,
+    int64_t* ring_state, uint8_t* keep_mask, int32_t* positions, int32_t* active_offsets,
+    int32_t* raw_indices, int32_t* active_positions, int32_t* next_position,
+    int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
+    int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
+    int32_t* freed_slots, int32_t* totals, int32_t* status, void* stream) {
+  using namespace akv;
+  if (n_requests < 0 || n_tiles < 0 || n_requests > kStaticMaxRequests ||
+      n_tiles > kStaticMaxTiles)
+    return AKV_ERR_INVALID;
+  if (workspace_bytes(n_requests, n_tiles) > kStaticScratchBytes) return AKV_ERR_INVALID;
+  void* scratch = nullptr;
+  const int st = static_scratch(&scratch);
+  if (st != AKV_OK) return st;
+  return akv_drop_compact(n_requests, token_offsets, tile_offsets, n_tiles, range_offsets, ranges,
+                          shared_prefix, req_to_token, row_ids, row_stride, reposition, ring,
+                          ring_capacity, ring_state, keep_mask, positions, active_offsets,
+                          raw_indices, active_positions, next_position, transition_offsets,
+                          transition_source, transition_destination, transition_pairs,
+                          transition_raw, freed_offsets, freed_slots, totals, status, scratch,
+                          stream);
 }

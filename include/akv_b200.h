@@ -149,6 +149,38 @@ int akv_drop_compact(
     int32_t* freed_slots, int32_t* totals, int32_t* status, void* workspace, void* stream);
 
 /*
+ * akv_drop_compact without a workspace argument: the same computation and
+ * outputs, with its scratch in a file-scope device array of this library
+ * instead of caller memory.  No counterpart in the reference: it is for
+ * callers that cannot allocate device memory for a workspace -- a runtime
+ * whose memory is all reserved for its KV pool, a caller whose allocator
+ * forbids cudaMalloc on the serving path, or a C/FFI caller without a device
+ * allocator.  It allocates nothing and frees nothing.
+ *
+ * Limits: n_requests <= akv_drop_compact_static_max_requests() (4096) and
+ * n_tiles <= akv_drop_compact_static_max_tiles() (16384, i.e. 32M tokens);
+ * larger calls return AKV_ERR_INVALID before any launch.  The array (about
+ * 0.6 MB) is held by every GPU that loads the library until exit.  The first
+ * call on a device looks the array's device address up
+ * (cudaGetSymbolAddress) and caches it; make that first call before any
+ * stream capture.  All calls on a device share the array, which keeps the
+ * last call's contents (nothing in it needs to start at zero): calls whose
+ * kernels may overlap on the GPU race and must be ordered by the caller.
+ */
+int64_t akv_drop_compact_static_max_requests(void);
+int64_t akv_drop_compact_static_max_tiles(void);
+int akv_drop_compact_static(
+    int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
+    int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
+    const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
+    int64_t row_stride, int32_t reposition, int32_t* ring, int64_t ring_capacity,
+    int64_t* ring_state, uint8_t* keep_mask, int32_t* positions, int32_t* active_offsets,
+    int32_t* raw_indices, int32_t* active_positions, int32_t* next_position,
+    int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
+    int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
+    int32_t* freed_slots, int32_t* totals, int32_t* status, void* stream);
+
+/*
  * Decode read indices.  Replaces the Triton kernel context_decode_indices
  * (akv/system/sglang/kernels/ops/attention/context_page_table.py:34-76),
  * same contract: registry rows of six int64 cells {raw_ids*, positions*,
