@@ -33,6 +33,17 @@ namespace akv {
 namespace {
 
 constexpr int kGroup = 8;  // query heads per KV head (the MMA N)
+
+// 16-key stages, two of them: 64 KiB of shared memory for 8 KV heads of
+// 64 dims, so three CTAs share an SM (measured on c4: 0.74 ms per full
+// layer, against 0.77 with three stages / two CTAs and 0.95 with 32-key
+// stages / one CTA).
+#ifndef AKV_ATTENTION_TILE_BYTES
+#define AKV_ATTENTION_TILE_BYTES 16384
+#endif
+#ifndef AKV_ATTENTION_STAGES
+#define AKV_ATTENTION_STAGES 2
+#endif
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -131,33 +142,47 @@ decode_attention_kernel(const AttnParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
 
-  // Gather one tile of K and V rows into stage `s`.
-  auto load_tile = [&](int tile, int s) {
+  // Each thread gathers kCpt 16-byte chunks of one key of every tile, so it
+  // needs one index per tile, and that index is loaded a tile ahead: the
+  // copies never wait on their own address.
+  constexpr int kTpk = C::kThreads / TK;        // threads per key
+  constexpr int kCpt = C::kChunks / kTpk;       // chunks per thread (K, and as many of V)
+  static_assert(C::kThreads % TK == 0 && C::kChunks % kTpk == 0, "tile split");
+  const int my_key = tid / kTpk, my_q = tid - my_key * kTpk;
+  // Slot of this thread's key in `tile`, or -1 past the range end.
+  auto fetch_slot = [&](int tile) -> long long {
+    const int kk = kv_begin + tile * TK + my_key;
+    if (tile >= n_tiles || kk >= kv_end) return -1;
+    long long slot = __ldg(p.kv_indices + kk);
+    if (slot < 0 || slot >= p.num_slots) {  // never touch memory outside the pools
+      if (p.error_flag) *p.error_flag = 1;
+      slot = 0;
+    }
+    return slot;
+  };
+  auto issue_tile = [&](int s, long long slot) {
     const uint32_t kbase = smem_u32(smem + s * C::kStageBytes);
     const uint32_t vbase = kbase + C::kTileBytes;
-    for (int i = tid; i < TK * C::kChunks; i += C::kThreads) {
-      const int j = i / C::kChunks;  // key within the tile
-      const int c = i - j * C::kChunks;
+    const bool valid = slot >= 0;
+    const long long sl = valid ? slot : 0;
+    const int bytes = valid ? 16 : 0;  // zero-fill past the range end
+#pragma unroll
+    for (int i = 0; i < kCpt; ++i) {
+      const int c = my_q + kTpk * i;
       const int head = c / C::kCph, cc = c - head * C::kCph;
-      const int kk = kv_begin + tile * TK + j;
-      const bool valid = kk < kv_end;
-      long long slot = valid ? (long long)__ldg(p.kv_indices + kk) : 0;
-      if (slot < 0 || slot >= p.num_slots) {  // never touch memory outside the pools
-        if (valid && p.error_flag) *p.error_flag = 1;
-        slot = 0;
-      }
-      const int phys = head * C::kCph + (cc ^ (j & 7));
-      const uint32_t off = j * C::kRowBytes + phys * 16;
-      cp_async16(kbase + off, p.k + slot * p.k_ss + head * p.k_sh + cc * 8, valid ? 16 : 0);
-      cp_async16(vbase + off, p.v + slot * p.v_ss + head * p.v_sh + cc * 8, valid ? 16 : 0);
+      const int phys = head * C::kCph + (cc ^ (my_key & 7));
+      const uint32_t off = my_key * C::kRowBytes + phys * 16;
+      cp_async16(kbase + off, p.k + sl * p.k_ss + head * p.k_sh + cc * 8, bytes);
+      cp_async16(vbase + off, p.v + sl * p.v_ss + head * p.v_sh + cc * 8, bytes);
     }
   };
 
 #pragma unroll
   for (int s = 0; s < NSTAGE - 1; ++s) {
-    if (s < n_tiles) load_tile(s, s);
+    if (s < n_tiles) issue_tile(s, fetch_slot(s));
     cp_async_commit();
   }
+  long long next_slot = fetch_slot(NSTAGE - 1);
 
   // Q^T fragments of this warp's 8 query heads (B operand, k = dims).
   const int qh0 = warp * kGroup;
@@ -181,7 +206,10 @@ decode_attention_kernel(const AttnParams p) {
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     const int nt = tile + NSTAGE - 1;
-    if (nt < n_tiles) load_tile(nt, nt % NSTAGE);
+    if (nt < n_tiles) {
+      issue_tile(nt % NSTAGE, next_slot);
+      next_slot = fetch_slot(nt + 1);
+    }
     cp_async_commit();
     cp_async_wait<NSTAGE - 1>();
     __syncthreads();
@@ -344,8 +372,11 @@ __global__ void decode_combine_kernel(const AttnParams p, const int2* merge, int
 template <int D, int HKV>
 int launch_attention(const AttnParams& p, int n_items, const int2* merge, int batch,
                      cudaStream_t s) {
-  constexpr int TK = (HKV * D <= 512) ? 32 : 16;
-  constexpr int NSTAGE = (HKV * D <= 256) ? 4 : 3;
+  // Keys per stage: as many as fit AKV_ATTENTION_TILE_BYTES of K rows, 16
+  // or 32; stages: AKV_ATTENTION_STAGES, one more when a stage is small.
+  constexpr int kRow = HKV * D * 2;
+  constexpr int TK = (AKV_ATTENTION_TILE_BYTES / kRow >= 32) ? 32 : 16;
+  constexpr int NSTAGE = AKV_ATTENTION_STAGES + ((HKV * D <= 256) ? 1 : 0);
   using C = Cfg<D, HKV, TK, NSTAGE>;
   auto kernel = decode_attention_kernel<D, HKV, TK, NSTAGE>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=

@@ -57,6 +57,7 @@ WORKLOADS = {
     "c1": (1, 8, 64, "rope10000"),
     "c2": (36, 8, 64, "yarn"),
     "c5": (80, 8, 128, "rope500000"),
+    "c4": (36, 8, 64, None),  # decode attention only (see bench_attention)
 }
 
 
@@ -434,6 +435,12 @@ def run_ours(args):
     achieved = rep_bytes / (rep_mean / 1e3) / 1e9
     traffic = ncu_traffic(args.workload) if world == 1 else None
 
+    # Second metric: paged GQA decode attention over the compacted cache (c4).
+    del k_pools, v_pools
+    torch.cuda.empty_cache()
+    attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
+                                max(5, min(args.steps // 20, 20)))
+
     cpu = None
     if rank == 0 and world == 1:
         cache_np = cache.cpu().numpy()
@@ -474,6 +481,7 @@ def run_ours(args):
                              "reposition": round(rep_mean, 4)},
             "gpu_launches": 4 * args.steps,
             "cpu_baseline": cpu,
+            "decode_attention": attention,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
@@ -484,8 +492,108 @@ def run_ours(args):
     return 0
 
 
+def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36):
+    """c4: batch 128, 64 query / 8 KV heads (split 8/N per rank), head_dim 64,
+    bf16, lognormal KV lengths (median 8192, sigma 1.0, max 65536), 36 layers
+    alternating sliding window 128 and full attention, per-head sinks.  One
+    step = one decode token for the whole batch = 36 layer launches (18
+    full over all keys, 18 over the 129 visible keys of each request), each
+    layer with its own K/V pool.  tokens/s = batch / step time."""
+    from akv_b200 import workloads
+    from akv_b200.context_attention import DecodeAttention
+
+    bs, hq_total, hkv_total, d, window = 128, 64, 8, 64, 128
+    hkv = hkv_total // world
+    hq = hq_total // world
+    lengths = workloads.c4_lengths(seed=seed, batch=bs)
+    rng = np.random.default_rng(seed)
+    total = int(lengths.sum())
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    full_indptr = np.concatenate(([0], np.cumsum(lengths)))
+    swa_len = np.minimum(lengths, window + 1)
+    swa_indptr = np.concatenate(([0], np.cumsum(swa_len)))
+    # Keys of a request sit at random slots of its layer's pool.
+    full_idx = torch.from_numpy(rng.permutation(total).astype(np.int32)).to(dev)
+    swa_idx = torch.from_numpy(rng.permutation(int(swa_len.sum())).astype(np.int32)).to(dev)
+    pools = []
+    for layer in range(layers):
+        slots = total if layer % 2 else int(swa_len.sum())
+        pools.append((torch.randn(slots, hkv, d, device=dev, generator=g, dtype=torch.bfloat16),
+                      torch.randn(slots, hkv, d, device=dev, generator=g, dtype=torch.bfloat16)))
+    q = torch.randn(bs, hq, d, device=dev, generator=g, dtype=torch.bfloat16)
+    sinks = torch.randn(hq, device=dev, generator=g)
+    full = DecodeAttention(hq, hkv, d, bs, dev).plan(full_indptr)
+    swa = DecodeAttention(hq, hkv, d, bs, dev).plan(swa_indptr)
+    out = torch.empty(bs, hq, d, device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+
+    def step(i=None):
+        for layer in range(layers):
+            if i is not None and layer == 1:
+                ev[i][0].record(stream)
+            kp, vp = pools[layer]
+            if layer % 2:
+                full.run(q, kp, vp, full_idx, sinks=sinks, out=out)
+            else:
+                swa.run(q, kp, vp, swa_idx, sinks=sinks, out=out)
+            if i is not None and layer == 1:
+                ev[i][1].record(stream)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(steps):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = dist_max(t0.elapsed_time(t1) / steps, world)
+    full_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    full_bytes = total * hkv * d * 2 * 2
+    swa_bytes = int(swa_len.sum()) * hkv * d * 2 * 2
+    step_bytes = (layers // 2) * (full_bytes + swa_bytes) * world
+    peak, peak_kind = measured_peak()
+    achieved = full_bytes / (full_ms / 1e3) / 1e9
+    del pools
+    torch.cuda.empty_cache()
+    return {
+        "metric": "paged GQA decode attn tokens/s", "value": round(bs / (ms / 1e3), 1),
+        "unit": "tokens/s", "ms_per_step": round(ms, 4), "n_gpus": world,
+        "gb_per_s": round(step_bytes / (ms / 1e3) / 1e9, 1),
+        "config": {"workload": "c4", "batch": bs, "q_heads": hq_total, "kv_heads": hkv_total,
+                   "head_dim": d, "layers": layers, "sliding_window": window,
+                   "kv_tokens": total, "lengths": "lognormal median 8192 sigma 1.0",
+                   "sinks": True, "work_items_full": full.n_items, "chunk": full.chunk},
+        "roofline": {"bound": "hbm", "kernel": "decode_attention_kernel (full layer)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": full_bytes,
+                     "ms_per_launch": round(full_ms, 4)},
+        "gpu_launches_per_step": layers + (layers // 2 if full.split else 0),
+    }
+
+
 def main():
     args = parse_args()
+    if args.workload == "c4" and args.impl == "ours":
+        # Decode attention alone (for profiling cuts: --layers 2).
+        world, rank, local = dist_setup()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = bench_attention(dev, world, rank, max(3, args.warmup), max(3, args.steps // 20),
+                              layers=args.layers or 36)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return 0
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
