@@ -14,7 +14,7 @@
 // there on every kept token moves -- context_plan.py:405-440).
 //
 // Three launches, no inter-block waiting:
-//   1. count   -- per 2048-token tile: keep mask from a difference array of
+//   1. count   -- per 512-token tile: keep mask from a difference array of
 //                 the request's drop ranges (shared-memory atomics + block
 //                 scan), four per-tile counters {kept, moved, cow, freed};
 //   2. plan    -- one block: exclusive scan of the tile counters, per-request
@@ -32,14 +32,14 @@
 namespace akv {
 namespace {
 
-constexpr int kTile = 2048;
-constexpr int kThreads = 256;
-constexpr int kPerThread = kTile / kThreads;  // 8 contiguous tokens per thread
+constexpr int kTile = 512;
+constexpr int kThreads = 128;
+constexpr int kPerThread = kTile / kThreads;  // 4 contiguous tokens per thread
 constexpr int kPlanThreads = 1024;
 constexpr int kFields = 4;  // kept, moved, cow, freed
 
 // Field packing for the block scan: 16 bits per counter (a tile holds at
-// most 2048 tokens, so no field overflows into the next).
+// most 512 tokens, so no field overflows into the next).
 __device__ __forceinline__ unsigned long long pack4(int a, int b, int c, int d) {
   return (unsigned long long)a | ((unsigned long long)b << 16) | ((unsigned long long)c << 32) |
          ((unsigned long long)d << 48);
@@ -346,6 +346,12 @@ __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a
   const int req_kept_base = a.active_offsets[c.r];
   int32_t* row = a.req_to_token + a.row_ids[c.r] * a.row_stride;
   const long long head = a.ws.plan[0], tail = a.ws.plan[1];
+  // All of this thread's slot loads go out before any store: the stores
+  // below may alias the row (copy-on-write rewrites it) so the compiler
+  // would otherwise serialise load, store, load, ...
+  int slots[kPerThread];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) slots[k] = base + k < c.n ? row[c.t0 + base + k] : 0;
 #pragma unroll
   for (int k = 0; k < kPerThread; ++k) {
     const int i = base + k;
@@ -359,7 +365,7 @@ __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a
       a.active_positions[gk] = pos;
       ++gk;
       if (a.reposition && t > first_drop) {
-        const int slot = row[t];
+        const int slot = slots[k];
         int dst = slot;
         if (t < c.P) {
           dst = a.ring[(head + gc) % a.ring_capacity];
@@ -376,7 +382,7 @@ __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a
     } else {
       a.positions[c.flat0 + i] = t;
       if (t >= c.P) {
-        const int slot = row[t];
+        const int slot = slots[k];
         a.freed_slots[gf] = slot;
         a.ring[(tail + gf) % a.ring_capacity] = slot;
         ++gf;
@@ -464,7 +470,7 @@ extern "C" int akv_drop_compact(
 // this library holds the array until the process exits.
 //
 // Limits: at most kStaticMaxRequests requests and kStaticMaxTiles tiles
-// (kStaticMaxTiles * 2048 = 32M tokens) per call; larger calls are refused
+// (kStaticMaxTiles * 512 = 32M tokens) per call; larger calls are refused
 // with AKV_ERR_INVALID before anything is launched.  No part of the scratch
 // needs to start at zero -- each call writes every entry before reading it --
 // so nothing is cleared between calls.  All calls on a device share the one
@@ -474,9 +480,9 @@ extern "C" int akv_drop_compact(
 namespace akv {
 namespace {
 constexpr int kStaticMaxRequests = 4096;
-constexpr int kStaticMaxTiles = 16384;
+constexpr int kStaticMaxTiles = 65536;
 constexpr size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-// The workspace layout of carve() at the maximum sizes (about 0.6 MB).
+// The workspace layout of carve() at the maximum sizes (about 2.4 MB).
 constexpr size_t kStaticScratchBytes =
     align256(sizeof(int) * 5 * kStaticMaxTiles) + align256(sizeof(int) * 4 * kStaticMaxTiles) +
     align256(sizeof(int) * kStaticMaxRequests) + align256(sizeof(long long) * 4);

@@ -158,9 +158,9 @@ int akv_drop_compact(
  * allocator.  It allocates nothing and frees nothing.
  *
  * Limits: n_requests <= akv_drop_compact_static_max_requests() (4096) and
- * n_tiles <= akv_drop_compact_static_max_tiles() (16384, i.e. 32M tokens);
+ * n_tiles <= akv_drop_compact_static_max_tiles() (65536, i.e. 32M tokens);
  * larger calls return AKV_ERR_INVALID before any launch.  The array (about
- * 0.6 MB) is held by every GPU that loads the library until exit.  The first
+ * 2.4 MB) is held by every GPU that loads the library until exit.  The first
  * call on a device looks the array's device address up
  * (cudaGetSymbolAddress) and caches it; make that first call before any
  * stream capture.  All calls on a device share the array, which keeps the

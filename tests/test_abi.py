@@ -45,7 +45,7 @@ def test_host_only_entry_points():
     from akv_b200 import _native
 
     assert _native.lib.akv_version().startswith(b"akv_b200")
-    assert _native.lib.akv_drop_compact_tile_tokens() == 2048
+    assert _native.lib.akv_drop_compact_tile_tokens() == 512
     assert _native.lib.akv_drop_compact_workspace_bytes(64, 700) > 0
 
 

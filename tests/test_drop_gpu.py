@@ -128,7 +128,7 @@ def test_drop_edge_cases_match_oracle():
     from akv_b200.workloads import DropProgram
 
     # request 0: no ranges; 1: empty request; 2: a suffix drop (Reposition
-    # ignored); 3: spans crossing 2048-token tile boundaries; 4: one token
+    # ignored); 3: spans crossing 512-token tile boundaries; 4: one token
     # kept at the end; 5: a range covering the first token only.
     counts = np.array([300, 0, 40, 7000, 3000, 2])
     per = [[], [], [30, 40], [100, 2047, 2049, 4097, 6000, 6999], [0, 2999], [0, 1]]

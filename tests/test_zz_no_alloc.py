@@ -84,7 +84,7 @@ def test_static_entry_point_refuses_calls_beyond_its_limits():
     lib = _native.lib
     max_req = int(lib.akv_drop_compact_static_max_requests())
     max_tiles = int(lib.akv_drop_compact_static_max_tiles())
-    assert (max_req, max_tiles) == (4096, 16384)
+    assert (max_req, max_tiles) == (4096, 65536)
     nulls = [None] * 19
     for n_requests, n_tiles in ((max_req + 1, 1), (1, max_tiles + 1)):
         status = lib.akv_drop_compact_static(
