@@ -27,6 +27,7 @@ import torch
 from . import _native
 
 NUM_SMS = 148
+MAX_SPLITS = 512  # key ranges per request the combine kernel merges
 
 
 class DecodeAttention:
@@ -74,7 +75,7 @@ class DecodeAttention:
             if n <= chunk:
                 items.append((b, start, start + int(n), -1))
                 continue
-            k = -(-int(n) // chunk)
+            k = min(-(-int(n) // chunk), MAX_SPLITS)
             cuts = start + (np.arange(k + 1) * int(n)) // k
             merge[b] = (partials, k)
             for i in range(k):

@@ -340,33 +340,59 @@ decode_attention_kernel(const AttnParams p) {
   }
 }
 
-// Combine the partial results of split requests: one block per request,
-// one thread per (head, dim).
+// Combine the partial results of split requests.  Block (request, head
+// group): one warp per query head.  The warp first turns the splits' maxima
+// into per-split weights 2^(m_i - M) (kept in shared memory) and the
+// denominator, then each lane sums its D/32 output dims over the splits
+// with loads that are contiguous across the warp.
+constexpr int kCombineHeads = 8;     // warps (query heads) per block
+constexpr int kCombineMaxSplits = 512;
+
 template <int D>
-__global__ void decode_combine_kernel(const AttnParams p, const int2* merge, int batch) {
+__global__ void __launch_bounds__(32 * kCombineHeads)
+decode_combine_kernel(const AttnParams p, const int2* merge, int batch) {
+  __shared__ float weight[kCombineHeads][kCombineMaxSplits];
   const int b = blockIdx.x;
   const int2 mg = merge[b];  // {first partial, count}; count 0 = written directly
   if (mg.y == 0) return;
-  for (int i = threadIdx.x; i < p.num_q_heads * D; i += blockDim.x) {
-    const int h = i / D, d = i - h * D;
-    float mx = -INFINITY;
-    for (int s = 0; s < mg.y; ++s)
-      mx = fmaxf(mx, p.part_ml[((long long)(mg.x + s) * p.num_q_heads + h) * 2]);
-    const float base = mx == -INFINITY ? 0.f : mx;
-    float den = 0.f, num = 0.f;
-    for (int s = 0; s < mg.y; ++s) {
-      const long long q = (long long)(mg.x + s) * p.num_q_heads + h;
-      const float f = fast_exp2(p.part_ml[2 * q] - base);
-      den += p.part_ml[2 * q + 1] * f;
-      num += p.part_acc[q * D + d] * f;
-    }
-    if (p.sinks) den += fast_exp2(p.sinks[h] * kLog2e - base);
-    p.out[(long long)b * p.o_sb + (long long)h * p.o_sh + d] =
-        __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
-    if (p.lse && d == 0)
-      p.lse[(long long)b * p.num_q_heads + h] =
-          den > 0.f ? (base + log2f(den)) * kLn2 : -INFINITY;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int h = blockIdx.y * kCombineHeads + w;
+  if (h >= p.num_q_heads) return;
+  const int n = mg.y;
+  float mx = -INFINITY;
+  for (int s = lane; s < n; s += 32)
+    mx = fmaxf(mx, p.part_ml[((long long)(mg.x + s) * p.num_q_heads + h) * 2]);
+#pragma unroll
+  for (int x = 16; x > 0; x >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+  const float base = mx == -INFINITY ? 0.f : mx;
+  float den = 0.f;
+  for (int s = lane; s < n; s += 32) {
+    const long long q = (long long)(mg.x + s) * p.num_q_heads + h;
+    const float f = fast_exp2(p.part_ml[2 * q] - base);
+    weight[w][s] = f;
+    den += p.part_ml[2 * q + 1] * f;
   }
+#pragma unroll
+  for (int x = 16; x > 0; x >>= 1) den += __shfl_xor_sync(0xffffffffu, den, x);
+  __syncwarp();
+  if (p.sinks) den += fast_exp2(p.sinks[h] * kLog2e - base);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  constexpr int kPer = D / 32;
+  float num[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) num[k] = 0.f;
+  const float* acc = p.part_acc + ((long long)mg.x * p.num_q_heads + h) * D + lane;
+  const long long split_stride = (long long)p.num_q_heads * D;
+  for (int s = 0; s < n; ++s) {
+    const float f = weight[w][s];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) num[k] += acc[s * split_stride + 32 * k] * f;
+  }
+  __nv_bfloat16* o = p.out + (long long)b * p.o_sb + (long long)h * p.o_sh + lane;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) o[32 * k] = __float2bfloat16_rn(num[k] * inv);
+  if (p.lse && lane == 0)
+    p.lse[(long long)b * p.num_q_heads + h] = den > 0.f ? (base + log2f(den)) * kLn2 : -INFINITY;
 }
 
 template <int D, int HKV>
@@ -383,7 +409,10 @@ int launch_attention(const AttnParams& p, int n_items, const int2* merge, int ba
       cudaSuccess)
     return AKV_ERR_CUDA;
   if (n_items > 0) kernel<<<n_items, C::kThreads, C::kSmem, s>>>(p);
-  if (merge != nullptr && batch > 0) decode_combine_kernel<D><<<batch, 256, 0, s>>>(p, merge, batch);
+  if (merge != nullptr && batch > 0) {
+    const dim3 grid(batch, (p.num_q_heads + kCombineHeads - 1) / kCombineHeads);
+    decode_combine_kernel<D><<<grid, 32 * kCombineHeads, 0, s>>>(p, merge, batch);
+  }
   return launch_status();
 }
 
