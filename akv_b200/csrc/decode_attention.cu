@@ -35,9 +35,11 @@ namespace {
 constexpr int kGroup = 8;  // query heads per KV head (the MMA N)
 
 // 16-key stages, two of them: 64 KiB of shared memory for 8 KV heads of
-// 64 dims, so three CTAs share an SM (measured on c4: 0.74 ms per full
-// layer, against 0.77 with three stages / two CTAs and 0.95 with 32-key
-// stages / one CTA).
+// 64 dims, so three CTAs share an SM (measured on c4: 0.66 ms per full
+// layer with its combine, 5.3 TB/s; 2 CTAs x 3 stages and 1 CTA x 32-key
+// stages were slower, and so were per-warp rings -- a key's 1 KiB row then
+// reaches DRAM as eight separate 128-byte requests -- and a warp-specialised
+// variant with one cp.async.bulk per row and an mbarrier ring, 0.67 ms).
 #ifndef AKV_ATTENTION_TILE_BYTES
 #define AKV_ATTENTION_TILE_BYTES 16384
 #endif
