@@ -24,6 +24,29 @@ _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _I64 = ctypes.c_int64
 
+LAYOUT_CAPACITY, LAYOUT_ERROR, LAYOUT_TOO_MANY = 1, 2, 4
+
+
+class LayoutBatch(ctypes.Structure):
+    """struct akv_layout_batch of include/akv_b200.h, field for field."""
+
+    _fields_ = [
+        ("n_requests", _I32), ("n_tiles", _I32), ("n_tokens", _I64), ("n_repositions", _I64),
+        ("n_count_cells", _I64), ("token_offsets", _P), ("token_ids", _P),
+        ("token_ids_is64", _I32), ("tile_offsets", _P), ("count_offsets", _P),
+        ("drop_event_offsets", _P), ("drop_insert_offsets", _P), ("drop_range_offsets", _P),
+        ("drop_ranges", _P), ("reposition_offsets", _P), ("reposition_raw_boundaries", _P),
+        ("positions", _P), ("keep_mask", _P), ("materialized_stage", _P),
+        ("birth_positions", _P), ("birth_stages", _P), ("token_to_key", _P), ("records", _P),
+        ("virtual_mask", _P), ("key_to_token", _P), ("transition_offsets", _P),
+        ("transition_request_offsets", _P), ("transition_raw_tokens", _P),
+        ("transition_old_positions", _P), ("transition_new_positions", _P),
+        ("transition_capacity", _I64), ("effective_reposition_stages", _P),
+        ("effective_repositions", _P), ("ignored_repositions", _P), ("drop_event_to_key", _P),
+        ("status", _P), ("active_offsets", _P), ("raw_indices", _P), ("active_positions", _P),
+        ("totals", _P), ("workspace", _P),
+    ]
+
 # name -> argument types, in the order of include/akv_b200.h
 SIGNATURES = {
     "akv_version": [],
@@ -53,6 +76,10 @@ SIGNATURES = {
         _P, _P, _I64, _P, _P, _I64, _P, _I64, _I32, _P, _P, _P, _P, _P,
     ],
     "akv_write_row_slots": [_P, _P, _I32, _P, _I32, _P, _I32, _I64, _P],
+    "akv_compile_layouts_max_repositions": [],
+    "akv_compile_layouts_workspace_bytes": [_I32, _I64, _I64, _I64],
+    "akv_compile_layouts_batch_bytes": [],
+    "akv_compile_layouts": [ctypes.POINTER(LayoutBatch), _P],
     "akv_decode_attention": [
         _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, ctypes.c_float, _I32,
         _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P, _I64, _I64, _P, _P, _P,
@@ -64,6 +91,9 @@ RESTYPES = {
     "akv_drop_compact_workspace_bytes": _I64,
     "akv_drop_compact_static_max_requests": _I64,
     "akv_drop_compact_static_max_tiles": _I64,
+    "akv_compile_layouts_max_repositions": _I64,
+    "akv_compile_layouts_workspace_bytes": _I64,
+    "akv_compile_layouts_batch_bytes": _I64,
 }
 
 

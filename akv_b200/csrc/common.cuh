@@ -100,4 +100,69 @@ __device__ __forceinline__ void st16_stream(T* p, const Vec16<T>& v) {
                : "memory");
 }
 
+// Block-wide exclusive scan built from warp shuffles.  Returns the
+// exclusive prefix of `v` and writes the block total to *total.  Every
+// thread of the block must call it (it synchronises the block).
+template <typename U>
+__device__ U block_exclusive_scan(U v, U* total) {
+  __shared__ U warp_sums[32];
+  __shared__ U block_total;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  U inc = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    U o = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += o;
+  }
+  if (lane == 31) warp_sums[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    U w = lane < nwarps ? warp_sums[lane] : U(0);
+    U winc = w;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      U o = __shfl_up_sync(0xffffffffu, winc, d);
+      if (lane >= d) winc += o;
+    }
+    if (lane < nwarps) warp_sums[lane] = winc - w;  // exclusive base of each warp
+    if (lane == 31) block_total = winc;
+  }
+  __syncthreads();
+  const U base = warp_sums[warp];
+  *total = block_total;
+  __syncthreads();  // the next call may overwrite warp_sums
+  return base + inc - v;
+}
+
+// Inclusive scan across one warp.
+template <typename U>
+__device__ __forceinline__ U warp_inclusive_scan(U v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    U o = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += o;
+  }
+  return v;
+}
+
+template <typename U>
+__device__ __forceinline__ U warp_sum(U v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+  return v;
+}
+
+// Number of entries of the sorted vector a[0, n) that are < x.
+__device__ __forceinline__ int count_below(const int32_t* a, int n, long long x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if ((long long)__ldg(a + mid) < x) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
 }  // namespace akv

@@ -48,40 +48,6 @@ __device__ __forceinline__ int field(unsigned long long v, int f) {
   return (int)((v >> (16 * f)) & 0xffffull);
 }
 
-// Block-wide exclusive scan built from warp shuffles.  Returns the
-// exclusive prefix of `v` and writes the block total to *total.
-template <typename U>
-__device__ U block_exclusive_scan(U v, U* total) {
-  __shared__ U warp_sums[32];
-  __shared__ U block_total;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nwarps = (blockDim.x + 31) >> 5;
-  U inc = v;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    U o = __shfl_up_sync(0xffffffffu, inc, d);
-    if (lane >= d) inc += o;
-  }
-  if (lane == 31) warp_sums[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    U w = lane < nwarps ? warp_sums[lane] : U(0);
-    U winc = w;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      U o = __shfl_up_sync(0xffffffffu, winc, d);
-      if (lane >= d) winc += o;
-    }
-    if (lane < nwarps) warp_sums[lane] = winc - w;  // exclusive base of each warp
-    if (lane == 31) block_total = winc;
-  }
-  __syncthreads();
-  const U base = warp_sums[warp];
-  *total = block_total;
-  __syncthreads();  // the next call may overwrite warp_sums
-  return base + inc - v;
-}
-
 struct Workspace {
   int* tile_sums;   // [n_tiles][5]: four counters + bad-range flag
   int* tile_base;   // [n_tiles][4]: exclusive scan of the counters

@@ -165,3 +165,41 @@ def c4_lengths(seed=0, batch=128, median=8192, sigma=1.0, max_len=65536):
     rng = np.random.default_rng(seed)
     lengths = np.clip(np.round(rng.lognormal(np.log(median), sigma, size=batch)), 1, max_len)
     return lengths.astype(np.int64)
+
+
+def event_program(rng, tokens, events, repositions, max_ranges=4, span=None):
+    """A seeded multi-event program in the reference's input format
+    (compile_context_layout, ir.py:113-121): ``events`` Drop events at
+    distinct insertion offsets in [1, tokens], each with 1..max_ranges
+    ordered, disjoint, already materialized ranges (later events may cover
+    tokens an earlier one dropped), and ``repositions`` Repositions at
+    distinct raw boundaries.  ``span`` caps a range's length (None: up to
+    the insertion offset).  Returns (token_ids int64, drop_insert_offsets,
+    drop_range_offsets, drop_ranges, reposition_raw_boundaries), int32
+    except the ids."""
+    tokens = int(tokens)
+    events = min(int(events), tokens)
+    inserts = (np.sort(rng.choice(np.arange(1, tokens + 1), size=events, replace=False))
+               if events else np.zeros(0, np.int64))
+    offsets, ranges = [0], []
+    for ins in inserts:
+        k = int(min(rng.integers(1, max_ranges + 1), (ins + 1) // 2))
+        if span is None:
+            points = np.sort(rng.choice(np.arange(0, ins + 1), size=2 * k, replace=False))
+        else:
+            starts = np.sort(rng.choice(np.arange(0, ins), size=k, replace=False))
+            ends = np.minimum(starts + rng.integers(1, span + 1, size=k), ins)
+            ends = np.minimum(ends, np.append(starts[1:] - 1, ins))  # keep previous_end < start
+            keep = ends > starts
+            points = np.stack((starts[keep], ends[keep]), 1).reshape(-1)
+            k = len(points) // 2
+            if k == 0:
+                points, k = np.array([ins - 1, ins]), 1
+        ranges += [int(x) for x in points]
+        offsets.append(offsets[-1] + k)
+    reps = min(int(repositions), tokens)
+    bounds = (np.sort(rng.choice(np.arange(0, tokens), size=reps, replace=False))
+              if reps else np.zeros(0, np.int64))
+    ids = rng.integers(0, 200000, size=tokens).astype(np.int64)
+    return (ids, inserts.astype(np.int32), np.asarray(offsets, np.int32),
+            np.asarray(ranges, np.int32), bounds.astype(np.int32))

@@ -181,6 +181,116 @@ int akv_drop_compact_static(
     int32_t* freed_slots, int32_t* totals, int32_t* status, void* stream);
 
 /*
+ * General event compiler for a batch of request programs.  Replaces
+ * compile_radix_reposition_layout and count_radix_reposition_transitions
+ * (akv/system/sglang/kernels/ops/attention/context_plan.py:80-532) as called
+ * by compile_context_layout (srt/context_system/ir.py:113-274): any number
+ * of Drop events and Reposition events per request, in the reference's
+ * order (a Drop runs before a Reposition at the same insertion offset), with
+ * every output tensor of the reference's ContextLayout, plus the decode view
+ * of ContextDecodeLayout.from_layout (srt/context_system/occurrence.py:47-66).
+ *
+ * Batch layout (all device pointers, request-local values as in the
+ * reference): request b owns tokens [token_offsets[b], token_offsets[b+1])
+ * of the flat per-token arrays; its Drop events are
+ * [drop_event_offsets[b], drop_event_offsets[b+1]) of drop_insert_offsets,
+ * event e owning the range pairs [drop_range_offsets[e], drop_range_offsets[e+1])
+ * of drop_ranges (drop_range_offsets is one increasing vector over the whole
+ * batch); its Reposition events are [reposition_offsets[b],
+ * reposition_offsets[b+1]) of reposition_raw_boundaries (insertion offset =
+ * boundary + 1).  The metadata must satisfy the reference's checks
+ * (context_plan.py:309-325 and the range check at :367-371); the host
+ * validates it before the call, the device does not re-check it.
+ *
+ * Outputs, per request at the same offsets as the inputs:
+ *   per token: positions, keep_mask, materialized_stage, birth_positions,
+ *     birth_stages (int32 / uint8), token_to_key (int64, request-local key);
+ *   per key, at key offset token_offsets[b] + (ranges before b) +
+ *     reposition_offsets[b], capacity T + R + P per request: records
+ *     [.,3] int32, virtual_mask uint8, key_to_token int64;
+ *   per Reposition: effective_reposition_stages (int32, -1 if ignored),
+ *     effective_repositions, ignored_repositions (uint8);
+ *   transition_offsets: P_b + 1 int32 entries at reposition_offsets[b] + b,
+ *     stage-indexed and relative to the request's first transition (entries
+ *     past the request's stage count hold its total);
+ *   per Drop event: drop_event_to_key (int64);
+ *   transitions (raw token, old, new position; int32) of request b at
+ *     [transition_request_offsets[b], transition_request_offsets[b+1]), at
+ *     most transition_capacity in total (more sets AKV_LAYOUT_CAPACITY and
+ *     the excess is not written);
+ *   status [n][5] int64, the reference's status vector per request:
+ *     {0, key_len, stages, next_position, -1} or {1 (no active token at a
+ *     Reposition), ., ., ., boundary} or {2 (token id outside [0, 2^31)), .,
+ *     ., ., token id};
+ *   decode view (optional, all three NULL to skip): active_offsets [n+1],
+ *     raw_indices, active_positions;
+ *   totals [4] int64: {transitions, kept tokens, keys, AKV_LAYOUT_* bits}.
+ *
+ * tile_offsets[n+1]: prefix over requests of ceil(T_b / 512); count_offsets
+ * [n+1] int64: prefix over requests of tiles_b * (P_b + 1).  The workspace
+ * (akv_compile_layouts_workspace_bytes with the batch's n_requests,
+ * n_tokens, n_repositions, n_count_cells) needs no initial contents.  At
+ * most akv_compile_layouts_max_repositions() Reposition events per request.
+ * Work: linear in tokens and ranges (times log P for a binary search), plus
+ * one 512-token block scan per pair of tile and effective Reposition whose
+ * transitions reach into the tile.
+ */
+#define AKV_LAYOUT_CAPACITY 1  /* transitions exceed transition_capacity      */
+#define AKV_LAYOUT_ERROR 2     /* some request's status[0] is non-zero         */
+#define AKV_LAYOUT_TOO_MANY 4  /* a request has more Repositions than allowed;
+                                  its outputs are not written (status[0] = -1) */
+
+typedef struct akv_layout_batch {
+  int32_t n_requests;
+  int32_t n_tiles;
+  int64_t n_tokens;       /* token_offsets[n_requests] */
+  int64_t n_repositions;  /* reposition_offsets[n_requests] */
+  int64_t n_count_cells;  /* count_offsets[n_requests] */
+  const int64_t* token_offsets;
+  const void* token_ids;
+  int32_t token_ids_is64;
+  const int32_t* tile_offsets;
+  const int64_t* count_offsets;
+  const int32_t* drop_event_offsets;
+  const int32_t* drop_insert_offsets;
+  const int32_t* drop_range_offsets;
+  const int32_t* drop_ranges;
+  const int32_t* reposition_offsets;
+  const int32_t* reposition_raw_boundaries;
+  int32_t* positions;
+  uint8_t* keep_mask;
+  int32_t* materialized_stage;
+  int32_t* birth_positions;
+  int32_t* birth_stages;
+  int64_t* token_to_key;
+  int32_t* records;
+  uint8_t* virtual_mask;
+  int64_t* key_to_token;
+  int32_t* transition_offsets;
+  int32_t* transition_request_offsets;
+  int32_t* transition_raw_tokens;
+  int32_t* transition_old_positions;
+  int32_t* transition_new_positions;
+  int64_t transition_capacity;
+  int32_t* effective_reposition_stages;
+  uint8_t* effective_repositions;
+  uint8_t* ignored_repositions;
+  int64_t* drop_event_to_key;
+  int64_t* status;
+  int32_t* active_offsets;
+  int32_t* raw_indices;
+  int32_t* active_positions;
+  int64_t* totals;
+  void* workspace;
+} akv_layout_batch;
+
+int64_t akv_compile_layouts_max_repositions(void);
+int64_t akv_compile_layouts_batch_bytes(void); /* sizeof(akv_layout_batch), for FFI checks */
+int64_t akv_compile_layouts_workspace_bytes(int32_t n_requests, int64_t n_tokens,
+                                            int64_t n_repositions, int64_t n_count_cells);
+int akv_compile_layouts(const akv_layout_batch* batch, void* stream);
+
+/*
  * Decode read indices.  Replaces the Triton kernel context_decode_indices
  * (akv/system/sglang/kernels/ops/attention/context_page_table.py:34-76),
  * same contract: registry rows of six int64 cells {raw_ids*, positions*,

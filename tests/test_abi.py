@@ -66,3 +66,21 @@ def test_argument_errors_are_reported_before_any_launch():
         None, None, 0, None, 0, None, 0, None, 0, None, 0, None, 0, None, 0, 1, 4,
         None) == _native.AKV_ERR_INVALID
     assert lib.akv_write_row_slots(None, None, 0, None, 0, None, 0, 0, None) == _native.AKV_OK
+
+
+def test_layout_batch_struct_matches_the_header():
+    """The ctypes mirror of akv_layout_batch has the C struct's size, and
+    every field name of the header, in order."""
+    import ctypes
+
+    from akv_b200 import _native
+
+    assert ctypes.sizeof(_native.LayoutBatch) == _native.lib.akv_compile_layouts_batch_bytes()
+    text = open(os.path.join(ROOT, "include", "akv_b200.h")).read()
+    body = text[text.index("typedef struct akv_layout_batch {"):]
+    body = re.sub(r"/\*.*?\*/", "", body[: body.index("} akv_layout_batch;")], flags=re.S)
+    names = re.findall(r"\b([a-z_0-9]+);", body)
+    assert names == [f[0] for f in _native.LayoutBatch._fields_]
+    assert _native.lib.akv_compile_layouts_max_repositions() >= 1024
+    assert _native.lib.akv_compile_layouts_workspace_bytes(3, 5000, 10, 300) > 0
+    assert _native.lib.akv_compile_layouts(None, None) == _native.AKV_ERR_INVALID
