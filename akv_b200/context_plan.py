@@ -268,6 +268,19 @@ class LayoutCompiler:
 
     def compile(self, programs) -> BatchLayout:
         """Compile a list of ``Program`` (validated) on the current stream."""
+        return self.launch(self.prepare(programs))
+
+    def launch(self, prepared) -> BatchLayout:
+        """Run the four launches on inputs already copied by ``prepare``
+        (stream-ordered, no host synchronisation)."""
+        batch, plan = prepared
+        _native.check(_native.lib.akv_compile_layouts(batch, _native.stream_of(self.device)),
+                      "compile_layouts")
+        return BatchLayout(self, plan)
+
+    def prepare(self, programs):
+        """Pack the programs and copy them to the device (one pinned copy for
+        the metadata, one for the token ids); returns what ``launch`` takes."""
         n = len(programs)
         T = [len(p.token_ids) for p in programs]
         E = [len(p.drop_insert_offsets) for p in programs]
@@ -344,11 +357,10 @@ class LayoutCompiler:
         if int(cells[-1]) > self.max_cells or int(_native.lib.akv_compile_layouts_workspace_bytes(
                 n, int(tokens[-1]), int(reps[-1]), int(cells[-1]))) > self.workspace.numel():
             raise ValueError("batch exceeds the compiler's workspace")
-        _native.check(_native.lib.akv_compile_layouts(b, _native.stream_of(self.device)),
-                      "compile_layouts")
         plan = dict(n=n, tokens=tokens.tolist(), events=events.tolist(), ranges=ranges.tolist(),
-                    reps=reps.tolist(), programs=programs)
-        return BatchLayout(self, plan)
+                    reps=reps.tolist(), programs=programs,
+                    h2d_bytes=4 * o + ids_host.itemsize * len(ids))
+        return b, plan
 
 
 def _check_vector(name, value):

@@ -203,3 +203,38 @@ def event_program(rng, tokens, events, repositions, max_ranges=4, span=None):
     ids = rng.integers(0, 200000, size=tokens).astype(np.int64)
     return (ids, inserts.astype(np.int32), np.asarray(offsets, np.int32),
             np.asarray(ranges, np.int32), bounds.astype(np.int32))
+
+
+def agent_turn_programs(seed=0, requests=64, turns=8, min_len=2048, max_len=32768,
+                        drop_frac=0.3, max_span=1024):
+    """Multi-turn agent programs for the general event compiler ("c3m"):
+    the c3 request lengths (lengths U{min_len..max_len}, seeded), each prompt
+    cut into ``turns`` turns at sorted random raw boundaries; at the end of
+    every turn one Drop event removes spans (each at most ``max_span``
+    tokens, about ``drop_frac`` of the turn's new tokens in total) from the
+    text materialized so far, and a Reposition at the same insertion offset
+    compacts the positions -- the cache operation an agent runs per turn.
+    Returns a list of (token_ids, drop_insert_offsets, drop_range_offsets,
+    drop_ranges, reposition_raw_boundaries)."""
+    rng = np.random.default_rng(seed)
+    counts = rng.integers(min_len, max_len + 1, size=requests)
+    programs = []
+    for length in counts:
+        length = int(length)
+        bounds = np.sort(rng.choice(np.arange(turns, length - 1), size=turns, replace=False))
+        inserts, offsets, ranges = [], [0], []
+        prev = 0
+        for b in bounds:
+            ins = int(b) + 1
+            budget = max(1, int(drop_frac * (ins - prev)))
+            count = max(1, -(-budget // max_span))
+            lengths = np.maximum(1, rescaled_lengths(rng, count, 1, max_span, budget))
+            spans = place_spans(rng, ins, lengths)
+            inserts.append(ins)
+            ranges += [int(x) for x in spans]
+            offsets.append(offsets[-1] + len(spans) // 2)
+            prev = ins
+        ids = rng.integers(0, 200000, size=length).astype(np.int64)
+        programs.append((ids, np.asarray(inserts, np.int32), np.asarray(offsets, np.int32),
+                         np.asarray(ranges, np.int32), bounds.astype(np.int32)))
+    return programs

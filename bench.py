@@ -2,7 +2,7 @@
 """Benchmark of the AKV cache-operation hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c1|c5]
+                    [--workload c2|c1|c5|c4|c3m] [--layers L]
 
 Metric: reposition+drop retained-KV GB/s (algorithmic bytes / time).  At
 N = 1 the workload is c2, the GPT-OSS-120B-shaped cache: one 65536-token
@@ -25,6 +25,14 @@ metadata (the scheduler state is replicated per TP rank); no collective on
 the data path, a barrier around the timed region and a MAX all-reduce of
 the timings afterwards.  The workload is fixed as N grows (strong
 scaling); the aggregate counts every rank's bytes.
+
+The same JSON line carries two more sections of the path, each with its own
+metric, roofline and CPU reference: ``decode_attention`` (c4: paged GQA
+decode with sinks over the compacted cache, batch 128, 36 layers alternating
+sliding-window and full attention; tokens/s) and ``event_compiler`` (c3m: the
+general multi-stage event compiler over 64 multi-turn agent programs,
+1.13M tokens; tokens/s).  ``--workload c4`` / ``--workload c3m`` run one of
+them alone.
 
 ``--impl reference``: the reference's CPU implementation of the path on the
 host cores (rank 0 only): its own C++ event compiler (oracle/_ref, built
@@ -58,6 +66,7 @@ WORKLOADS = {
     "c2": (36, 8, 64, "yarn"),
     "c5": (80, 8, 128, "rope500000"),
     "c4": (36, 8, 64, None),  # decode attention only (see bench_attention)
+    "c3m": (0, 0, 0, None),   # event compiler only (see bench_compiler)
 }
 
 
@@ -453,6 +462,7 @@ def run_ours(args):
     torch.cuda.empty_cache()
     attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                 max(5, min(args.steps // 20, 20)))
+    compiler = bench_compiler(dev, world, rank, 3, 20)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -495,6 +505,7 @@ def run_ours(args):
             "gpu_launches": 4 * args.steps,
             "cpu_baseline": cpu,
             "decode_attention": attention,
+            "event_compiler": compiler,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
@@ -591,8 +602,114 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36):
     }
 
 
+def bench_compiler(dev, world, rank, warmup, steps, seed=0):
+    """c3m: the general event compiler over 64 multi-turn agent programs
+    (c3 request lengths, 8 turns each: a Drop event then a Reposition at the
+    end of every turn; 1.13M tokens at seed 0).  The program is the same on
+    every rank (scheduler state is replicated per TP rank), so this is a
+    replica measurement.  Device: the four launches on resident inputs.
+    e2e: host programs -> packing -> H2D -> launches -> D2H of the
+    per-request status and the totals.  CPU: the reference's C++ compiler
+    (oracle/_ref), request by request on one thread as its scheduler runs
+    it."""
+    from akv_b200 import workloads
+    from akv_b200.context_plan import LayoutCompiler, Program
+
+    progs = [Program.of(*p) for p in workloads.agent_turn_programs(seed=seed)]
+    tokens = sum(len(p.token_ids) for p in progs)
+    comp = LayoutCompiler(dev, max_tokens=tokens, max_requests=len(progs),
+                          max_events=sum(len(p.drop_insert_offsets) for p in progs),
+                          max_ranges=sum(len(p.drop_ranges) // 2 for p in progs),
+                          max_repositions=sum(len(p.reposition_raw_boundaries) for p in progs),
+                          transition_capacity=4 * tokens)
+    stream = torch.cuda.current_stream(dev)
+    prepared = comp.prepare(progs)
+    for _ in range(warmup):
+        comp.launch(prepared)
+    torch.cuda.synchronize()
+    totals = comp.totals.cpu().tolist()
+    if totals[3]:
+        raise RuntimeError(f"event compiler benchmark: status bits {totals[3]}")
+    dist_barrier(world)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for a, b in ev:
+        a.record(stream)
+        comp.launch(prepared)
+        b.record(stream)
+    torch.cuda.synchronize()
+    dev_ms = dist_max(statistics.median(a.elapsed_time(b) for a, b in ev), world)
+    # End to end through the public API, one step after another.
+    status_host = torch.empty_like(comp.status, device="cpu").pin_memory()
+    totals_host = torch.empty(4, dtype=torch.int64).pin_memory()
+    e2e = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(stream)
+        comp.compile(progs)
+        status_host.copy_(comp.status, non_blocking=True)
+        totals_host.copy_(comp.totals, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        e2e.append(a.elapsed_time(b))
+    e2e_ms = dist_max(statistics.median(e2e), world)
+    h2d = prepared[1]["h2d_bytes"]
+    d2h = status_host.numel() * 8 + 32
+    transitions, kept = int(totals[0]), int(totals[1])
+    # Algorithmic bytes: ids in; per token 4+1+4+4+4+8 (positions, keep, stage, birth
+    # position and stage, token_to_key) + 12+1+8 (record, virtual flag, key_to_token)
+    # out; 8 per kept token (decode view); 12 per transition.
+    alg = tokens * (8 + 25 + 21) + kept * 8 + transitions * 12
+    peak, peak_kind = measured_peak()
+    cpu = None
+    if rank == 0 and world == 1:
+        from oracle import oracle, reference
+
+        comp_fn = reference.compile_context_layout if reference.available() else \
+            oracle.compile_layout
+        t0 = time.perf_counter()
+        for p in progs:
+            comp_fn(p.token_ids, p.drop_insert_offsets, p.drop_range_offsets, p.drop_ranges,
+                    p.reposition_raw_boundaries, p.reposition_raw_boundaries.astype(np.int64) + 1)
+        sec = time.perf_counter() - t0
+        cpu = {"value": round(tokens / sec, 1), "unit": "tokens/s", "cores": 1,
+               "kind": "reference" if reference.available() else "port",
+               "sample": f"all {len(progs)} programs ({tokens} tokens), compile_context_layout "
+                         f"count + compile passes, one request at a time"}
+    return {
+        "metric": "event compiler tokens/s", "value": round(tokens * world / (dev_ms / 1e3), 1),
+        "unit": "tokens/s", "ms_per_step": round(dev_ms, 4), "n_gpus": world,
+        "scaling": "replicas",
+        "config": {"workload": "c3m", "requests": len(progs), "tokens": tokens, "turns": 8,
+                   "transitions": transitions, "kept": kept},
+        "e2e": {"value": round(tokens * world / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "kernel": "layout_* (4 launches)",
+                     "achieved": round(alg / (dev_ms / 1e3) / 1e9, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(alg / (dev_ms / 1e3) / 1e9 / peak, 4),
+                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": alg},
+        "gpu_launches_per_step": 4,
+        "cpu_baseline": cpu,
+    }
+
+
 def main():
     args = parse_args()
+    if args.workload == "c3m" and args.impl == "ours":
+        # The event compiler alone.
+        world, rank, local = dist_setup()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = bench_compiler(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return 0
     if args.workload == "c4" and args.impl == "ours":
         # Decode attention alone (for profiling cuts: --layers 2).
         world, rank, local = dist_setup()
