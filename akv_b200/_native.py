@@ -82,8 +82,9 @@ SIGNATURES = {
     "akv_compile_layouts": [ctypes.POINTER(LayoutBatch), _P],
     "akv_decode_attention": [
         _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, ctypes.c_float, _I32,
-        _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P, _I64, _I64, _P, _P, _P,
+        _I32, _I32, _I32, _P, _I32, _P, _I32, _P, _P, _P, _P, _I64, _I64, _P, _P, _P,
     ],
+    "akv_decode_attention_ctas_per_sm": [_I32, _I32],
 }
 RESTYPES = {
     "akv_version": ctypes.c_char_p,

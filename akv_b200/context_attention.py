@@ -27,12 +27,13 @@ import torch
 from . import _native
 
 NUM_SMS = 148
-MAX_SPLITS = 512  # key ranges per request the combine kernel merges
+ITEMS_PER_CTA = 4   # key ranges per persistent CTA
+MAX_SPLITS = 512    # key ranges per request the combine kernel merges
 
 
 class DecodeAttention:
     def __init__(self, num_q_heads, num_kv_heads, head_dim, max_batch, device, *,
-                 max_items=None, sm_scale=None):
+                 max_items=None, sm_scale=None, ctas=None):
         if num_q_heads != 8 * num_kv_heads or num_kv_heads not in (1, 2, 4, 8):
             raise ValueError("decode attention supports GQA groups of 8 and 1-8 KV heads")
         if head_dim not in (64, 128):
@@ -44,9 +45,20 @@ class DecodeAttention:
         self.hq, self.hkv, self.d = num_q_heads, num_kv_heads, head_dim
         self.sm_scale = 1.0 / math.sqrt(head_dim) if sm_scale is None else float(sm_scale)
         self.max_batch = int(max_batch)
-        self.max_items = int(max_items or max(4 * NUM_SMS, 2 * self.max_batch) + self.max_batch)
+        if ctas is None:
+            per_sm = int(_native.lib.akv_decode_attention_ctas_per_sm(num_kv_heads, head_dim))
+            if per_sm <= 0:
+                raise RuntimeError("decode attention: occupancy query failed")
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            ctas = per_sm * sms
+        self.ctas = int(ctas)
+        # Enough items for the default plan: ITEMS_PER_CTA per CTA, plus one
+        # rounding remainder per request.
+        self.max_items = int(max_items if max_items is not None else
+                             max(ITEMS_PER_CTA, 1) * self.ctas + self.max_batch)
         n = self.max_items
-        self._host = torch.empty(4 * n + 2 * self.max_batch, dtype=torch.int32, pin_memory=True)
+        self._host = torch.empty(4 * n + 2 * self.max_batch + self.ctas + 1, dtype=torch.int32,
+                                 pin_memory=True)
         self._dev = torch.empty_like(self._host, device=device)
         self.part_acc = torch.empty((n, num_q_heads, head_dim), dtype=torch.float32, device=device)
         self.part_ml = torch.empty((n, num_q_heads, 2), dtype=torch.float32, device=device)
@@ -54,20 +66,30 @@ class DecodeAttention:
         self._copied = torch.cuda.Event()
         self._copied.record(torch.cuda.current_stream(device))
         self.n_items = 0
+        self.n_ctas = 0
         self.batch = 0
         self.split = False
 
-    def plan(self, kv_indptr_host, chunk=None):
-        """Work list from host-known CSR offsets of the key lists."""
+    def plan(self, kv_indptr_host, chunk=None, items_per_cta=None):
+        """Work list from host-known CSR offsets of the key lists.
+
+        With ``items_per_cta`` (default ``ITEMS_PER_CTA``) the launch is
+        persistent: ``ctas`` CTAs (all that fit on the GPU at once) each run a
+        list of items, the key ranges cut ``items_per_cta`` times finer than
+        one range per CTA and dealt to the CTAs longest first in a
+        back-and-forth order, so that every CTA ends at about the same time.
+        ``items_per_cta=0`` launches one CTA per item instead."""
         indptr = np.asarray(kv_indptr_host, np.int64)
         lengths = np.diff(indptr)
         batch = len(lengths)
         if batch > self.max_batch:
             raise ValueError("batch exceeds the planned maximum")
         total = int(lengths.sum())
+        per_cta = ITEMS_PER_CTA if items_per_cta is None else int(items_per_cta)
         if chunk is None:
-            # About three CTAs per SM in total, whole 32-key tiles, at least 256 keys.
-            chunk = max(256, -(-total // (3 * NUM_SMS)))
+            # Whole 32-key tiles, at least 256 keys; about `per_cta` items per
+            # resident CTA (one per CTA when not persistent).
+            chunk = max(256, -(-total // (self.ctas * max(1, per_cta))))
             chunk = -(-chunk // 32) * 32
         items, merge, partials = [], np.zeros((batch, 2), np.int64), 0
         for b, n in enumerate(lengths):
@@ -86,16 +108,30 @@ class DecodeAttention:
         # Longest ranges first: the short tails fill the last wave.
         items.sort(key=lambda it: it[1] - it[2])
         work = np.asarray(items, np.int32).reshape(-1, 4)
+        n = len(work)
+        ctas = 0
+        if per_cta > 0 and n > 0:
+            ctas = min(self.ctas, n)
+            i = np.arange(n)
+            lap, pos = i // ctas, i % ctas
+            owner = np.where(lap % 2 == 0, pos, ctas - 1 - pos)
+            order = np.argsort(owner, kind="stable")
+            work = work[order]
+            cta_items = np.searchsorted(owner[order], np.arange(ctas + 1)).astype(np.int32)
         self._copied.synchronize()
         host = self._host
-        host[: 4 * len(work)].copy_(torch.from_numpy(work.reshape(-1)))
-        host[4 * self.max_items: 4 * self.max_items + 2 * batch].copy_(
-            torch.from_numpy(merge.astype(np.int32).reshape(-1)))
-        self._dev[: 4 * len(work)].copy_(host[: 4 * len(work)], non_blocking=True)
-        self._dev[4 * self.max_items: 4 * self.max_items + 2 * batch].copy_(
-            host[4 * self.max_items: 4 * self.max_items + 2 * batch], non_blocking=True)
+        mo, co = 4 * self.max_items, 4 * self.max_items + 2 * self.max_batch
+        host[: 4 * n].copy_(torch.from_numpy(work.reshape(-1)))
+        host[mo: mo + 2 * batch].copy_(torch.from_numpy(merge.astype(np.int32).reshape(-1)))
+        if ctas:
+            host[co: co + ctas + 1].copy_(torch.from_numpy(cta_items))
+        self._dev[: 4 * n].copy_(host[: 4 * n], non_blocking=True)
+        self._dev[mo: mo + 2 * batch].copy_(host[mo: mo + 2 * batch], non_blocking=True)
+        if ctas:
+            self._dev[co: co + ctas + 1].copy_(host[co: co + ctas + 1], non_blocking=True)
         self._copied.record(torch.cuda.current_stream(self.device))
-        self.n_items, self.batch, self.split = len(work), batch, partials > 0
+        self.n_items, self.batch, self.split = n, batch, partials > 0
+        self.n_ctas = ctas
         self.chunk = chunk
         return self
 
@@ -116,13 +152,16 @@ class DecodeAttention:
         if out is None:
             out = torch.empty((self.batch, self.hq, self.d), dtype=torch.bfloat16,
                               device=self.device)
-        merge = self._dev[4 * self.max_items:] if self.split else None
+        mo, co = 4 * self.max_items, 4 * self.max_items + 2 * self.max_batch
+        merge = self._dev[mo:] if self.split else None
+        cta_items = self._dev[co:] if self.n_ctas else None
         status = _native.lib.akv_decode_attention(
             _native.ptr(q), q.stride(0), q.stride(1), _native.ptr(k_pool), _native.ptr(v_pool),
             k_pool.stride(0), k_pool.stride(1), v_pool.stride(0), v_pool.stride(1),
             min(k_pool.shape[0], v_pool.shape[0]), _native.ptr(kv_indices), _native.ptr(sinks),
             self.sm_scale, self.batch, self.hq, self.hkv, self.d, _native.ptr(self._dev),
-            self.n_items, _native.ptr(merge), _native.ptr(self.part_acc),
+            self.n_items, _native.ptr(cta_items), self.n_ctas, _native.ptr(merge),
+            _native.ptr(self.part_acc),
             _native.ptr(self.part_ml), _native.ptr(out), out.stride(0), out.stride(1),
             _native.ptr(lse), _native.ptr(self.error_flag), _native.stream_of(self.device),
         )

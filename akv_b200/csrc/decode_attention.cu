@@ -60,6 +60,7 @@ struct AttnParams {
   const float* sinks;  // [q_heads] natural-log logits, or null
   float scale_log2;    // sm_scale * log2(e)
   const int4* work;    // {request, kv_begin, kv_end, partial or -1}
+  const int* cta_items;  // [ctas + 1] per-CTA item lists, or null (one item per CTA)
   float* part_acc;     // [partials, q_heads, D]
   float* part_ml;      // [partials, q_heads, 2] (max in base 2, sum)
   __nv_bfloat16* out;
@@ -129,15 +130,15 @@ struct Cfg {
   static constexpr int kSmem = NSTAGE * kStageBytes;
 };
 
+// One work item: a key range of one request, all KV heads.  Called by every
+// thread of the CTA; it leaves no copy in flight and ends on a barrier, so
+// the next item may reuse the shared-memory stages at once.
 template <int D, int HKV, int TK, int NSTAGE>
-__global__ void __launch_bounds__(32 * HKV)
-decode_attention_kernel(const AttnParams p) {
+__device__ __forceinline__ void attend_item(const AttnParams& p, const int4 w,
+                                            unsigned char* smem) {
   using C = Cfg<D, HKV, TK, NSTAGE>;
   static_assert(D % 16 == 0 && D >= 64, "head_dim must be a multiple of 16, at least 64");
   static_assert(TK % 16 == 0, "key tile is a whole number of 16-key MMA blocks");
-  extern __shared__ __align__(128) unsigned char smem[];
-
-  const int4 w = p.work[blockIdx.x];
   const int b = w.x, kv_begin = w.y, kv_end = w.z, partial = w.w;
   const int n_keys = kv_end - kv_begin;
   const int n_tiles = (n_keys + TK - 1) / TK;
@@ -342,6 +343,22 @@ decode_attention_kernel(const AttnParams p) {
   }
 }
 
+// One CTA per work item, or -- with cta_items -- a persistent CTA that runs
+// its list of items [cta_items[c], cta_items[c+1]) one after another (the
+// host balances the lists, so no CTA is left with a long tail).
+template <int D, int HKV, int TK, int NSTAGE>
+__global__ void __launch_bounds__(32 * HKV)
+decode_attention_kernel(const AttnParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  if (p.cta_items == nullptr) {
+    attend_item<D, HKV, TK, NSTAGE>(p, p.work[blockIdx.x], smem);
+    return;
+  }
+  const int i1 = p.cta_items[blockIdx.x + 1];
+  for (int i = p.cta_items[blockIdx.x]; i < i1; ++i)
+    attend_item<D, HKV, TK, NSTAGE>(p, p.work[i], smem);
+}
+
 // Combine the partial results of split requests.  Block (request, head
 // group): one warp per query head.  The warp first turns the splits' maxima
 // into per-split weights 2^(m_i - M) (kept in shared memory) and the
@@ -397,20 +414,41 @@ decode_combine_kernel(const AttnParams p, const int2* merge, int batch) {
     p.lse[(long long)b * p.num_q_heads + h] = den > 0.f ? (base + log2f(den)) * kLn2 : -INFINITY;
 }
 
-template <int D, int HKV>
-int launch_attention(const AttnParams& p, int n_items, const int2* merge, int batch,
-                     cudaStream_t s) {
-  // Keys per stage: as many as fit AKV_ATTENTION_TILE_BYTES of K rows, 16
-  // or 32; stages: AKV_ATTENTION_STAGES, one more when a stage is small.
-  constexpr int kRow = HKV * D * 2;
-  constexpr int TK = (AKV_ATTENTION_TILE_BYTES / kRow >= 32) ? 32 : 16;
-  constexpr int NSTAGE = AKV_ATTENTION_STAGES + ((HKV * D <= 256) ? 1 : 0);
+// Keys per stage: as many as fit AKV_ATTENTION_TILE_BYTES of K rows, 16 or
+// 32; stages: AKV_ATTENTION_STAGES, one more when a stage is small.
+template <int D, int HKV> struct Pick {
+  static constexpr int kRow = HKV * D * 2;
+  static constexpr int TK = (AKV_ATTENTION_TILE_BYTES / kRow >= 32) ? 32 : 16;
+  static constexpr int NSTAGE = AKV_ATTENTION_STAGES + ((HKV * D <= 256) ? 1 : 0);
   using C = Cfg<D, HKV, TK, NSTAGE>;
-  auto kernel = decode_attention_kernel<D, HKV, TK, NSTAGE>;
+};
+
+// Resident CTAs per SM of the kernel for this shape (the persistent grid).
+template <int D, int HKV>
+int ctas_per_sm() {
+  using P = Pick<D, HKV>;
+  auto kernel = decode_attention_kernel<D, HKV, P::TK, P::NSTAGE>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P::C::kSmem) !=
+      cudaSuccess)
+    return -AKV_ERR_CUDA;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, P::C::kThreads, P::C::kSmem) !=
+      cudaSuccess)
+    return -AKV_ERR_CUDA;
+  return n;
+}
+
+template <int D, int HKV>
+int launch_attention(const AttnParams& p, int n_items, int n_ctas, const int2* merge,
+                     int batch, cudaStream_t s) {
+  using P = Pick<D, HKV>;
+  using C = typename P::C;
+  auto kernel = decode_attention_kernel<D, HKV, P::TK, P::NSTAGE>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
       cudaSuccess)
     return AKV_ERR_CUDA;
-  if (n_items > 0) kernel<<<n_items, C::kThreads, C::kSmem, s>>>(p);
+  const int grid = p.cta_items != nullptr ? n_ctas : n_items;
+  if (n_items > 0 && grid > 0) kernel<<<grid, C::kThreads, C::kSmem, s>>>(p);
   if (merge != nullptr && batch > 0) {
     const dim3 grid(batch, (p.num_q_heads + kCombineHeads - 1) / kCombineHeads);
     decode_combine_kernel<D><<<grid, 32 * kCombineHeads, 0, s>>>(p, merge, batch);
@@ -419,13 +457,13 @@ int launch_attention(const AttnParams& p, int n_items, const int2* merge, int ba
 }
 
 template <int D>
-int dispatch_heads(const AttnParams& p, int hkv, int n_items, const int2* merge, int batch,
-                   cudaStream_t s) {
+int dispatch_heads(const AttnParams& p, int hkv, int n_items, int n_ctas, const int2* merge,
+                   int batch, cudaStream_t s) {
   switch (hkv) {
-    case 1: return launch_attention<D, 1>(p, n_items, merge, batch, s);
-    case 2: return launch_attention<D, 2>(p, n_items, merge, batch, s);
-    case 4: return launch_attention<D, 4>(p, n_items, merge, batch, s);
-    case 8: return launch_attention<D, 8>(p, n_items, merge, batch, s);
+    case 1: return launch_attention<D, 1>(p, n_items, n_ctas, merge, batch, s);
+    case 2: return launch_attention<D, 2>(p, n_items, n_ctas, merge, batch, s);
+    case 4: return launch_attention<D, 4>(p, n_items, n_ctas, merge, batch, s);
+    case 8: return launch_attention<D, 8>(p, n_items, n_ctas, merge, batch, s);
   }
   return AKV_ERR_UNSUPPORTED;
 }
@@ -438,11 +476,13 @@ extern "C" int akv_decode_attention(
     const void* v_pool, int64_t k_stride_slot, int64_t k_stride_head, int64_t v_stride_slot,
     int64_t v_stride_head, int64_t num_slots, const int32_t* kv_indices, const float* sinks,
     float sm_scale, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-    const int32_t* work, int32_t n_items, const int32_t* merge, float* partial_acc,
+    const int32_t* work, int32_t n_items, const int32_t* cta_items, int32_t n_ctas,
+    const int32_t* merge, float* partial_acc,
     float* partial_ml, void* out, int64_t out_stride_batch, int64_t out_stride_head, float* lse,
     int32_t* error_flag, void* stream) {
   using namespace akv;
-  if (batch < 0 || n_items < 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads * kGroup ||
+  if (batch < 0 || n_items < 0 || (cta_items != nullptr && n_ctas < 0) || num_kv_heads <= 0 ||
+      num_q_heads != num_kv_heads * kGroup ||
       !q || !k_pool || !v_pool || !kv_indices || !work || !out || num_slots <= 0)
     return AKV_ERR_INVALID;
   if ((q_stride_head % 2) || (reinterpret_cast<uintptr_t>(q) & 3) ||
@@ -464,6 +504,7 @@ extern "C" int akv_decode_attention(
   p.sinks = sinks;
   p.scale_log2 = sm_scale * kLog2e;
   p.work = reinterpret_cast<const int4*>(work);
+  p.cta_items = cta_items;
   p.part_acc = partial_acc;
   p.part_ml = partial_ml;
   p.out = static_cast<__nv_bfloat16*>(out);
@@ -476,8 +517,23 @@ extern "C" int akv_decode_attention(
   if (mg != nullptr && (!partial_acc || !partial_ml)) return AKV_ERR_INVALID;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (head_dim) {
-    case 64: return dispatch_heads<64>(p, num_kv_heads, n_items, mg, batch, s);
-    case 128: return dispatch_heads<128>(p, num_kv_heads, n_items, mg, batch, s);
+    case 64: return dispatch_heads<64>(p, num_kv_heads, n_items, n_ctas, mg, batch, s);
+    case 128: return dispatch_heads<128>(p, num_kv_heads, n_items, n_ctas, mg, batch, s);
   }
   return AKV_ERR_UNSUPPORTED;
+}
+
+extern "C" int32_t akv_decode_attention_ctas_per_sm(int32_t num_kv_heads, int32_t head_dim) {
+  using namespace akv;
+  switch (head_dim * 16 + num_kv_heads) {
+    case 64 * 16 + 1: return ctas_per_sm<64, 1>();
+    case 64 * 16 + 2: return ctas_per_sm<64, 2>();
+    case 64 * 16 + 4: return ctas_per_sm<64, 4>();
+    case 64 * 16 + 8: return ctas_per_sm<64, 8>();
+    case 128 * 16 + 1: return ctas_per_sm<128, 1>();
+    case 128 * 16 + 2: return ctas_per_sm<128, 2>();
+    case 128 * 16 + 4: return ctas_per_sm<128, 4>();
+    case 128 * 16 + 8: return ctas_per_sm<128, 8>();
+  }
+  return -AKV_ERR_UNSUPPORTED;
 }

@@ -355,7 +355,10 @@ int akv_build_decode_metadata(
  * output directly, else the item's slot in partial_acc [P, q_heads, D] and
  * partial_ml [P, q_heads, 2]); merge: DEVICE int32 [batch, 2] rows
  * {first partial, count} (count 0 = written directly) or NULL when no item
- * is split.  out: bf16 [batch, q_heads, head_dim]; lse: fp32 [batch, q_heads]
+ * is split.  cta_items: DEVICE int32 [n_ctas + 1] or NULL: with it, n_ctas
+ * persistent CTAs run, CTA c processing work rows [cta_items[c],
+ * cta_items[c+1]) in order (the host balances the lists); NULL launches one
+ * CTA per work row.  out: bf16 [batch, q_heads, head_dim]; lse: fp32 [batch, q_heads]
  * natural-log LSE including the sink, or NULL.  A slot outside [0, num_slots)
  * is read as slot 0 and sets *error_flag (DEVICE int32, may be NULL).
  * The host side (akv_b200/context_attention.py) builds work/merge from
@@ -366,9 +369,15 @@ int akv_decode_attention(
     const void* v_pool, int64_t k_stride_slot, int64_t k_stride_head, int64_t v_stride_slot,
     int64_t v_stride_head, int64_t num_slots, const int32_t* kv_indices, const float* sinks,
     float sm_scale, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-    const int32_t* work, int32_t n_items, const int32_t* merge, float* partial_acc,
-    float* partial_ml, void* out, int64_t out_stride_batch, int64_t out_stride_head, float* lse,
-    int32_t* error_flag, void* stream);
+    const int32_t* work, int32_t n_items, const int32_t* cta_items, int32_t n_ctas,
+    const int32_t* merge, float* partial_acc, float* partial_ml, void* out,
+    int64_t out_stride_batch, int64_t out_stride_head, float* lse, int32_t* error_flag,
+    void* stream);
+
+/* Resident CTAs per SM of akv_decode_attention for this shape (the size of
+ * a persistent launch is this times the SM count); a negative AKV_* status
+ * on error.  Needs a CUDA device.  No reference counterpart. */
+int32_t akv_decode_attention_ctas_per_sm(int32_t num_kv_heads, int32_t head_dim);
 
 /*
  * Overflow-row slot scatter.  Replaces the Triton kernel write_row_slots
