@@ -85,6 +85,11 @@ SIGNATURES = {
         _I32, _I32, _I32, _P, _I32, _P, _I32, _P, _P, _P, _P, _I64, _I64, _P, _P, _P,
     ],
     "akv_decode_attention_ctas_per_sm": [_I32, _I32],
+    "akv_context_attention_query_block": [],
+    "akv_context_attention": [
+        _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P,
+        ctypes.c_float, _I64, _I32, _I32, _I32, _P, _I32, _P, _I64, _I64, _P, _P, _P,
+    ],
 }
 RESTYPES = {
     "akv_version": ctypes.c_char_p,
@@ -95,6 +100,8 @@ RESTYPES = {
     "akv_compile_layouts_max_repositions": _I64,
     "akv_compile_layouts_workspace_bytes": _I64,
     "akv_compile_layouts_batch_bytes": _I64,
+    "akv_decode_attention_ctas_per_sm": _I32,
+    "akv_context_attention_query_block": _I64,
 }
 
 

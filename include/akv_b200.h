@@ -374,6 +374,42 @@ int akv_decode_attention(
     int64_t out_stride_batch, int64_t out_stride_head, float* lse, int32_t* error_flag,
     void* stream);
 
+/*
+ * Ragged prefill (extend) attention with context positions and sinks.
+ * Replaces the native ragged prefill launch of ContextAttentionMetadata.forward
+ * and its host-side native_plan gathers
+ * (srt/layers/attention/context_backend.py:184-241; the position-aware
+ * extend kernel of akv/system/sglang.patch:106-237) and the sink correction
+ * of flash_attention_with_sink (context_backend.py:244-272).
+ *
+ * Request b: Q_b = qo_indptr[b+1] - qo_indptr[b] new tokens (rows of q and
+ * out, DEVICE int32 birth_slots and q_positions at the same rows; their K/V
+ * already written to the pools) after P_b = kv_indptr[b+1] - kv_indptr[b]
+ * prefix keys (kv_indices, kv_positions).  Query i sees prefix key j when
+ * window < 0 or q_pos - k_pos <= window, and new-token key j when j <= i and
+ * the same window test holds (positions increase along each request's key
+ * list).  q / out: bf16 [tokens, q_heads, head_dim] (strides in elements);
+ * pools bf16 [slots, kv_heads, head_dim]; num_q_heads = 8 * num_kv_heads,
+ * head_dim 64 or 128; sinks fp32 [q_heads] or NULL; lse fp32 [tokens,
+ * q_heads] (natural log, including the sink) or NULL.
+ * work: DEVICE int32 [n_items, 4] rows {request, first query (request-local,
+ * a multiple of akv_context_attention_query_block()), key_lo, key_hi}: the
+ * block's queries read keys [key_lo, key_hi) of the request's key list
+ * (key_hi = P_b + last query + 1; key_lo = first key the window can reach);
+ * built on the host from the CPU positions (akv_b200/context_prefill.py).
+ * A slot outside [0, num_slots) is read as slot 0 and sets *error_flag.
+ */
+int64_t akv_context_attention_query_block(void);
+int akv_context_attention(
+    const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_pool,
+    const void* v_pool, int64_t k_stride_slot, int64_t k_stride_head, int64_t v_stride_slot,
+    int64_t v_stride_head, int64_t num_slots, const int32_t* qo_indptr, const int32_t* kv_indptr,
+    const int32_t* kv_indices, const int32_t* birth_slots, const int32_t* q_positions,
+    const int32_t* kv_positions, const float* sinks, float sm_scale, int64_t window,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const int32_t* work,
+    int32_t n_items, void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
+    int32_t* error_flag, void* stream);
+
 /* Resident CTAs per SM of akv_decode_attention for this shape (the size of
  * a persistent launch is this times the SM count); a negative AKV_* status
  * on error.  Needs a CUDA device.  No reference counterpart. */

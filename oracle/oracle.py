@@ -385,3 +385,55 @@ def decode_attention(q, k_pool, v_pool, kv_indptr, kv_indices, sinks=None, scale
         sig = np.where(np.isfinite(lse), sig, 0.0)
         out = out * sig[:, :, None]
     return out, lse
+
+
+def prefill_attention(q, k_pool, v_pool, qo_indptr, kv_indptr, kv_indices, birth_slots,
+                      q_positions, kv_positions, sinks=None, window=-1, scale=None):
+    """Ragged prefill attention with context positions, in float64.
+
+    Follows the reference's position-aware extend mask (sglang.patch:524-541,
+    725-741; ContextAttentionMetadata.native_plan, context_backend.py:184-222):
+    request b's keys are its prefix (kv_indices / kv_positions at
+    kv_indptr[b]..) followed by its new tokens (birth_slots / q_positions at
+    qo_indptr[b]..); query i sees prefix key j when window < 0 or
+    q_pos - k_pos <= window, and new-token key j when also j <= i.  The sink
+    multiplies the output by sigmoid(lse - sink) (context_backend.py:266-268).
+    Returns (out [tokens, Hq, D], lse [tokens, Hq]).
+    """
+    q = np.asarray(q, np.float64)
+    n, hq, d = q.shape
+    hkv = k_pool.shape[1]
+    group = hq // hkv
+    scale = 1.0 / np.sqrt(d) if scale is None else scale
+    out = np.zeros((n, hq, d))
+    lse = np.full((n, hq), -np.inf)
+    for b in range(len(qo_indptr) - 1):
+        a, e = int(qo_indptr[b]), int(qo_indptr[b + 1])
+        x, y = int(kv_indptr[b]), int(kv_indptr[b + 1])
+        slots = np.concatenate((np.asarray(kv_indices[x:y], np.int64),
+                                np.asarray(birth_slots[a:e], np.int64)))
+        kpos = np.concatenate((np.asarray(kv_positions[x:y], np.int64),
+                               np.asarray(q_positions[a:e], np.int64)))
+        if len(slots) == 0:
+            continue
+        k = np.asarray(k_pool[slots], np.float64)
+        v = np.asarray(v_pool[slots], np.float64)
+        p_count = y - x
+        j = np.arange(len(slots))
+        for i in range(e - a):
+            qp = int(q_positions[a + i])
+            vis = (j < p_count) | (j - p_count <= i)
+            if window is not None and window >= 0:
+                vis &= qp - kpos <= window
+            for h in range(hq):
+                s = (k[vis, h // group, :] @ q[a + i, h]) * scale
+                mx = s.max()
+                wgt = np.exp(s - mx)
+                tot = wgt.sum()
+                out[a + i, h] = (wgt @ v[vis, h // group, :]) / tot
+                lse[a + i, h] = mx + np.log(tot)
+    if sinks is not None:
+        sig = 1.0 / (1.0 + np.exp(-(lse - np.asarray(sinks, np.float64)[None, :])))
+        sig = np.where(np.isfinite(lse), sig, 0.0)
+        out = out * sig[:, :, None]
+    return out, lse
