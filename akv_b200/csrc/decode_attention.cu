@@ -34,18 +34,17 @@ namespace {
 
 constexpr int kGroup = 8;  // query heads per KV head (the MMA N)
 
-// 16-key stages, two of them: 64 KiB of shared memory for 8 KV heads of
-// 64 dims, so three CTAs share an SM (measured on c4: 0.66 ms per full
-// layer with its combine, 5.3 TB/s; 2 CTAs x 3 stages and 1 CTA x 32-key
-// stages were slower, and so were per-warp rings -- a key's 1 KiB row then
-// reaches DRAM as eight separate 128-byte requests -- and a warp-specialised
-// variant with one cp.async.bulk per row and an mbarrier ring, 0.67 ms).
-#ifndef AKV_ATTENTION_TILE_BYTES
-#define AKV_ATTENTION_TILE_BYTES 16384
-#endif
-#ifndef AKV_ATTENTION_STAGES
-#define AKV_ATTENTION_STAGES 2
-#endif
+// 16-key stages, two of them, for every head count: 64 KiB of shared memory
+// for 8 KV heads of 64 dims (three CTAs per SM), proportionally less -- and
+// more CTAs per SM -- when tensor parallelism leaves fewer heads per GPU.
+// Measured on the c4 full layer: 8 heads 0.578 ms; 4 heads 0.371 ms (32-key
+// stages: 0.744), 2 heads 0.347 ms (0.642), 1 head 0.310 ms (0.435); 3 or
+// 4 stages were no better.  Also slower for 8 heads: 2 CTAs x 3 stages,
+// 1 CTA x 32-key stages, per-warp rings (a key's 1 KiB row then reaches
+// DRAM as eight separate 128-byte requests) and a warp-specialised variant
+// with one cp.async.bulk per row and an mbarrier ring.
+constexpr int kTileKeys = 16;
+constexpr int kStages = 2;
 
 struct AttnParams {
   const __nv_bfloat16* q;
@@ -363,12 +362,10 @@ decode_combine_kernel(const AttnParams p, const int2* merge, int batch) {
     p.lse[(long long)b * p.num_q_heads + h] = den > 0.f ? (base + log2f(den)) * kLn2 : -INFINITY;
 }
 
-// Keys per stage: as many as fit AKV_ATTENTION_TILE_BYTES of K rows, 16 or
-// 32; stages: AKV_ATTENTION_STAGES, one more when a stage is small.
+// Keys per stage and stages (see kTileKeys).
 template <int D, int HKV> struct Pick {
-  static constexpr int kRow = HKV * D * 2;
-  static constexpr int TK = (AKV_ATTENTION_TILE_BYTES / kRow >= 32) ? 32 : 16;
-  static constexpr int NSTAGE = AKV_ATTENTION_STAGES + ((HKV * D <= 256) ? 1 : 0);
+  static constexpr int TK = kTileKeys;
+  static constexpr int NSTAGE = kStages;
   using C = Cfg<D, HKV, TK, NSTAGE>;
 };
 

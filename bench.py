@@ -2,7 +2,7 @@
 """Benchmark of the AKV cache-operation hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c1|c5|c4|c3m] [--layers L]
+                    [--workload c2|c1|c5|c4|c3m|c4p] [--layers L]
 
 Metric: reposition+drop retained-KV GB/s (algorithmic bytes / time).  At
 N = 1 the workload is c2, the GPT-OSS-120B-shaped cache: one 65536-token
@@ -26,12 +26,14 @@ the data path, a barrier around the timed region and a MAX all-reduce of
 the timings afterwards.  The workload is fixed as N grows (strong
 scaling); the aggregate counts every rank's bytes.
 
-The same JSON line carries two more sections of the path, each with its own
+The same JSON line carries three more sections of the path, each with its own
 metric, roofline and CPU reference: ``decode_attention`` (c4: paged GQA
 decode with sinks over the compacted cache, batch 128, 36 layers alternating
 sliding-window and full attention; tokens/s) and ``event_compiler`` (c3m: the
 general multi-stage event compiler over 64 multi-turn agent programs,
-1.13M tokens; tokens/s).  ``--workload c4`` / ``--workload c3m`` run one of
+1.13M tokens; tokens/s), and ``prefill_attention`` (c4p: the new turn's
+prefill over the compacted cache with position holes, tensor-bound;
+tokens/s and TFLOP/s).  ``--workload c4`` / ``c3m`` / ``c4p`` run one of
 them alone.
 
 ``--impl reference``: the reference's CPU implementation of the path on the
@@ -67,6 +69,7 @@ WORKLOADS = {
     "c5": (80, 8, 128, "rope500000"),
     "c4": (36, 8, 64, None),  # decode attention only (see bench_attention)
     "c3m": (0, 0, 0, None),   # event compiler only (see bench_compiler)
+    "c4p": (36, 8, 64, None),  # prefill attention only (see bench_prefill)
 }
 
 
@@ -469,6 +472,7 @@ def run_ours(args):
     attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                 max(5, min(args.steps // 20, 20)))
     compiler = bench_compiler(dev, world, rank, 3, 20)
+    prefill = bench_prefill(dev, world, rank, 3, 5)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -512,6 +516,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "decode_attention": attention,
             "event_compiler": compiler,
+            "prefill_attention": prefill,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
@@ -605,6 +610,127 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36):
                      "algorithmic_bytes_per_launch": full_bytes,
                      "ms_per_launch": round(full_ms, 4)},
         "gpu_launches_per_step": layers + (layers // 2 if full.split else 0),
+    }
+
+
+def measured_tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36):
+    """c4p: prefill of a new agent turn over the compacted cache -- 16
+    requests, each a compacted prefix (lognormal length, median 8192, with
+    position holes from dropped tokens) plus 1,024 new tokens; GPT-OSS-120B
+    shape (64 query / 8 KV heads split 8/N per rank, head_dim 64), sinks,
+    36 layers alternating sliding window 128 and full attention.  Tensor
+    bound: FLOPs = 4 * head_dim per visible (query, key, query head)."""
+    from akv_b200 import workloads
+    from akv_b200.context_prefill import ContextPrefillAttention
+
+    bs, new, hq_total, hkv_total, d, window = 16, 1024, 64, 8, 64, 128
+    hkv, hq = hkv_total // world, hq_total // world
+    rng = np.random.default_rng(seed)
+    prefix = workloads.c4_lengths(seed=seed, batch=bs)
+    qo = np.concatenate(([0], np.cumsum([new] * bs))).astype(np.int64)
+    kv = np.concatenate(([0], np.cumsum(prefix))).astype(np.int64)
+    kpos, qpos = [], []
+    for p in prefix:
+        pp = np.cumsum(rng.integers(1, 3, size=int(p))) - 1  # about a third dropped
+        kpos.append(pp)
+        qpos.append((pp[-1] if len(pp) else -1) + 1 + np.arange(new))
+    kpos = np.concatenate(kpos).astype(np.int32)
+    qpos = np.concatenate(qpos).astype(np.int32)
+    n_keys = int(kv[-1] + qo[-1])
+    perm = torch.from_numpy(rng.permutation(n_keys).astype(np.int32)).to(dev)
+    kv_idx, births = perm[: kv[-1]], perm[kv[-1]:]
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    pools = [(torch.randn(n_keys, hkv, d, device=dev, generator=g, dtype=torch.bfloat16),
+              torch.randn(n_keys, hkv, d, device=dev, generator=g, dtype=torch.bfloat16))
+             for _ in range(2)]
+    q = torch.randn(int(qo[-1]), hq, d, device=dev, generator=g, dtype=torch.bfloat16)
+    sinks = torch.randn(hq, device=dev, generator=g)
+    t_qpos = torch.from_numpy(qpos).to(dev)
+    t_kpos = torch.from_numpy(kpos).to(dev)
+    full = ContextPrefillAttention(hq, hkv, d, dev).plan(qo, kv, qpos, kpos, window=-1)
+    swa = ContextPrefillAttention(hq, hkv, d, dev).plan(qo, kv, qpos, kpos, window=window)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+
+    def layer(i):
+        kp, vp = pools[i % 2]
+        (full if i % 2 else swa).run(q, kp, vp, kv_idx, births, t_qpos, t_kpos, sinks=sinks,
+                                     out=out)
+
+    for _ in range(warmup):
+        for i in range(layers):
+            layer(i)
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    ev_full = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for s in range(steps):
+        for i in range(layers):
+            if i == 1:
+                ev_full[s][0].record(stream)
+            layer(i)
+            if i == 1:
+                ev_full[s][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = dist_max(t0.elapsed_time(t1) / steps, world)
+    full_ms = statistics.median(a.elapsed_time(b) for a, b in ev_full)
+    full_flops = 4.0 * d * hq * full.visible
+    step_flops = (layers // 2) * 4.0 * d * hq * (full.visible + swa.visible) * world
+    peak, peak_kind = measured_tensor_peak()
+    achieved = full_flops / (full_ms / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1:
+        # Torch fp32 on the host cores over a bounded sample (the reference
+        # has no CPU path for this kernel): one request, 64 of its queries,
+        # full attention; scaled to the full layer by visible pairs.
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        kq = q[:64].float().cpu()
+        slots = torch.cat((kv_idx[: kv[1]], births[:64])).long()
+        kk = pools[1][0][slots].float().cpu().repeat_interleave(8, dim=1)
+        vv = pools[1][1][slots].float().cpu().repeat_interleave(8, dim=1)
+        n_p = int(kv[1])
+        vis = (torch.arange(n_p + 64)[None, :] < n_p) | \
+            (torch.arange(n_p + 64)[None, :] - n_p <= torch.arange(64)[:, None])
+        t_cpu = time.perf_counter()
+        sc = torch.einsum("qhd,khd->hqk", kq, kk) / np.sqrt(d)
+        sc = sc.masked_fill(~vis[None], float("-inf"))
+        torch.einsum("hqk,khd->qhd", torch.softmax(sc, dim=2), vv)
+        sec = time.perf_counter() - t_cpu
+        pairs = int(vis.sum())
+        cpu = {"value": round(4.0 * d * hq * pairs / sec / 1e12, 4), "unit": "TFLOP/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"torch fp32 CPU, request 0, 64 of its queries x {n_p + 64} keys, "
+                         f"full attention, all {hq} heads"}
+    del pools
+    torch.cuda.empty_cache()
+    return {
+        "metric": "context prefill attention new tokens/s",
+        "value": round(int(qo[-1]) / (ms / 1e3), 1), "unit": "tokens/s",
+        "ms_per_step": round(ms, 4), "n_gpus": world,
+        "tflops": round(step_flops / (ms / 1e3) / 1e12, 1),
+        "config": {"workload": "c4p", "requests": bs, "new_tokens_per_request": new,
+                   "prefix_keys": int(kv[-1]), "q_heads": hq_total, "kv_heads": hkv_total,
+                   "head_dim": d, "layers": layers, "sliding_window": window, "sinks": True,
+                   "positions": "prefix with holes (about a third dropped)"},
+        "roofline": {"bound": "tensor", "kernel": "prefill_attention_kernel (full layer)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "algorithmic_flops_per_launch": full_flops,
+                     "ms_per_launch": round(full_ms, 4)},
+        "gpu_launches_per_step": layers,
+        "cpu_baseline": cpu,
     }
 
 
@@ -703,6 +829,20 @@ def bench_compiler(dev, world, rank, warmup, steps, seed=0):
 
 def main():
     args = parse_args()
+    if args.workload == "c4p" and args.impl == "ours":
+        # Prefill attention alone.
+        world, rank, local = dist_setup()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = bench_prefill(dev, world, rank, max(3, min(args.warmup, 5)),
+                            max(3, min(args.steps, 20)), layers=args.layers or 36)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return 0
     if args.workload == "c3m" and args.impl == "ours":
         # The event compiler alone.
         world, rank, local = dist_setup()
