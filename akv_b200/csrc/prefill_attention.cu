@@ -163,6 +163,8 @@ prefill_attention_kernel(const PrefillParams p) {
   const int pb = vb ? __ldg(p.q_positions + qo0 + qb) : 0;
   // Birth keys a query may see: indices up to its own (j - n_prefix <= q).
   const int ja = n_prefix + qa, jb = n_prefix + qb;
+  // Position of the CTA's newest query (the window test of a whole tile).
+  const int q_last_pos = __ldg(p.q_positions + qo0 + min(qb0 + kQBlock, nq_req) - 1);
 
   float m[2] = {-INFINITY, -INFINITY};  // rows g (query qa) and g + 8 (query qb)
   float l[2] = {0.f, 0.f};
@@ -208,23 +210,41 @@ prefill_attention_kernel(const PrefillParams p) {
     }
 
     // ---- mask, scale, online softmax (rows g: qa, g + 8: qb) ----
+    // A tile whose every key is visible to every query of the CTA (all keys
+    // live, none after the first query's own token, the oldest key inside
+    // the newest query's window) skips the per-element mask.
+    const bool tile_full = j0 + kTK <= key_hi && j0 + kTK - 1 <= n_prefix + qb0 &&
+                           (p.window < 0 || q_last_pos - kpos[0] <= p.window);
     float bm0 = -INFINITY, bm1 = -INFINITY;
+    if (tile_full) {
 #pragma unroll
-    for (int n = 0; n < kTK / 8; ++n) {
+      for (int n = 0; n < kTK / 8; ++n) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int kk = n * 8 + 2 * t + e;
-        const int j = j0 + kk;
-        const int kp = kpos[kk];
-        const bool live = j < key_hi;
-        const bool ok_a = va && live && (j < n_prefix || j <= ja) &&
-                          (p.window < 0 || pa - kp <= p.window);
-        const bool ok_b = vb && live && (j < n_prefix || j <= jb) &&
-                          (p.window < 0 || pb - kp <= p.window);
-        s[n][e] = ok_a ? s[n][e] * p.scale_log2 : -INFINITY;
-        s[n][2 + e] = ok_b ? s[n][2 + e] * p.scale_log2 : -INFINITY;
-        bm0 = fmaxf(bm0, s[n][e]);
-        bm1 = fmaxf(bm1, s[n][2 + e]);
+        for (int e = 0; e < 2; ++e) {
+          s[n][e] *= p.scale_log2;
+          s[n][2 + e] *= p.scale_log2;
+          bm0 = fmaxf(bm0, s[n][e]);
+          bm1 = fmaxf(bm1, s[n][2 + e]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < kTK / 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int kk = n * 8 + 2 * t + e;
+          const int j = j0 + kk;
+          const int kp = kpos[kk];
+          const bool live = j < key_hi;
+          const bool ok_a = va && live && (j < n_prefix || j <= ja) &&
+                            (p.window < 0 || pa - kp <= p.window);
+          const bool ok_b = vb && live && (j < n_prefix || j <= jb) &&
+                            (p.window < 0 || pb - kp <= p.window);
+          s[n][e] = ok_a ? s[n][e] * p.scale_log2 : -INFINITY;
+          s[n][2 + e] = ok_b ? s[n][2 + e] * p.scale_log2 : -INFINITY;
+          bm0 = fmaxf(bm0, s[n][e]);
+          bm1 = fmaxf(bm1, s[n][2 + e]);
+        }
       }
     }
 #pragma unroll
