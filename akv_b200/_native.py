@@ -88,7 +88,7 @@ SIGNATURES = {
     "akv_context_attention_query_block": [],
     "akv_context_attention": [
         _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P,
-        ctypes.c_float, _I64, _I32, _I32, _I32, _P, _I32, _P, _I64, _I64, _P, _P, _P,
+        ctypes.c_float, _I64, _I32, _I32, _I32, _P, _I32, _P, _I64, _I64, _P, _P, _I32, _P,
     ],
 }
 RESTYPES = {

@@ -99,9 +99,11 @@ class ContextPrefillAttention:
         return total
 
     def run(self, q, k_pool, v_pool, kv_indices, birth_slots, q_positions, kv_positions,
-            sinks=None, out=None, lse=None):
+            sinks=None, out=None, lse=None, variant=0):
         """q [tokens, Hq, D] bf16; pools [slots, Hkv, D] bf16; index and
-        position vectors int32 on the device."""
+        position vectors int32 on the device.  ``variant``: 0 the faster
+        kernel for the shape, 1 the mma.sync kernel, 2 the tcgen05 / TMEM
+        kernel (head_dim 64)."""
         if q.dtype != torch.bfloat16 or k_pool.dtype != torch.bfloat16 or \
                 v_pool.dtype != torch.bfloat16:
             raise ValueError("context attention runs on bf16 q / K / V")
@@ -127,7 +129,7 @@ class ContextPrefillAttention:
             _native.ptr(q_positions), _native.ptr(kv_positions), _native.ptr(sinks),
             self.sm_scale, self.window, self.hq, self.hkv, self.d, _native.ptr(self.work),
             self.n_items, _native.ptr(out), out.stride(0), out.stride(1), _native.ptr(lse),
-            _native.ptr(self.error_flag), _native.stream_of(self.device),
+            _native.ptr(self.error_flag), int(variant), _native.stream_of(self.device),
         )
         _native.check(status, "context_attention")
         return out

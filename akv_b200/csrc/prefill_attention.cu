@@ -346,6 +346,428 @@ prefill_attention_kernel(const PrefillParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// 5th-generation tensor cores (tcgen05) for head_dim 64.
+//
+// Same work split (a CTA = 16 queries x 8 heads = 128 rows of one KV head)
+// and the same mask, with the two GEMMs on tcgen05.mma and the accumulators
+// in tensor memory (TMEM): thread r of the 128-thread CTA owns row r, which
+// is TMEM lane r, so the softmax needs no shuffles.
+//   S = Q K^T      kind::f16, M=128 N=64 K=64: A = Q, B = the K tile, both
+//                  from shared memory (K-major, 128-byte swizzle);
+//   O += P V       A = P from TMEM (hi and lo bf16 terms, two MMAs), B = the
+//                  V tile from shared memory (MN-major, 128-byte swizzle).
+// One thread issues the MMAs; tcgen05.commit arrives on an mbarrier that the
+// CTA waits on (bounded: a wait that runs out sets error_flag and the CTA
+// frees its TMEM and returns).  The row max is kept stale unless a tile
+// raises it by more than 2^8, so O is rescaled in TMEM only then.
+// Shared-memory tiles use the XOR swizzle chunk ^ (row & 7) on 128-byte rows
+// from 1024-byte aligned bases, which is the canonical SWIZZLE_128B layout.
+// ---------------------------------------------------------------------------
+constexpr int kTcThreads = 128;
+constexpr int kTcKeys = 64;
+constexpr int kTcStages = 3;
+constexpr int kTcCols = 256;          // TMEM columns per CTA (2 CTAs per SM)
+constexpr int kColS = 0, kColPHi = 64, kColPLo = 96, kColO = 128;
+constexpr int kTcQBytes = 128 * 128;  // Q tile: 128 rows x 64 bf16
+constexpr int kTcKVBytes = kTcKeys * 128;
+constexpr int kTcStageBytes = 2 * kTcKVBytes;
+constexpr int kTcPosOff = kTcQBytes + kTcStages * kTcStageBytes;
+constexpr int kTcBarOff = kTcPosOff + kTcStages * kTcKeys * 4;
+// + alignment slack; at least 80 KB so that no more than two CTAs share an
+// SM, which is all the tensor memory (2 x 256 columns) holds.
+constexpr int kTcSmemUsed = kTcBarOff + 64 + 1024;
+constexpr int kTcSmem = kTcSmemUsed > 80 * 1024 ? kTcSmemUsed : 80 * 1024;
+constexpr float kStaleMax = 8.f;      // log2 headroom before O is rescaled
+constexpr unsigned long long kWaitNs = 100000000ull;  // 100 ms per mbarrier wait
+
+// Shared-memory matrix descriptor, 128-byte swizzle (UMMA canonical layout):
+// start address >> 4, leading offset 16 B (unused for these shapes), stride
+// offset 1024 B between 8-row groups, version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, A
+// K-major, B K-major (b_mn = 0) or MN-major (1), M = 128, N.
+__host__ __device__ constexpr uint32_t f16_idesc(int n, int b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait on an mbarrier phase (kWaitNs of wall time); false when it
+// ran out.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitNs) return false;
+  return true;
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(const PrefillParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  // 1024-byte aligned base for the swizzled tiles.
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* smem = smem_raw + (base - raw);
+  const uint32_t sQ = base;
+  const uint32_t bar_s = base + kTcBarOff, bar_o = bar_s + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTcBarOff + 16);
+  __shared__ int s_abort;
+
+  const int4 w = p.work[blockIdx.x];
+  const int hk = blockIdx.y;
+  const int b = w.x, qb0 = w.y, key_lo = w.z, key_hi = w.w;
+  const int qo0 = p.qo_indptr[b], nq_req = p.qo_indptr[b + 1] - qo0;
+  const int kv0 = p.kv_indptr[b], n_prefix = p.kv_indptr[b + 1] - kv0;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int n_tiles = (key_hi - key_lo + kTcKeys - 1) / kTcKeys;
+  // After a wait ran out anywhere in the grid, later CTAs do nothing.
+  if (p.error_flag != nullptr && *reinterpret_cast<volatile int*>(p.error_flag) == 2) return;
+
+  if (warp == 0) {  // TMEM for S, P (hi, lo) and O
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTcCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_abort = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
+
+  // ---- key gather: two threads per key, four 16-byte chunks each of K and V ----
+  auto key_slot_pos = [&](int j, long long& slot, int& pos) {
+    if (j < n_prefix) {
+      slot = __ldg(p.kv_indices + kv0 + j);
+      pos = __ldg(p.kv_positions + kv0 + j);
+    } else {
+      slot = __ldg(p.birth_slots + qo0 + (j - n_prefix));
+      pos = __ldg(p.q_positions + qo0 + (j - n_prefix));
+    }
+    if (slot < 0 || slot >= p.num_slots) {
+      if (p.error_flag) *p.error_flag = 1;
+      slot = 0;
+    }
+  };
+  const int my_key = tid >> 1, my_half = tid & 1;
+  struct KeyRef {
+    long long slot;
+    int pos;
+  };
+  auto fetch = [&](int tile) -> KeyRef {
+    KeyRef r{0, INT_MAX};
+    const int j = key_lo + tile * kTcKeys + my_key;
+    if (tile < n_tiles && j < key_hi) key_slot_pos(j, r.slot, r.pos);
+    return r;
+  };
+  auto issue_tile = [&](int stage, const KeyRef r) {
+    const uint32_t kb = base + kTcQBytes + stage * kTcStageBytes, vb = kb + kTcKVBytes;
+    int* kpos = reinterpret_cast<int*>(smem + kTcPosOff + stage * kTcKeys * 4);
+    if (my_half == 0) kpos[my_key] = r.pos;
+    const int bytes = r.pos != INT_MAX ? 16 : 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = my_half * 4 + i;
+      const uint32_t off = my_key * 128 + ((c ^ (my_key & 7)) * 16);
+      cp_async16(kb + off, p.k + r.slot * p.k_ss + hk * p.k_sh + c * 8, bytes);
+      cp_async16(vb + off, p.v + r.slot * p.v_ss + hk * p.v_sh + c * 8, bytes);
+    }
+  };
+
+  // ---- Q: thread r loads row r = (query r / 8, head r % 8) ----
+  const int q_local = qb0 + (tid >> 3);
+  const int head = hk * kGroupP + (tid & 7);
+  const bool row_valid = q_local < nq_req;
+  {
+    const __nv_bfloat16* src = p.q + (long long)(qo0 + (row_valid ? q_local : 0)) * p.q_st +
+                               (long long)head * p.q_sh;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      cp_async16(sQ + tid * 128 + ((c ^ (tid & 7)) * 16), src + c * 8, row_valid ? 16 : 0);
+  }
+#pragma unroll
+  for (int s = 0; s < kTcStages - 1; ++s) {
+    if (s < n_tiles) issue_tile(s, fetch(s));
+    cp_async_commit();  // group s (group 0 also holds Q)
+  }
+  KeyRef next = fetch(kTcStages - 1);
+
+  // O = 0 in TMEM (every MMA then accumulates).
+  {
+    uint32_t z[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) z[i] = 0u;
+    tmem_st32(trow + kColO, z);
+    tmem_st32(trow + kColO + 32, z);
+    tmem_wait_st();
+  }
+  const int pq = row_valid ? __ldg(p.q_positions + qo0 + q_local) : 0;
+  const int jq = n_prefix + q_local;
+  const int q_last_pos = __ldg(p.q_positions + qo0 + min(qb0 + kQBlock, nq_req) - 1);
+  float m_used = -INFINITY, l = 0.f;
+  uint32_t phase_s = 0, phase_o = 0;
+  bool timed_out = false;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int st = tile % kTcStages;
+    if (tile + 1 < n_tiles) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    fence_async_smem();  // this thread's copies -> visible to the tensor cores
+    tc_fence_before();
+    __syncthreads();
+    const uint32_t kb = base + kTcQBytes + st * kTcStageBytes, vb = kb + kTcKVBytes;
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < 4; ++k)  // K = 64 dims in 4 steps of 16 (32 bytes)
+        mma_ss(tmem + kColS, sw128_desc(sQ + 32 * k), sw128_desc(kb + 32 * k),
+               f16_idesc(kTcKeys, 0), k > 0);
+      umma_commit(bar_s);
+    }
+    timed_out |= !mbar_wait(bar_s, phase_s);
+    phase_s ^= 1;
+    tc_fence_after();
+
+    // ---- softmax over this row's 64 keys ----
+    float s[kTcKeys];
+    tmem_ld32(trow + kColS, s);
+    tmem_ld32(trow + kColS + 32, s + 32);
+    tmem_wait_ld();
+    const int j0 = key_lo + tile * kTcKeys;
+    const int* kpos = reinterpret_cast<const int*>(smem + kTcPosOff + st * kTcKeys * 4);
+    const bool tile_full = j0 + kTcKeys <= key_hi && j0 + kTcKeys - 1 <= n_prefix + qb0 &&
+                           (p.window < 0 || q_last_pos - kpos[0] <= p.window);
+    float bm = -INFINITY;
+#pragma unroll
+    for (int kk = 0; kk < kTcKeys; ++kk) {
+      bool ok = row_valid;
+      if (!tile_full) {
+        const int j = j0 + kk;
+        ok = ok && j < key_hi && (j < n_prefix || j <= jq) &&
+             (p.window < 0 || pq - kpos[kk] <= p.window);
+      }
+      s[kk] = ok ? s[kk] * p.scale_log2 : -INFINITY;
+      bm = fmaxf(bm, s[kk]);
+    }
+    // Keep the exponent base unless this tile exceeds it by 2^8 (or it is
+    // unset); rescale O and l only then.
+    float alpha = 1.f;
+    bool rescale = false;
+    if (bm > m_used + kStaleMax || (m_used == -INFINITY && bm != -INFINITY)) {
+      alpha = m_used == -INFINITY ? 0.f : fast_exp2(m_used - bm);
+      rescale = m_used != -INFINITY;
+      m_used = bm;
+    }
+    const float base2 = m_used == -INFINITY ? 0.f : m_used;
+    uint32_t hi[kTcKeys / 2], lo[kTcKeys / 2];
+    float rs = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kTcKeys; kk += 2) {
+      const float e0 = fast_exp2(s[kk] - base2), e1 = fast_exp2(s[kk + 1] - base2);
+      rs += e0 + e1;
+      split_bf16(e0, e1, hi[kk / 2], lo[kk / 2]);
+    }
+    l = l * alpha + rs;
+
+    // The previous tile's P.V must be done before P and O are rewritten.
+    if (tile > 0) {
+      timed_out |= !mbar_wait(bar_o, phase_o);
+      phase_o ^= 1;
+      tc_fence_after();
+    }
+    // Refill the stage the previous tile used (its P.V has completed).
+    {
+      const int nt = tile + kTcStages - 1;
+      if (nt < n_tiles) {
+        issue_tile(nt % kTcStages, next);
+        next = fetch(nt + 1);
+      }
+      cp_async_commit();
+    }
+    // tcgen05.ld / st are warp-wide: a warp rescales when any of its rows must
+    // (alpha stays 1 for the others).
+    if (__any_sync(0xffffffffu, rescale)) {
+      float o[32];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        tmem_ld32(trow + kColO + 32 * h2, o);
+        tmem_wait_ld();
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
+        tmem_st32(trow + kColO + 32 * h2, r);
+      }
+    }
+    tmem_st16(trow + kColPHi, hi);
+    tmem_st16(trow + kColPHi + 16, hi + 16);
+    tmem_st16(trow + kColPLo, lo);
+    tmem_st16(trow + kColPLo + 16, lo + 16);
+    tmem_wait_st();
+    tc_fence_before();
+    if (__syncthreads_or(timed_out)) {
+      if (tid == 0) s_abort = 1;
+      break;
+    }
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int k = 0; k < kTcKeys / 16; ++k) {  // 16 keys per step: 8 TMEM columns, 2 KiB of V
+        mma_ts(tmem + kColO, tmem + kColPHi + 8 * k, sw128_desc(vb + 2048 * k),
+               f16_idesc(64, 1), 1);
+        mma_ts(tmem + kColO, tmem + kColPLo + 8 * k, sw128_desc(vb + 2048 * k),
+               f16_idesc(64, 1), 1);
+      }
+      umma_commit(bar_o);
+    }
+  }
+  cp_async_wait<0>();
+
+  // ---- epilogue ----
+  __syncthreads();
+  if (!s_abort && n_tiles > 0) {
+    timed_out |= !mbar_wait(bar_o, phase_o);
+    tc_fence_after();
+  }
+  const bool failed = __syncthreads_or(timed_out || s_abort);  // uniform over the CTA
+  if (failed && tid == 0 && p.error_flag) *p.error_flag = 2;
+  if (!failed) {
+    float o[64];
+    tmem_ld32(trow + kColO, o);  // every thread: the load is warp-wide
+    tmem_ld32(trow + kColO + 32, o + 32);
+    tmem_wait_ld();
+    float den = l;
+    const float mb = m_used == -INFINITY ? 0.f : m_used;
+    if (p.sinks) den += fast_exp2(p.sinks[head] * kLog2e - mb);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    __nv_bfloat16* dst = p.out + (long long)(qo0 + q_local) * p.o_st + (long long)head * p.o_sh;
+#pragma unroll
+    for (int c = 0; c < 8 && row_valid; ++c) {
+      uint4 v;
+      v.x = pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv);
+      v.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+      v.z = pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+      v.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+      *reinterpret_cast<uint4*>(dst + 8 * c) = v;
+    }
+    if (p.lse && row_valid)
+      p.lse[(long long)(qo0 + q_local) * p.num_q_heads + head] =
+          den > 0.f ? (mb + log2f(den)) * kLn2 : -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTcCols));
+  }
+}
+
+int launch_prefill_tc(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
+  if (cudaFuncSetAttribute(prefill_attention_tc_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
+    return AKV_ERR_CUDA;
+  if (n_items > 0)
+    prefill_attention_tc_kernel<<<dim3(n_items, num_kv_heads), kTcThreads, kTcSmem, s>>>(p);
+  return launch_status();
+}
+
 template <int D>
 int launch_prefill(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
   using C = PCfg<D>;
@@ -370,7 +792,7 @@ extern "C" int akv_context_attention(
     const int32_t* kv_positions, const float* sinks, float sm_scale, int64_t window,
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const int32_t* work,
     int32_t n_items, void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
-    int32_t* error_flag, void* stream) {
+    int32_t* error_flag, int32_t variant, void* stream) {
   using namespace akv;
   if (n_items < 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads * kGroupP ||
       num_kv_heads > 65535 || num_slots <= 0)
@@ -413,6 +835,16 @@ extern "C" int akv_context_attention(
   p.num_q_heads = num_q_heads;
   p.error_flag = error_flag;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // tcgen05 path: head_dim 64 with 16-byte aligned q / out rows.
+  const bool aligned16 = (reinterpret_cast<uintptr_t>(q) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(out) & 15) == 0 && q_stride_token % 8 == 0 &&
+                         q_stride_head % 8 == 0 && out_stride_token % 8 == 0 &&
+                         out_stride_head % 8 == 0;
+  if (variant < 0 || variant > 2) return AKV_ERR_INVALID;
+  if (variant == 2) {
+    if (head_dim != 64 || !aligned16) return AKV_ERR_UNSUPPORTED;
+    return launch_prefill_tc(p, n_items, num_kv_heads, s);
+  }
   switch (head_dim) {
     case 64: return launch_prefill<64>(p, n_items, num_kv_heads, s);
     case 128: return launch_prefill<128>(p, n_items, num_kv_heads, s);

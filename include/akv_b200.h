@@ -398,6 +398,11 @@ int akv_decode_attention(
  * (key_hi = P_b + last query + 1; key_lo = first key the window can reach);
  * built on the host from the CPU positions (akv_b200/context_prefill.py).
  * A slot outside [0, num_slots) is read as slot 0 and sets *error_flag.
+ * variant: 0 = the faster kernel for the shape (currently mma.sync), 1 =
+ * the mma.sync kernel, 2 = the tcgen05 / TMEM kernel (head_dim 64 with
+ * 16-byte aligned q and out rows; AKV_ERR_UNSUPPORTED otherwise).  A tcgen05
+ * wait that does not complete sets *error_flag to 2 (the CTA frees its
+ * tensor memory and returns).
  */
 int64_t akv_context_attention_query_block(void);
 int akv_context_attention(
@@ -408,7 +413,7 @@ int akv_context_attention(
     const int32_t* kv_positions, const float* sinks, float sm_scale, int64_t window,
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const int32_t* work,
     int32_t n_items, void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
-    int32_t* error_flag, void* stream);
+    int32_t* error_flag, int32_t variant, void* stream);
 
 /* Resident CTAs per SM of akv_decode_attention for this shape (the size of
  * a persistent launch is this times the SM count); a negative AKV_* status

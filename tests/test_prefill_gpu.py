@@ -74,7 +74,7 @@ def torch_reference(x, window, sinks, scale):
     return out
 
 
-def run_ours(x, hkv, d, window, sinks, lse=None):
+def run_ours(x, hkv, d, window, sinks, lse=None, variant=0):
     from akv_b200.context_prefill import ContextPrefillAttention
 
     dev = x["q"].device
@@ -82,7 +82,7 @@ def run_ours(x, hkv, d, window, sinks, lse=None):
         x["qo"], x["kv"], x["qpos"], x["kpos"], window=window)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)  # noqa: E731
     out = att.run(x["q"], x["k_pool"], x["v_pool"], t(x["kv_idx"]), t(x["births"]),
-                  t(x["qpos"]), t(x["kpos"]), sinks=sinks, lse=lse)
+                  t(x["qpos"]), t(x["kpos"]), sinks=sinks, lse=lse, variant=variant)
     torch.cuda.synchronize()
     assert int(att.error_flag.item()) == 0
     return out, att
@@ -100,14 +100,18 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("variant", [0, 1, 2], ids=["auto", "mma_sync", "tcgen05"])
 @pytest.mark.parametrize("case", range(len(CASES)))
-def test_prefill_matches_torch(case):
+def test_prefill_matches_torch(case, variant):
+    """variant 1 runs the mma.sync kernel, 2 the tcgen05 one (head_dim 64)."""
     prefix, queries, hkv, d, window, use_sinks = CASES[case]
+    if variant == 2 and d != 64:
+        pytest.skip("the tcgen05 kernel covers head_dim 64")
     rng = np.random.default_rng(case)
     x = make_batch(rng, prefix, queries, hkv, d)
     sinks = torch.randn(8 * hkv, device="cuda") if use_sinks else None
     scale = 1.0 / np.sqrt(d)
-    out, _ = run_ours(x, hkv, d, window, sinks)
+    out, _ = run_ours(x, hkv, d, window, sinks, variant=variant)
     want = torch_reference(x, window, sinks, scale)
     torch.testing.assert_close(out.float(), want, atol=ATOL, rtol=RTOL)
 
@@ -120,7 +124,7 @@ def test_prefill_matches_float64_oracle_with_lse():
     x = make_batch(rng, [150, 40], [37, 20], hkv, d)
     sinks = torch.randn(8 * hkv, device="cuda")
     lse = torch.empty(x["q"].shape[0], 8 * hkv, device="cuda")
-    out, _ = run_ours(x, hkv, d, window, sinks, lse=lse)
+    out, _ = run_ours(x, hkv, d, window, sinks, lse=lse, variant=2)  # tcgen05
     want, want_lse = oracle.prefill_attention(
         x["q"].float().cpu().numpy(), x["k_pool"].float().cpu().numpy(),
         x["v_pool"].float().cpu().numpy(), x["qo"], x["kv"], x["kv_idx"], x["births"],
