@@ -364,16 +364,17 @@ prefill_attention_kernel(const PrefillParams p) {
 // Shared-memory tiles use the XOR swizzle chunk ^ (row & 7) on 128-byte rows
 // from 1024-byte aligned bases, which is the canonical SWIZZLE_128B layout.
 // ---------------------------------------------------------------------------
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 256;   // two warps per 32 rows: one per column half
 constexpr int kTcKeys = 64;
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 5;        // K/V tiles in flight: loads run 4 tiles ahead
 constexpr int kTcCols = 256;          // TMEM columns per CTA (2 CTAs per SM)
-constexpr int kColS = 0, kColPHi = 64, kColPLo = 96, kColO = 128;
+constexpr int kColS = 0, kColPHi = 128, kColPLo = 160, kColO = 192;  // S: two buffers
 constexpr int kTcQBytes = 128 * 128;  // Q tile: 128 rows x 64 bf16
 constexpr int kTcKVBytes = kTcKeys * 128;
 constexpr int kTcStageBytes = 2 * kTcKVBytes;
 constexpr int kTcPosOff = kTcQBytes + kTcStages * kTcStageBytes;
-constexpr int kTcBarOff = kTcPosOff + kTcStages * kTcKeys * 4;
+constexpr int kTcRowOff = kTcPosOff + kTcStages * kTcKeys * 4;  // half-row max / sum
+constexpr int kTcBarOff = kTcRowOff + 4 * 128 * 4;
 // + alignment slack; at least 80 KB so that no more than two CTAs share an
 // SM, which is all the tensor memory (2 x 256 columns) holds.
 constexpr int kTcSmemUsed = kTcBarOff + 64 + 1024;
@@ -500,8 +501,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* smem = smem_raw + (base - raw);
   const uint32_t sQ = base;
-  const uint32_t bar_s = base + kTcBarOff, bar_o = bar_s + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTcBarOff + 16);
+  const uint32_t bar_s0 = base + kTcBarOff, bar_o = bar_s0 + 16;  // bar_s0, bar_s0 + 8: S buffers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kTcBarOff + 24);
+  float* s_max = reinterpret_cast<float*>(smem + kTcRowOff);      // [2][128] half-row maxima
+  float* s_sum = s_max + 2 * 128;                                  // [2][128] half-row sums
   __shared__ int s_abort;
 
   const int4 w = p.work[blockIdx.x];
@@ -509,19 +512,22 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   const int b = w.x, qb0 = w.y, key_lo = w.z, key_hi = w.w;
   const int qo0 = p.qo_indptr[b], nq_req = p.qo_indptr[b + 1] - qo0;
   const int kv0 = p.kv_indptr[b], n_prefix = p.kv_indptr[b + 1] - kv0;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Warp w serves TMEM lanes 32 * (w % 4) .. (its rows) and column half w / 4.
+  const int row = ((warp & 3) << 5) | lane, half = warp >> 2;
   const int n_tiles = (key_hi - key_lo + kTcKeys - 1) / kTcKeys;
   // After a wait ran out anywhere in the grid, later CTAs do nothing.
   if (p.error_flag != nullptr && *reinterpret_cast<volatile int*>(p.error_flag) == 2) return;
 
-  if (warp == 0) {  // TMEM for S, P (hi, lo) and O
+  if (warp == 0) {  // TMEM: two S buffers, P (hi, lo) and O
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTcCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(bar_s, 1);
+    mbar_init(bar_s0, 1);
+    mbar_init(bar_s0 + 8, 1);
     mbar_init(bar_o, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
@@ -530,9 +536,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
+  const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lanes
 
-  // ---- key gather: two threads per key, four 16-byte chunks each of K and V ----
+  // ---- key gather: four threads per key, two 16-byte chunks each of K and V ----
   auto key_slot_pos = [&](int j, long long& slot, int& pos) {
     if (j < n_prefix) {
       slot = __ldg(p.kv_indices + kv0 + j);
@@ -546,7 +552,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
       slot = 0;
     }
   };
-  const int my_key = tid >> 1, my_half = tid & 1;
+  const int my_key = tid >> 2, my_quarter = tid & 3;
   struct KeyRef {
     long long slot;
     int pos;
@@ -557,97 +563,119 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
     if (tile < n_tiles && j < key_hi) key_slot_pos(j, r.slot, r.pos);
     return r;
   };
-  auto issue_tile = [&](int stage, const KeyRef r) {
-    const uint32_t kb = base + kTcQBytes + stage * kTcStageBytes, vb = kb + kTcKVBytes;
-    int* kpos = reinterpret_cast<int*>(smem + kTcPosOff + stage * kTcKeys * 4);
-    if (my_half == 0) kpos[my_key] = r.pos;
+  auto stage_k = [&](int tile) { return base + kTcQBytes + (tile % kTcStages) * kTcStageBytes; };
+  auto issue_tile = [&](int tile, const KeyRef r) {
+    const uint32_t kb = stage_k(tile), vb = kb + kTcKVBytes;
+    int* kpos = reinterpret_cast<int*>(smem + kTcPosOff + (tile % kTcStages) * kTcKeys * 4);
+    if (my_quarter == 0) kpos[my_key] = r.pos;
     const int bytes = r.pos != INT_MAX ? 16 : 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int c = my_half * 4 + i;
+    for (int i = 0; i < 2; ++i) {
+      const int c = my_quarter * 2 + i;
       const uint32_t off = my_key * 128 + ((c ^ (my_key & 7)) * 16);
       cp_async16(kb + off, p.k + r.slot * p.k_ss + hk * p.k_sh + c * 8, bytes);
       cp_async16(vb + off, p.v + r.slot * p.v_ss + hk * p.v_sh + c * 8, bytes);
     }
   };
+  // S(t) = Q K(t)^T into S buffer t & 1 (called by one thread).
+  auto issue_s = [&](int tile) {
+    const uint32_t kb = stage_k(tile);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)  // K = 64 dims in 4 steps of 16 (32 bytes)
+      mma_ss(tmem + kColS + (tile & 1) * kTcKeys, sw128_desc(sQ + 32 * k),
+             sw128_desc(kb + 32 * k), f16_idesc(kTcKeys, 0), k > 0);
+    umma_commit(bar_s0 + 8 * (tile & 1));
+  };
 
-  // ---- Q: thread r loads row r = (query r / 8, head r % 8) ----
-  const int q_local = qb0 + (tid >> 3);
-  const int head = hk * kGroupP + (tid & 7);
+  // ---- Q: row r = (query r / 8, head r % 8); two threads per row, four chunks each ----
+  const int q_local = qb0 + (row >> 3);
+  const int head = hk * kGroupP + (row & 7);
   const bool row_valid = q_local < nq_req;
   {
     const __nv_bfloat16* src = p.q + (long long)(qo0 + (row_valid ? q_local : 0)) * p.q_st +
                                (long long)head * p.q_sh;
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-      cp_async16(sQ + tid * 128 + ((c ^ (tid & 7)) * 16), src + c * 8, row_valid ? 16 : 0);
+    for (int i = 0; i < 4; ++i) {
+      const int c = half * 4 + i;
+      cp_async16(sQ + row * 128 + ((c ^ (row & 7)) * 16), src + c * 8, row_valid ? 16 : 0);
+    }
   }
+  // Groups: Q + tile 0, then tiles 1 .. kTcStages - 2, one group each.
 #pragma unroll
-  for (int s = 0; s < kTcStages - 1; ++s) {
-    if (s < n_tiles) issue_tile(s, fetch(s));
-    cp_async_commit();  // group s (group 0 also holds Q)
+  for (int t = 0; t < kTcStages - 1; ++t) {
+    if (t < n_tiles) issue_tile(t, fetch(t));
+    cp_async_commit();
   }
   KeyRef next = fetch(kTcStages - 1);
 
-  // O = 0 in TMEM (every MMA then accumulates).
+  // O = 0 in TMEM (every P.V then accumulates); this warp's 32 columns.
   {
     uint32_t z[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) z[i] = 0u;
-    tmem_st32(trow + kColO, z);
-    tmem_st32(trow + kColO + 32, z);
+    tmem_st32(trow + kColO + 32 * half, z);
     tmem_wait_st();
   }
+  // S(0) as soon as Q and tile 0 have landed.
+  cp_async_wait<kTcStages - 2>();
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && n_tiles > 0) {
+    tc_fence_after();
+    issue_s(0);
+  }
+
   const int pq = row_valid ? __ldg(p.q_positions + qo0 + q_local) : 0;
   const int jq = n_prefix + q_local;
   const int q_last_pos = __ldg(p.q_positions + qo0 + min(qb0 + kQBlock, nq_req) - 1);
-  float m_used = -INFINITY, l = 0.f;
-  uint32_t phase_s = 0, phase_o = 0;
+  float m_used = -INFINITY, l = 0.f;  // l: this thread's half of the row sum
+  uint32_t phase_s[2] = {0u, 0u}, phase_o = 0u;
   bool timed_out = false;
+  constexpr int kHalf = kTcKeys / 2;
 
   for (int tile = 0; tile < n_tiles; ++tile) {
-    const int st = tile % kTcStages;
-    if (tile + 1 < n_tiles) cp_async_wait<1>();
-    else cp_async_wait<0>();
-    fence_async_smem();  // this thread's copies -> visible to the tensor cores
-    tc_fence_before();
-    __syncthreads();
-    const uint32_t kb = base + kTcQBytes + st * kTcStageBytes, vb = kb + kTcKVBytes;
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int k = 0; k < 4; ++k)  // K = 64 dims in 4 steps of 16 (32 bytes)
-        mma_ss(tmem + kColS, sw128_desc(sQ + 32 * k), sw128_desc(kb + 32 * k),
-               f16_idesc(kTcKeys, 0), k > 0);
-      umma_commit(bar_s);
-    }
-    timed_out |= !mbar_wait(bar_s, phase_s);
-    phase_s ^= 1;
+    // 1. S(t) done -> this thread's 32 values of its row.
+    timed_out |= !mbar_wait(bar_s0 + 8 * (tile & 1), phase_s[tile & 1]);
+    phase_s[tile & 1] ^= 1u;
     tc_fence_after();
-
-    // ---- softmax over this row's 64 keys ----
-    float s[kTcKeys];
-    tmem_ld32(trow + kColS, s);
-    tmem_ld32(trow + kColS + 32, s + 32);
+    float s[kHalf];
+    tmem_ld32(trow + kColS + (tile & 1) * kTcKeys + half * kHalf, s);
     tmem_wait_ld();
+
+    // 2. Mask and scale; half-row maximum to shared memory.
     const int j0 = key_lo + tile * kTcKeys;
-    const int* kpos = reinterpret_cast<const int*>(smem + kTcPosOff + st * kTcKeys * 4);
+    const int* kpos =
+        reinterpret_cast<const int*>(smem + kTcPosOff + (tile % kTcStages) * kTcKeys * 4);
     const bool tile_full = j0 + kTcKeys <= key_hi && j0 + kTcKeys - 1 <= n_prefix + qb0 &&
                            (p.window < 0 || q_last_pos - kpos[0] <= p.window);
-    float bm = -INFINITY;
+    float hm = -INFINITY;
 #pragma unroll
-    for (int kk = 0; kk < kTcKeys; ++kk) {
+    for (int i = 0; i < kHalf; ++i) {
       bool ok = row_valid;
       if (!tile_full) {
-        const int j = j0 + kk;
+        const int kk = half * kHalf + i, j = j0 + kk;
         ok = ok && j < key_hi && (j < n_prefix || j <= jq) &&
              (p.window < 0 || pq - kpos[kk] <= p.window);
       }
-      s[kk] = ok ? s[kk] * p.scale_log2 : -INFINITY;
-      bm = fmaxf(bm, s[kk]);
+      s[i] = ok ? s[i] * p.scale_log2 : -INFINITY;
+      hm = fmaxf(hm, s[i]);
     }
-    // Keep the exponent base unless this tile exceeds it by 2^8 (or it is
-    // unset); rescale O and l only then.
+    s_max[half * 128 + row] = hm;
+
+    // 3. Tile t+1 landed -> S(t+1) on the tensor cores during this softmax.
+    if (tile + 1 < n_tiles) cp_async_wait<kTcStages - 3>();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && tile + 1 < n_tiles) {
+      tc_fence_after();
+      issue_s(tile + 1);
+    }
+
+    // 4. Exponentials against the row's base; the base only moves when the
+    //    tile exceeds it by 2^8, and then O and l are rescaled.
+    const float bm = fmaxf(s_max[row], s_max[128 + row]);
     float alpha = 1.f;
     bool rescale = false;
     if (bm > m_used + kStaleMax || (m_used == -INFINITY && bm != -INFINITY)) {
@@ -656,57 +684,53 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
       m_used = bm;
     }
     const float base2 = m_used == -INFINITY ? 0.f : m_used;
-    uint32_t hi[kTcKeys / 2], lo[kTcKeys / 2];
+    uint32_t hi[kHalf / 2], lo[kHalf / 2];
     float rs = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < kTcKeys; kk += 2) {
-      const float e0 = fast_exp2(s[kk] - base2), e1 = fast_exp2(s[kk + 1] - base2);
+    for (int i = 0; i < kHalf; i += 2) {
+      const float e0 = fast_exp2(s[i] - base2), e1 = fast_exp2(s[i + 1] - base2);
       rs += e0 + e1;
-      split_bf16(e0, e1, hi[kk / 2], lo[kk / 2]);
+      split_bf16(e0, e1, hi[i / 2], lo[i / 2]);
     }
     l = l * alpha + rs;
 
-    // The previous tile's P.V must be done before P and O are rewritten.
+    // 5. P(t-1).V done: P and O may be rewritten, the stage of tile t-1 refilled.
     if (tile > 0) {
       timed_out |= !mbar_wait(bar_o, phase_o);
-      phase_o ^= 1;
+      phase_o ^= 1u;
       tc_fence_after();
     }
-    // Refill the stage the previous tile used (its P.V has completed).
     {
-      const int nt = tile + kTcStages - 1;
+      const int nt = tile + kTcStages - 1;  // into the stage tile t-1 used
       if (nt < n_tiles) {
-        issue_tile(nt % kTcStages, next);
+        issue_tile(nt, next);
         next = fetch(nt + 1);
       }
       cp_async_commit();
     }
-    // tcgen05.ld / st are warp-wide: a warp rescales when any of its rows must
-    // (alpha stays 1 for the others).
+    // 6. Rescale this warp's half of O, write its half of P (tcgen05.ld / st
+    //    are warp-wide: a warp rescales when any of its rows must).
     if (__any_sync(0xffffffffu, rescale)) {
       float o[32];
+      tmem_ld32(trow + kColO + 32 * half, o);
+      tmem_wait_ld();
+      uint32_t r[32];
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        tmem_ld32(trow + kColO + 32 * h2, o);
-        tmem_wait_ld();
-        uint32_t r[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
-        tmem_st32(trow + kColO + 32 * h2, r);
-      }
+      for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
+      tmem_st32(trow + kColO + 32 * half, r);
     }
-    tmem_st16(trow + kColPHi, hi);
-    tmem_st16(trow + kColPHi + 16, hi + 16);
-    tmem_st16(trow + kColPLo, lo);
-    tmem_st16(trow + kColPLo + 16, lo + 16);
+    tmem_st16(trow + kColPHi + half * (kHalf / 2), hi);
+    tmem_st16(trow + kColPLo + half * (kHalf / 2), lo);
     tmem_wait_st();
     tc_fence_before();
     if (__syncthreads_or(timed_out)) {
       if (tid == 0) s_abort = 1;
       break;
     }
+    // 7. O += P(t) V(t).
     if (tid == 0) {
       tc_fence_after();
+      const uint32_t vb = stage_k(tile) + kTcKVBytes;
 #pragma unroll
       for (int k = 0; k < kTcKeys / 16; ++k) {  // 16 keys per step: 8 TMEM columns, 2 KiB of V
         mma_ts(tmem + kColO, tmem + kColPHi + 8 * k, sw128_desc(vb + 2048 * k),
@@ -720,6 +744,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   cp_async_wait<0>();
 
   // ---- epilogue ----
+  s_sum[half * 128 + row] = l;
   __syncthreads();
   if (!s_abort && n_tiles > 0) {
     timed_out |= !mbar_wait(bar_o, phase_o);
@@ -728,17 +753,17 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   const bool failed = __syncthreads_or(timed_out || s_abort);  // uniform over the CTA
   if (failed && tid == 0 && p.error_flag) *p.error_flag = 2;
   if (!failed) {
-    float o[64];
-    tmem_ld32(trow + kColO, o);  // every thread: the load is warp-wide
-    tmem_ld32(trow + kColO + 32, o + 32);
+    float o[32];
+    tmem_ld32(trow + kColO + 32 * half, o);  // every thread: the load is warp-wide
     tmem_wait_ld();
-    float den = l;
+    float den = s_sum[row] + s_sum[128 + row];
     const float mb = m_used == -INFINITY ? 0.f : m_used;
     if (p.sinks) den += fast_exp2(p.sinks[head] * kLog2e - mb);
     const float inv = den > 0.f ? 1.f / den : 0.f;
-    __nv_bfloat16* dst = p.out + (long long)(qo0 + q_local) * p.o_st + (long long)head * p.o_sh;
+    __nv_bfloat16* dst = p.out + (long long)(qo0 + q_local) * p.o_st + (long long)head * p.o_sh +
+                         32 * half;
 #pragma unroll
-    for (int c = 0; c < 8 && row_valid; ++c) {
+    for (int c = 0; c < 4 && row_valid; ++c) {
       uint4 v;
       v.x = pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv);
       v.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
@@ -746,7 +771,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
       v.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
       *reinterpret_cast<uint4*>(dst + 8 * c) = v;
     }
-    if (p.lse && row_valid)
+    if (p.lse && row_valid && half == 0)
       p.lse[(long long)(qo0 + q_local) * p.num_q_heads + head] =
           den > 0.f ? (mb + log2f(den)) * kLn2 : -INFINITY;
   }

@@ -622,7 +622,7 @@ def measured_tensor_peak():
         return 1590.0, "fallback"
 
 
-def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36):
+def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0):
     """c4p: prefill of a new agent turn over the compacted cache -- 16
     requests, each a compacted prefix (lognormal length, median 8192, with
     position holes from dropped tokens) plus 1,024 new tokens; GPT-OSS-120B
@@ -664,7 +664,7 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36):
     def layer(i):
         kp, vp = pools[i % 2]
         (full if i % 2 else swa).run(q, kp, vp, kv_idx, births, t_qpos, t_kpos, sinks=sinks,
-                                     out=out)
+                                     out=out, variant=variant)
 
     for _ in range(warmup):
         for i in range(layers):
