@@ -82,6 +82,8 @@ def parse_args():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     p.add_argument("--layers", type=int, default=None,
                    help="override the workload's layer count (a smaller cut for ncu captures)")
+    p.add_argument("--variant", type=int, default=0,
+                   help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05)")
     return p.parse_args()
 
 
@@ -720,7 +722,8 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0)
         "value": round(int(qo[-1]) / (ms / 1e3), 1), "unit": "tokens/s",
         "ms_per_step": round(ms, 4), "n_gpus": world,
         "tflops": round(step_flops / (ms / 1e3) / 1e12, 1),
-        "config": {"workload": "c4p", "requests": bs, "new_tokens_per_request": new,
+        "config": {"workload": "c4p", "kernel_variant": variant, "requests": bs,
+                   "new_tokens_per_request": new,
                    "prefix_keys": int(kv[-1]), "q_heads": hq_total, "kv_heads": hkv_total,
                    "head_dim": d, "layers": layers, "sliding_window": window, "sinks": True,
                    "positions": "prefix with holes (about a third dropped)"},
@@ -835,7 +838,8 @@ def main():
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         res = bench_prefill(dev, world, rank, max(3, min(args.warmup, 5)),
-                            max(3, min(args.steps, 20)), layers=args.layers or 36)
+                            max(3, min(args.steps, 20)), layers=args.layers or 36,
+                            variant=args.variant)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
