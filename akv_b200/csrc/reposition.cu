@@ -408,8 +408,8 @@ __device__ __forceinline__ long long copy_dst(const UnitGeom& g, int c, int rot,
 template <typename T, bool NEOX, int V>
 __device__ void unit_direct(const RepositionParams& p, const unsigned long long* s_k,
                             const unsigned long long* s_v, const bool* s_vec, const UnitGeom& g,
-                            const Trig<V>& tr) {
-  for (int l = 0; l < p.n_layers; ++l) {
+                            const Trig<V>& tr, int l0, int l1) {
+  for (int l = l0; l < l1; ++l) {
     T* kb = reinterpret_cast<T*>(s_k[l]);
     Chunk<T, V> a, b;
     a.load(kb + g.ks + g.o1, s_vec[l]);
@@ -436,7 +436,7 @@ __device__ void unit_direct(const RepositionParams& p, const unsigned long long*
 template <typename T, typename C, bool NEOX, int V, int S, int NV>
 __device__ void unit_pipelined(const RepositionParams& p, const unsigned long long* s_k,
                                const unsigned long long* s_v, uint32_t stage, const UnitGeom& g,
-                               long long po, long long pn, int j) {
+                               long long po, long long pn, int j, int l0, int l1) {
   static_assert(S * NV <= kSlots, "staging slots");
   constexpr uint32_t kSlotStride = kThreads * 16;
   const int c0 = g.chunk, c1 = g.chunk + g.chunks;
@@ -456,14 +456,14 @@ __device__ void unit_pipelined(const RepositionParams& p, const unsigned long lo
     }
   };
 #pragma unroll
-  for (int l = 0; l < S - 1; ++l) {
-    if (l < p.n_layers) issue(l);
+  for (int i = 0; i < S - 1; ++i) {
+    if (l0 + i < l1) issue(l0 + i);
     cp_async_commit();
   }
   Trig<V> tr;
   load_trig<C, V>(p, po, pn, j, tr);
-  for (int l = 0; l < p.n_layers; ++l) {
-    if (l + S - 1 < p.n_layers) issue(l + S - 1);
+  for (int l = l0; l < l1; ++l) {
+    if (l + S - 1 < l1) issue(l + S - 1);
     cp_async_commit();
     cp_async_wait<S - 1>();
     const uint32_t base = stage + (uint32_t)((l % S) * NV) * kSlotStride;
@@ -532,9 +532,29 @@ reposition_kernel(const RepositionParams p) {
   g.tail_vecs = (p.head_dim - p.rotary_dim) / V;
   g.copy_vecs = g.tail_vecs + p.head_dim / V;
   const bool cow_pipelined = g.copy_vecs <= 2 * g.chunks;
-  const long long stride = (long long)gridDim.x * blockDim.x;
 
-  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += stride) {
+  // Work is split over warps as equal spans of (warp unit, layer) pairs, a
+  // warp unit being 32 consecutive units (the lanes of a warp).  A span
+  // covers a few warp units, the first and last possibly over part of the
+  // layers; every (unit, layer) row belongs to exactly one span.  Giving
+  // each thread whole units over all layers left a partial last wave when
+  // units are few (one KV head per GPU: 1.37 units per resident thread ran
+  // as two rounds).
+  const int n_layers = p.n_layers;
+  const long long warp_units = (total + 31) >> 5;
+  const long long n_warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long warp = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long work = warp_units * n_layers;
+  const long long per = work / n_warps, rest = work % n_warps;
+  long long pos = warp * per + (warp < rest ? warp : rest);
+  const long long end = pos + per + (warp < rest ? 1 : 0);
+  while (pos < end) {
+    const long long wu = pos / n_layers;
+    const int l0 = (int)(pos - wu * n_layers);
+    const int l1 = end - pos < n_layers - l0 ? l0 + (int)(end - pos) : n_layers;
+    pos += l1 - l0;
+    const long long u = (wu << 5) + (threadIdx.x & 31);
+    if (u >= total) continue;
     const long long tok = u / upt;
     const int rem = (int)(u - tok * upt);
     const int head = rem / g.chunks;
@@ -563,17 +583,17 @@ reposition_kernel(const RepositionParams p) {
 
     if constexpr (kVector) {
       if (all_vec && g.in_place) {
-        unit_pipelined<T, C, NEOX, V, 8, 2>(p, s_k, s_v, stage, g, po, pn, j);
+        unit_pipelined<T, C, NEOX, V, 8, 2>(p, s_k, s_v, stage, g, po, pn, j, l0, l1);
         continue;
       }
       if (all_vec && cow_pipelined) {
-        unit_pipelined<T, C, NEOX, V, 4, 4>(p, s_k, s_v, stage, g, po, pn, j);
+        unit_pipelined<T, C, NEOX, V, 4, 4>(p, s_k, s_v, stage, g, po, pn, j, l0, l1);
         continue;
       }
     }
     Trig<V> tr;
     load_trig<C, V>(p, po, pn, j, tr);
-    unit_direct<T, NEOX, V>(p, s_k, s_v, s_vec, g, tr);
+    unit_direct<T, NEOX, V>(p, s_k, s_v, s_vec, g, tr, l0, l1);
   }
 }
 
@@ -590,8 +610,12 @@ int launch(const RepositionParams& p, cudaStream_t stream) {
           cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
+  // Enough warps for spans of at least kMinSpan layers (so the per-thread
+  // pipeline still has layers in flight), at most one wave.
+  constexpr long long kMinSpan = 8;
   const long long units = p.count * (long long)p.num_heads * (p.half / V);
-  const long long blocks = (units + kThreads - 1) / kThreads;
+  const long long spans = ((units + 31) / 32 * p.n_layers + kMinSpan - 1) / kMinSpan;
+  const long long blocks = (spans + kThreads / 32 - 1) / (kThreads / 32);
   const int grid = persistent_grid(per_sm, blocks);
   kernel<<<grid, kThreads, smem, stream>>>(p);
   return launch_status();

@@ -404,8 +404,10 @@ def run_ours(args):
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
+    h0 = time.perf_counter()
     for i in range(args.steps):
         step(i)
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
     t_end.record(stream)
     torch.cuda.synchronize()
     dist_barrier(world)
@@ -512,6 +514,8 @@ def run_ours(args):
                          "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": rep_bytes,
                          "ms_per_launch": round(rep_mean, 4)},
+            # host time to enqueue one step; below ms_per_step the GPU never waits
+            "host_enqueue_ms_per_step": round(host_ms, 4),
             "breakdown_ms": {"drop_compact": round(statistics.mean(drop_ms), 4),
                              "reposition": round(rep_mean, 4)},
             "gpu_launches": 4 * args.steps,
