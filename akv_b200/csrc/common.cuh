@@ -31,6 +31,34 @@ inline int launch_status() {
   return e == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
 
+// Programmatic dependent launch.  A kernel launched by launch_pdl may be
+// scheduled while the previous kernel of the stream is still running, once
+// every block of that kernel has called pdl_launch_dependents() (or exited);
+// it calls pdl_wait() before its first global memory access, which returns
+// when the previous kernel has completed and its writes are visible.  This
+// hides the launch gap between short dependent kernels.  After work that is
+// not one of these kernels, the launch behaves like an ordinary one.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KernelArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // Load an index stored as int32 or int64 (dtype chosen at run time; the
 // branch is uniform across the grid).
 __device__ __forceinline__ int64_t ld_index(const void* p, int64_t i, int is64) {

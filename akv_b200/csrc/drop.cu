@@ -141,6 +141,7 @@ __device__ TileCtx tile_context(const DropArgs& a, int tile) {
 __global__ void __launch_bounds__(kThreads) drop_count_kernel(const DropArgs a) {
   __shared__ int diff[kTile + 1];
   __shared__ int s_first, s_bad;
+  pdl_launch_dependents();  // the plan block may be scheduled now; it waits for this grid
   const int tile = blockIdx.x;
   const TileCtx c = tile_context(a, tile);
   for (int i = threadIdx.x; i <= kTile; i += blockDim.x) diff[i] = 0;
@@ -204,6 +205,8 @@ __global__ void __launch_bounds__(kThreads) drop_count_kernel(const DropArgs a) 
 __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs a) {
   __shared__ int s_bad;
   __shared__ long long s_carry[kFields];
+  pdl_wait();
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     s_bad = 0;
     for (int f = 0; f < kFields; ++f) s_carry[f] = 0;
@@ -281,6 +284,8 @@ __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs 
 }
 
 __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();  // lets a following reposition launch be scheduled
   if (a.ws.plan[2] != 0) return;
   const int tile = blockIdx.x;
   const TileCtx c = tile_context(a, tile);
@@ -417,9 +422,14 @@ extern "C" int akv_drop_compact(
   a.status = status;
   a.ws = carve(workspace, n_requests, n_tiles);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // count is an ordinary launch (it overwrites outputs that earlier work in
+  // the stream may still read); plan and scatter follow it with
+  // programmatic dependent launches.
   if (n_tiles > 0) drop_count_kernel<<<n_tiles, kThreads, 0, s>>>(a);
-  drop_plan_kernel<<<1, kPlanThreads, 0, s>>>(a);
-  if (n_tiles > 0) drop_scatter_kernel<<<n_tiles, kThreads, 0, s>>>(a);
+  if (launch_pdl(drop_plan_kernel, 1, kPlanThreads, 0, s, a) != cudaSuccess) return AKV_ERR_CUDA;
+  if (n_tiles > 0 &&
+      launch_pdl(drop_scatter_kernel, n_tiles, kThreads, 0, s, a) != cudaSuccess)
+    return AKV_ERR_CUDA;
   return launch_status();
 }
 

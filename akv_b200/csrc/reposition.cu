@@ -500,6 +500,7 @@ reposition_kernel(const RepositionParams p) {
   __shared__ unsigned long long s_v[kMaxLayers];
   __shared__ bool s_vec[kMaxLayers];
   __shared__ int s_all_vec;
+  pdl_wait();  // transitions and their count may come from the kernel before
   if (threadIdx.x == 0) s_all_vec = 1;
   __syncthreads();
   for (int i = threadIdx.x; i < p.n_layers; i += blockDim.x) {
@@ -617,7 +618,7 @@ int launch(const RepositionParams& p, cudaStream_t stream) {
   const long long spans = ((units + 31) / 32 * p.n_layers + kMinSpan - 1) / kMinSpan;
   const long long blocks = (spans + kThreads / 32 - 1) / (kThreads / 32);
   const int grid = persistent_grid(per_sm, blocks);
-  kernel<<<grid, kThreads, smem, stream>>>(p);
+  if (launch_pdl(kernel, grid, kThreads, smem, stream, p) != cudaSuccess) return AKV_ERR_CUDA;
   return launch_status();
 }
 

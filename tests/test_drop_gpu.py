@@ -210,3 +210,67 @@ def test_drop_then_reposition_without_host_round_trip():
                                       hk[layer])
         np.testing.assert_array_equal(dv[layer].cpu().view(torch.int16).numpy().view(np.uint16),
                                       hv[layer])
+
+
+def test_drop_then_reposition_replayed_from_a_cuda_graph():
+    """The Drop launches (plan and scatter as programmatic dependent
+    launches) and the reposition launch are stream-ordered, allocate nothing
+    and read no host state, so one captured graph replays the whole cache
+    operation; the result equals the oracle pipeline's."""
+    from oracle import oracle
+    from akv_b200 import workloads
+    from akv_b200.context_drop import DropCompactor, FreeSlotRing
+    from akv_b200.context_reposition import layer_pointer_table, reposition_kv_layers
+    from akv_b200.rope import yarn_cos_sin_cache
+
+    dev = torch.device("cuda")
+    prog = workloads.c3_program(requests=6, max_len=7000, seed=5)
+    rows, nslots = workloads.slot_rows(np.random.default_rng(5), prog)
+    free = np.arange(nslots, nslots + int(prog.shared_prefix.sum()) + 8, dtype=np.int32)
+    slots = int(free.max()) + 1
+    layers, heads, dim = 2, 8, 64
+    ks = [torch.randn(slots, heads, dim).to(torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn(slots, heads, dim).to(torch.bfloat16) for _ in range(layers)]
+    cache = yarn_cos_sin_cache(40000, dim, 150000.0, 32.0, 4096)
+    hk = [k.view(torch.int16).numpy().view(np.uint16).copy() for k in ks]
+    hv = [v.view(torch.int16).numpy().view(np.uint16).copy() for v in vs]
+    want = oracle.drop_compact(prog.token_counts, prog.range_offsets, prog.ranges, rows,
+                               shared_prefix=prog.shared_prefix, free_ring=free, free_head=0,
+                               free_tail=len(free))
+    oracle.reposition(hk, hv, want["src"], want["dst"], want["pairs"], cache.numpy(), bf16=True,
+                      threads=4)
+
+    nreq = prog.requests
+    table = np.zeros((nreq + 1, int(prog.token_counts.max())), np.int32)
+    for r in range(nreq):
+        table[r + 1, : len(rows[r])] = rows[r]
+    req_to_token = torch.from_numpy(table).to(dev)
+    row_ids = np.arange(1, nreq + 1)
+    ring = FreeSlotRing(torch.from_numpy(free), capacity=len(free) + prog.total_tokens + 1,
+                        device=dev)
+    comp = DropCompactor(prog.total_tokens, nreq, max(1, len(prog.ranges) // 2), dev)
+    prepared = comp.prepare(prog.token_counts, prog.range_offsets, prog.ranges, row_ids,
+                            shared_prefix=prog.shared_prefix)
+    dk = [k.to(dev) for k in ks]
+    dv = [v.to(dev) for v in vs]
+    kp, vp, dcache = layer_pointer_table(dk), layer_pointer_table(dv), cache.to(dev)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        res = comp.launch(prepared, req_to_token, ring)
+        reposition_kv_layers(kp, vp, dk[0], dv[0], res.transition_source,
+                             res.transition_destination, res.transition_pairs, dcache,
+                             count_device=res.transition_count)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert int(res.status.item()) == 0
+    n = len(want["src"])
+    assert int(res.totals[1].item()) == n
+    np.testing.assert_array_equal(res.transition_source[:n].cpu().numpy(), want["src"])
+    np.testing.assert_array_equal(res.transition_destination[:n].cpu().numpy(), want["dst"])
+    for layer in range(layers):
+        np.testing.assert_array_equal(dk[layer].cpu().view(torch.int16).numpy().view(np.uint16),
+                                      hk[layer])
+        np.testing.assert_array_equal(dv[layer].cpu().view(torch.int16).numpy().view(np.uint16),
+                                      hv[layer])
+    del graph
