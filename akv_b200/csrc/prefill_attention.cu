@@ -630,38 +630,43 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   const int jq = n_prefix + q_local;
   const int q_last_pos = __ldg(p.q_positions + qo0 + min(qb0 + kQBlock, nq_req) - 1);
   float m_used = -INFINITY, l = 0.f;  // l: this thread's half of the row sum
-  uint32_t phase_s[2] = {0u, 0u}, phase_o = 0u;
+  uint32_t phase_o = 0u;
   bool timed_out = false;
   constexpr int kHalf = kTcKeys / 2;
 
   for (int tile = 0; tile < n_tiles; ++tile) {
-    // 1. S(t) done -> this thread's 32 values of its row.
-    timed_out |= !mbar_wait(bar_s0 + 8 * (tile & 1), phase_s[tile & 1]);
-    phase_s[tile & 1] ^= 1u;
+    // 1. S(t) done -> this thread's 32 values of its row.  S buffer t & 1
+    //    completes for the (t >> 1)-th time: its phase parity is (t >> 1) & 1.
+    timed_out |= !mbar_wait(bar_s0 + 8 * (tile & 1), (uint32_t)(tile >> 1) & 1u);
     tc_fence_after();
     float s[kHalf];
     tmem_ld32(trow + kColS + (tile & 1) * kTcKeys + half * kHalf, s);
     tmem_wait_ld();
 
-    // 2. Mask and scale; half-row maximum to shared memory.
+    // 2. Mask; half-row maximum of the raw scores (the scale is positive, so
+    //    it is applied to the maximum only) to shared memory.  Rows past the
+    //    block's last query have Q = 0 and finite scores; they are never
+    //    written out.
     const int j0 = key_lo + tile * kTcKeys;
     const int* kpos =
         reinterpret_cast<const int*>(smem + kTcPosOff + (tile % kTcStages) * kTcKeys * 4);
     const bool tile_full = j0 + kTcKeys <= key_hi && j0 + kTcKeys - 1 <= n_prefix + qb0 &&
                            (p.window < 0 || q_last_pos - kpos[0] <= p.window);
     float hm = -INFINITY;
+    if (tile_full) {
 #pragma unroll
-    for (int i = 0; i < kHalf; ++i) {
-      bool ok = row_valid;
-      if (!tile_full) {
+      for (int i = 0; i < kHalf; ++i) hm = fmaxf(hm, s[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) {
         const int kk = half * kHalf + i, j = j0 + kk;
-        ok = ok && j < key_hi && (j < n_prefix || j <= jq) &&
-             (p.window < 0 || pq - kpos[kk] <= p.window);
+        const bool ok = j < key_hi && (j < n_prefix || j <= jq) &&
+                        (p.window < 0 || pq - kpos[kk] <= p.window);
+        s[i] = ok ? s[i] : -INFINITY;
+        hm = fmaxf(hm, s[i]);
       }
-      s[i] = ok ? s[i] * p.scale_log2 : -INFINITY;
-      hm = fmaxf(hm, s[i]);
     }
-    s_max[half * 128 + row] = hm;
+    s_max[half * 128 + row] = hm * p.scale_log2;
 
     // 3. Tile t+1 landed -> S(t+1) on the tensor cores during this softmax.
     if (tile + 1 < n_tiles) cp_async_wait<kTcStages - 3>();
@@ -684,15 +689,29 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
       m_used = bm;
     }
     const float base2 = m_used == -INFINITY ? 0.f : m_used;
+    // Two elements per packed instruction: x = s * scale - base (one fma),
+    // exponentials, the row sum, and P = hi + lo (hi = RN_bf16(e), lo =
+    // RN_bf16(e - hi)).
+    const f32x2 scale2 = f2_pack(p.scale_log2, p.scale_log2), nbase2 = f2_pack(-base2, -base2);
     uint32_t hi[kHalf / 2], lo[kHalf / 2];
-    float rs = 0.f;
+    f32x2 rs2 = f2_pack(0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < kHalf; i += 2) {
-      const float e0 = fast_exp2(s[i] - base2), e1 = fast_exp2(s[i + 1] - base2);
-      rs += e0 + e1;
-      split_bf16(e0, e1, hi[i / 2], lo[i / 2]);
+      float x0, x1;
+      f2_unpack(f2_fma(f2_pack(s[i], s[i + 1]), scale2, nbase2), x0, x1);
+      const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+      const f32x2 e = f2_pack(e0, e1);
+      rs2 = f2_add(rs2, e);
+      const uint32_t h = pack_bf16(e0, e1);
+      float d0, d1;
+      f2_unpack(f2_sub(e, f2_pack(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u))),
+                d0, d1);
+      hi[i / 2] = h;
+      lo[i / 2] = pack_bf16(d0, d1);
     }
-    l = l * alpha + rs;
+    float rs0, rs1;
+    f2_unpack(rs2, rs0, rs1);
+    l = l * alpha + (rs0 + rs1);
 
     // 5. P(t-1).V done: P and O may be rewritten, the stage of tile t-1 refilled.
     if (tile > 0) {
@@ -866,10 +885,10 @@ extern "C" int akv_context_attention(
                          q_stride_head % 8 == 0 && out_stride_token % 8 == 0 &&
                          out_stride_head % 8 == 0;
   if (variant < 0 || variant > 2) return AKV_ERR_INVALID;
-  if (variant == 2) {
-    if (head_dim != 64 || !aligned16) return AKV_ERR_UNSUPPORTED;
-    return launch_prefill_tc(p, n_items, num_kv_heads, s);
-  }
+  // The tcgen05 kernel takes row maxima of unscaled scores: sm_scale > 0.
+  const bool tc_ok = head_dim == 64 && aligned16 && sm_scale > 0.f;
+  if (variant == 2 && !tc_ok) return AKV_ERR_UNSUPPORTED;
+  if (variant == 2 || (variant == 0 && tc_ok)) return launch_prefill_tc(p, n_items, num_kv_heads, s);
   switch (head_dim) {
     case 64: return launch_prefill<64>(p, n_items, num_kv_heads, s);
     case 128: return launch_prefill<128>(p, n_items, num_kv_heads, s);

@@ -737,7 +737,9 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0)
                    "prefix_keys": int(kv[-1]), "q_heads": hq_total, "kv_heads": hkv_total,
                    "head_dim": d, "layers": layers, "sliding_window": window, "sinks": True,
                    "positions": "prefix with holes (about a third dropped)"},
-        "roofline": {"bound": "tensor", "kernel": "prefill_attention_kernel (full layer)",
+        "roofline": {"bound": "tensor",
+                     "kernel": ("prefill_attention_kernel" if variant == 1 else
+                                "prefill_attention_tc_kernel") + " (full layer)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "algorithmic_flops_per_launch": full_flops,
