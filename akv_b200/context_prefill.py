@@ -102,8 +102,9 @@ class ContextPrefillAttention:
             sinks=None, out=None, lse=None, variant=0):
         """q [tokens, Hq, D] bf16; pools [slots, Hkv, D] bf16; index and
         position vectors int32 on the device.  ``variant``: 0 the faster
-        kernel for the shape (tcgen05 for head_dim 64), 1 the mma.sync
-        kernel, 2 the tcgen05 / TMEM kernel (head_dim 64)."""
+        kernel for the shape (3 for head_dim 64, else 1), 1 the mma.sync
+        kernel, 2 the tcgen05 / TMEM kernel (head_dim 64), 3 its
+        warp-specialised form."""
         if q.dtype != torch.bfloat16 or k_pool.dtype != torch.bfloat16 or \
                 v_pool.dtype != torch.bfloat16:
             raise ValueError("context attention runs on bf16 q / K / V")

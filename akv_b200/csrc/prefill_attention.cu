@@ -812,6 +812,393 @@ int launch_prefill_tc(const PrefillParams& p, int n_items, int num_kv_heads, cud
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialised form of the tcgen05 kernel: the same tiles, mask and
+// arithmetic, with mbarriers instead of block barriers so that warps drift
+// instead of meeting every tile.  Warps 0-7 gather K/V and run the softmax
+// (two warps per TMEM lane quadrant, one per column half); warp 8 issues the
+// MMAs.  P(t) is written over S(t) in tensor memory (hi bf16 pairs in
+// columns 0-31 of the buffer, lo in 32-63), so P is double-buffered with S
+// and the softmax never waits for the previous P.V.  Per key tile t:
+//   kv[t % S]  256 arrivals: every loader's copies of tile t have landed
+//              (cp.async.wait_group, proxy fence, arrive);
+//   s[t & 1]   tcgen05.commit of S(t) = Q K(t)^T;
+//   p          8 arrivals: P(t) is in tensor memory (and O rescaled);
+//   o          tcgen05.commit of O += P(t) V(t).
+// The issuer issues S(t) once K(t) has landed and P(t-2).V(t-2) is done
+// (buffer t & 1 then holds nothing live), and P(t-1).V(t-1) once every warp
+// has stored P(t-1).  Because S(t) completes after P(t-2).V(t-2), a softmax
+// warp that has seen S(t) may refill the stage of tile t-2 (loads run three
+// tiles ahead) and no further wait is needed before it stores P(t); only a
+// rescale of O waits for P(t-1).V(t-1).  The two warps of a lane quadrant
+// exchange half-row maxima through shared memory (double-buffered by tile
+// parity) and a 64-thread named barrier, which also orders their S loads
+// before either overwrites the buffer with P.  Every mbarrier wait is
+// bounded; once one runs out, the CTA's abort flag makes every later wait
+// return at once and the issuer stops issuing, so all warps still reach
+// each named barrier and the end, where the CTA sets *error_flag = 2 and
+// frees its tensor memory.
+// ---------------------------------------------------------------------------
+constexpr int kWsThreads = 288;
+constexpr int kWsAhead = kTcStages - 2;  // tiles loaded ahead of the one in the softmax
+constexpr int kWsRowOff = kTcPosOff + kTcStages * kTcKeys * 4;  // [2][2][128] max, [2][128] sum
+constexpr int kWsBarOff = kWsRowOff + 6 * 128 * 4;
+constexpr int kWsSmemUsed = kWsBarOff + 128 + 1024;
+constexpr int kWsSmem = kWsSmemUsed > 80 * 1024 ? kWsSmemUsed : 80 * 1024;
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// 64-thread named barrier 1 + q of the two warps of lane quadrant q
+// (immediate barrier ids, so the kernel reserves five barriers, not sixteen).
+__device__ __forceinline__ void pair_sync(int q) {
+  switch (q) {
+    case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
+    default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+  }
+}
+// Bounded wait that gives up at once after the CTA aborted.
+__device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (global_ns() - t0 > kWaitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kWsThreads, 2)
+prefill_attention_tc_ws_kernel(const PrefillParams p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* smem = smem_raw + (base - raw);
+  const uint32_t sQ = base;
+  const uint32_t bars = base + kWsBarOff;
+  const uint32_t bar_s0 = bars + 8 * kTcStages, bar_p = bar_s0 + 16, bar_o = bar_p + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kWsBarOff + 8 * kTcStages + 32);
+  float* s_max = reinterpret_cast<float*>(smem + kWsRowOff);  // [tile parity][half][128]
+  float* s_sum = s_max + 4 * 128;                             // [half][128]
+  __shared__ int s_abort;
+  volatile int* abort = &s_abort;
+  auto bar_kv = [&](int tile) { return bars + 8u * (uint32_t)(tile % kTcStages); };
+  auto kv_parity = [&](int tile) { return (uint32_t)(tile / kTcStages) & 1u; };
+
+  const int4 w = p.work[blockIdx.x];
+  const int hk = blockIdx.y;
+  const int b = w.x, qb0 = w.y, key_lo = w.z, key_hi = w.w;
+  const int qo0 = p.qo_indptr[b], nq_req = p.qo_indptr[b + 1] - qo0;
+  const int kv0 = p.kv_indptr[b], n_prefix = p.kv_indptr[b + 1] - kv0;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_tiles = (key_hi - key_lo + kTcKeys - 1) / kTcKeys;
+  if (p.error_flag != nullptr && *reinterpret_cast<volatile int*>(p.error_flag) == 2) return;
+
+  if (warp == 0) {  // TMEM: two S / P buffers and O
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTcCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    for (int st = 0; st < kTcStages; ++st) mbar_init(bars + 8 * st, 256);
+    mbar_init(bar_s0, 1);
+    mbar_init(bar_s0 + 8, 1);
+    mbar_init(bar_p, 8);
+    mbar_init(bar_o, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_abort = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto stage_k = [&](int tile) { return base + kTcQBytes + (tile % kTcStages) * kTcStageBytes; };
+
+  if (warp == 8) {
+    // ---- MMA issuer (one thread) ----
+    if (lane == 0) {
+      for (int t = 0; t <= n_tiles; ++t) {
+        if (t < n_tiles) {  // S(t): K(t) landed; buffer t & 1 free once P(t-2).V(t-2) is done
+          ws_wait(bar_kv(t), kv_parity(t), abort);
+          if (t >= 2) ws_wait(bar_o, (uint32_t)(t - 2) & 1u, abort);
+          if (!*abort) {
+            tc_fence_after();
+            const uint32_t kb = stage_k(t);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_ss(tmem + kColS + (t & 1) * kTcKeys, sw128_desc(sQ + 32 * k),
+                     sw128_desc(kb + 32 * k), f16_idesc(kTcKeys, 0), k > 0);
+            umma_commit(bar_s0 + 8 * (t & 1));
+          }
+        }
+        if (t >= 1) {  // O += P(t-1) V(t-1) once every warp has stored P(t-1)
+          const int u = t - 1;
+          ws_wait(bar_p, (uint32_t)u & 1u, abort);
+          if (!*abort) {
+            tc_fence_after();
+            const uint32_t vb = stage_k(u) + kTcKVBytes;
+            const uint32_t pb = tmem + kColS + (u & 1) * kTcKeys;
+#pragma unroll
+            for (int k = 0; k < kTcKeys / 16; ++k) {  // 16 keys: 8 P columns, 2 KiB of V
+              mma_ts(tmem + kColO, pb + 8 * k, sw128_desc(vb + 2048 * k), f16_idesc(64, 1), 1);
+              mma_ts(tmem + kColO, pb + 32 + 8 * k, sw128_desc(vb + 2048 * k), f16_idesc(64, 1),
+                     1);
+            }
+            umma_commit(bar_o);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- loaders + softmax: warp w serves TMEM lanes 32 (w % 4) .., column half w / 4 ----
+    const int row = ((warp & 3) << 5) | lane, half = warp >> 2;
+    const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    auto key_slot_pos = [&](int j, long long& slot, int& pos) {
+      if (j < n_prefix) {
+        slot = __ldg(p.kv_indices + kv0 + j);
+        pos = __ldg(p.kv_positions + kv0 + j);
+      } else {
+        slot = __ldg(p.birth_slots + qo0 + (j - n_prefix));
+        pos = __ldg(p.q_positions + qo0 + (j - n_prefix));
+      }
+      if (slot < 0 || slot >= p.num_slots) {
+        if (p.error_flag) *p.error_flag = 1;
+        slot = 0;
+      }
+    };
+    const int my_key = tid >> 2, my_quarter = tid & 3;
+    struct KeyRef {
+      long long slot;
+      int pos;
+    };
+    auto fetch = [&](int tile) -> KeyRef {
+      KeyRef r{0, INT_MAX};
+      const int j = key_lo + tile * kTcKeys + my_key;
+      if (tile < n_tiles && j < key_hi) key_slot_pos(j, r.slot, r.pos);
+      return r;
+    };
+    auto issue_tile = [&](int tile, const KeyRef r) {
+      const uint32_t kb = stage_k(tile), vb = kb + kTcKVBytes;
+      int* kpos = reinterpret_cast<int*>(smem + kTcPosOff + (tile % kTcStages) * kTcKeys * 4);
+      if (my_quarter == 0) kpos[my_key] = r.pos;
+      const int bytes = r.pos != INT_MAX ? 16 : 0;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int c = my_quarter * 2 + i;
+        const uint32_t off = my_key * 128 + ((c ^ (my_key & 7)) * 16);
+        cp_async16(kb + off, p.k + r.slot * p.k_ss + hk * p.k_sh + c * 8, bytes);
+        cp_async16(vb + off, p.v + r.slot * p.v_ss + hk * p.v_sh + c * 8, bytes);
+      }
+    };
+
+    // Q: row r = (query r / 8, head r % 8); two threads per row, four chunks each.
+    const int q_local = qb0 + (row >> 3);
+    const int head = hk * kGroupP + (row & 7);
+    const bool row_valid = q_local < nq_req;
+    {
+      const __nv_bfloat16* src = p.q + (long long)(qo0 + (row_valid ? q_local : 0)) * p.q_st +
+                                 (long long)head * p.q_sh;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = half * 4 + i;
+        cp_async16(sQ + row * 128 + ((c ^ (row & 7)) * 16), src + c * 8, row_valid ? 16 : 0);
+      }
+    }
+    // Groups: Q + tile 0, then tiles 1 .. kWsAhead - 1, one group each.
+#pragma unroll
+    for (int t = 0; t < kWsAhead; ++t) {
+      if (t < n_tiles) issue_tile(t, fetch(t));
+      cp_async_commit();
+    }
+    KeyRef next = fetch(kWsAhead);
+    {  // O = 0 (every P.V accumulates): this warp's 32 columns
+      uint32_t z[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) z[i] = 0u;
+      tmem_st32(trow + kColO + 32 * half, z);
+      tmem_wait_st();
+    }
+    if (n_tiles > 0) {  // Q and tile 0 landed
+      cp_async_wait<kWsAhead - 1>();
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_kv(0));
+    }
+
+    const int pq = row_valid ? __ldg(p.q_positions + qo0 + q_local) : 0;
+    const int jq = n_prefix + q_local;
+    const int q_last_pos = __ldg(p.q_positions + qo0 + min(qb0 + kQBlock, nq_req) - 1);
+    float m_used = -INFINITY, l = 0.f;
+    constexpr int kHalf = kTcKeys / 2;
+
+    for (int tile = 0; tile < n_tiles; ++tile) {
+      // 0. This thread's copies of tile t+1 have landed (groups committed:
+      //    tiles 0 .. t + kWsAhead - 1; tile t+1 and older complete).
+      if (tile + 1 < n_tiles) {
+        cp_async_wait<kWsAhead - 2>();
+        fence_async_smem();
+        mbar_arrive(bar_kv(tile + 1));
+      }
+      // 1. S(t) -> this thread's 32 values of its row.
+      ws_wait(bar_s0 + 8 * (tile & 1), (uint32_t)(tile >> 1) & 1u, abort);
+      tc_fence_after();
+      const uint32_t sbuf = trow + kColS + (tile & 1) * kTcKeys;
+      float s[kHalf];
+      tmem_ld32(sbuf + half * kHalf, s);
+      tmem_wait_ld();
+
+      // 2. Mask (key positions of tile t: acquired through its kv barrier);
+      //    half-row maximum of the raw scores, four independent chains.
+      ws_wait(bar_kv(tile), kv_parity(tile), abort);
+      const int j0 = key_lo + tile * kTcKeys;
+      const int* kpos =
+          reinterpret_cast<const int*>(smem + kTcPosOff + (tile % kTcStages) * kTcKeys * 4);
+      const bool tile_full = j0 + kTcKeys <= key_hi && j0 + kTcKeys - 1 <= n_prefix + qb0 &&
+                             (p.window < 0 || q_last_pos - kpos[0] <= p.window);
+      if (!tile_full) {
+#pragma unroll
+        for (int i = 0; i < kHalf; ++i) {
+          const int kk = half * kHalf + i, j = j0 + kk;
+          const bool ok = j < key_hi && (j < n_prefix || j <= jq) &&
+                          (p.window < 0 || pq - kpos[kk] <= p.window);
+          s[i] = ok ? s[i] : -INFINITY;
+        }
+      }
+      float hm4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int i = 4; i < kHalf; ++i) hm4[i & 3] = fmaxf(hm4[i & 3], s[i]);
+      const float hm = fmaxf(fmaxf(hm4[0], hm4[1]), fmaxf(hm4[2], hm4[3]));
+      float* mx = s_max + (tile & 1) * 256;
+      mx[half * 128 + row] = hm * p.scale_log2;
+      // Both warps of the quadrant have their maxima in place and have read
+      // S(t), which P(t) overwrites below.
+      tc_fence_before();
+      pair_sync(warp & 3);
+      tc_fence_after();
+      const float bm = fmaxf(mx[row], mx[128 + row]);
+
+      // 3. Exponentials against the row's base (moved only when the tile
+      //    exceeds it by 2^8; then O and l are rescaled).
+      float alpha = 1.f;
+      bool rescale = false;
+      if (bm > m_used + kStaleMax || (m_used == -INFINITY && bm != -INFINITY)) {
+        alpha = m_used == -INFINITY ? 0.f : fast_exp2(m_used - bm);
+        rescale = m_used != -INFINITY;
+        m_used = bm;
+      }
+      const float base2 = m_used == -INFINITY ? 0.f : m_used;
+      const f32x2 scale2 = f2_pack(p.scale_log2, p.scale_log2),
+                  nbase2 = f2_pack(-base2, -base2);
+      uint32_t hi[kHalf / 2], lo[kHalf / 2];
+      f32x2 rsa = f2_pack(0.f, 0.f), rsb = rsa;
+#pragma unroll
+      for (int i = 0; i < kHalf; i += 2) {
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(s[i], s[i + 1]), scale2, nbase2), x0, x1);
+        const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+        const f32x2 e = f2_pack(e0, e1);
+        if (i & 2) rsb = f2_add(rsb, e);
+        else rsa = f2_add(rsa, e);
+        const uint32_t h = pack_bf16(e0, e1);
+        float d0, d1;
+        f2_unpack(f2_sub(e, f2_pack(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u))),
+                  d0, d1);
+        hi[i / 2] = h;
+        lo[i / 2] = pack_bf16(d0, d1);
+      }
+      float rs0, rs1;
+      f2_unpack(f2_add(rsa, rsb), rs0, rs1);
+      l = l * alpha + (rs0 + rs1);
+
+      // 4. Tile t + kWsAhead into the stage of tile t-2: S(t) completed after
+      //    P(t-2).V(t-2), so that stage is no longer read.
+      {
+        const int nt = tile + kWsAhead;
+        if (nt < n_tiles) {
+          issue_tile(nt, next);
+          next = fetch(nt + 1);
+        }
+        cp_async_commit();
+      }
+      // 5. Rescale this warp's half of O after P(t-1).V(t-1) (warp-wide TMEM
+      //    access), then P(t) over S(t): hi in columns 0-31, lo in 32-63.
+      if (__any_sync(0xffffffffu, rescale)) {
+        ws_wait(bar_o, (uint32_t)(tile - 1) & 1u, abort);
+        tc_fence_after();
+        float o[32];
+        tmem_ld32(trow + kColO + 32 * half, o);
+        tmem_wait_ld();
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
+        tmem_st32(trow + kColO + 32 * half, r);
+      }
+      tmem_st16(sbuf + half * (kHalf / 2), hi);
+      tmem_st16(sbuf + 32 + half * (kHalf / 2), lo);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p);
+    }
+    cp_async_wait<0>();
+
+    // ---- epilogue ----
+    s_sum[half * 128 + row] = l;
+    pair_sync(warp & 3);
+    if (n_tiles > 0) {
+      ws_wait(bar_o, (uint32_t)(n_tiles - 1) & 1u, abort);
+      tc_fence_after();
+    }
+    if (!__any_sync(0xffffffffu, *abort != 0)) {
+      float o[32];
+      tmem_ld32(trow + kColO + 32 * half, o);  // every lane: the load is warp-wide
+      tmem_wait_ld();
+      float den = s_sum[row] + s_sum[128 + row];
+      const float mb = m_used == -INFINITY ? 0.f : m_used;
+      if (p.sinks) den += fast_exp2(p.sinks[head] * kLog2e - mb);
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      __nv_bfloat16* dst = p.out + (long long)(qo0 + q_local) * p.o_st +
+                           (long long)head * p.o_sh + 32 * half;
+#pragma unroll
+      for (int c = 0; c < 4 && row_valid; ++c) {
+        uint4 v;
+        v.x = pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv);
+        v.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+        v.z = pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+        v.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+        *reinterpret_cast<uint4*>(dst + 8 * c) = v;
+      }
+      if (p.lse && row_valid && half == 0)
+        p.lse[(long long)(qo0 + q_local) * p.num_q_heads + head] =
+            den > 0.f ? (mb + log2f(den)) * kLn2 : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && s_abort && p.error_flag) *p.error_flag = 2;
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTcCols));
+  }
+}
+
+int launch_prefill_tc_ws(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
+  if (cudaFuncSetAttribute(prefill_attention_tc_ws_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem) != cudaSuccess)
+    return AKV_ERR_CUDA;
+  if (n_items > 0)
+    prefill_attention_tc_ws_kernel<<<dim3(n_items, num_kv_heads), kWsThreads, kWsSmem, s>>>(p);
+  return launch_status();
+}
+
 template <int D>
 int launch_prefill(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
   using C = PCfg<D>;
@@ -884,11 +1271,13 @@ extern "C" int akv_context_attention(
                          (reinterpret_cast<uintptr_t>(out) & 15) == 0 && q_stride_token % 8 == 0 &&
                          q_stride_head % 8 == 0 && out_stride_token % 8 == 0 &&
                          out_stride_head % 8 == 0;
-  if (variant < 0 || variant > 2) return AKV_ERR_INVALID;
+  if (variant < 0 || variant > 3) return AKV_ERR_INVALID;
   // The tcgen05 kernel takes row maxima of unscaled scores: sm_scale > 0.
   const bool tc_ok = head_dim == 64 && aligned16 && sm_scale > 0.f;
-  if (variant == 2 && !tc_ok) return AKV_ERR_UNSUPPORTED;
-  if (variant == 2 || (variant == 0 && tc_ok)) return launch_prefill_tc(p, n_items, num_kv_heads, s);
+  if (variant >= 2 && !tc_ok) return AKV_ERR_UNSUPPORTED;
+  if (variant == 3 || (variant == 0 && tc_ok))
+    return launch_prefill_tc_ws(p, n_items, num_kv_heads, s);
+  if (variant == 2) return launch_prefill_tc(p, n_items, num_kv_heads, s);
   switch (head_dim) {
     case 64: return launch_prefill<64>(p, n_items, num_kv_heads, s);
     case 128: return launch_prefill<128>(p, n_items, num_kv_heads, s);

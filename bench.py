@@ -83,7 +83,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="override the workload's layer count (a smaller cut for ncu captures)")
     p.add_argument("--variant", type=int, default=0,
-                   help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05)")
+                   help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05, "
+                        "3 tcgen05 warp-specialised)")
     return p.parse_args()
 
 
@@ -696,6 +697,9 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0)
                 ev_full[s][1].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
+    for att in (full, swa):
+        if int(att.error_flag.item()) != 0:
+            raise RuntimeError(f"prefill attention error flag {int(att.error_flag.item())}")
     ms = dist_max(t0.elapsed_time(t1) / steps, world)
     full_ms = statistics.median(a.elapsed_time(b) for a, b in ev_full)
     full_flops = 4.0 * d * hq * full.visible
@@ -738,8 +742,8 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0)
                    "head_dim": d, "layers": layers, "sliding_window": window, "sinks": True,
                    "positions": "prefix with holes (about a third dropped)"},
         "roofline": {"bound": "tensor",
-                     "kernel": ("prefill_attention_kernel" if variant == 1 else
-                                "prefill_attention_tc_kernel") + " (full layer)",
+                     "kernel": {1: "prefill_attention_kernel", 2: "prefill_attention_tc_kernel"}
+                     .get(variant, "prefill_attention_tc_ws_kernel") + " (full layer)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "algorithmic_flops_per_launch": full_flops,

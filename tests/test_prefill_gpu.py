@@ -100,12 +100,13 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2], ids=["auto", "mma_sync", "tcgen05"])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3], ids=["auto", "mma_sync", "tcgen05", "tcgen05_ws"])
 @pytest.mark.parametrize("case", range(len(CASES)))
 def test_prefill_matches_torch(case, variant):
-    """variant 1 runs the mma.sync kernel, 2 the tcgen05 one (head_dim 64)."""
+    """variant 1 runs the mma.sync kernel, 2 the tcgen05 one (head_dim 64), 3 its
+    warp-specialised form."""
     prefix, queries, hkv, d, window, use_sinks = CASES[case]
-    if variant == 2 and d != 64:
+    if variant >= 2 and d != 64:
         pytest.skip("the tcgen05 kernel covers head_dim 64")
     rng = np.random.default_rng(case)
     x = make_batch(rng, prefix, queries, hkv, d)
@@ -116,7 +117,8 @@ def test_prefill_matches_torch(case, variant):
     torch.testing.assert_close(out.float(), want, atol=ATOL, rtol=RTOL)
 
 
-def test_prefill_matches_float64_oracle_with_lse():
+@pytest.mark.parametrize("variant", [1, 2, 3])
+def test_prefill_matches_float64_oracle_with_lse(variant):
     from oracle import oracle
 
     rng = np.random.default_rng(42)
@@ -124,7 +126,7 @@ def test_prefill_matches_float64_oracle_with_lse():
     x = make_batch(rng, [150, 40], [37, 20], hkv, d)
     sinks = torch.randn(8 * hkv, device="cuda")
     lse = torch.empty(x["q"].shape[0], 8 * hkv, device="cuda")
-    out, _ = run_ours(x, hkv, d, window, sinks, lse=lse, variant=2)  # tcgen05
+    out, _ = run_ours(x, hkv, d, window, sinks, lse=lse, variant=variant)
     want, want_lse = oracle.prefill_attention(
         x["q"].float().cpu().numpy(), x["k_pool"].float().cpu().numpy(),
         x["v_pool"].float().cpu().numpy(), x["qo"], x["kv"], x["kv_idx"], x["births"],
