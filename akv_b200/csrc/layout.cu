@@ -56,6 +56,11 @@ constexpr int kThreads = 256;
 constexpr int kPer = kTile / kThreads;  // contiguous tokens per thread
 constexpr int kMaxRepositions = 4094;
 constexpr int kListCap = 256;  // ranges overlapping one tile, painted cooperatively
+// Requests with at most this many Repositions and Drop events keep their
+// per-Reposition tables in shared memory while a block works on them (one
+// parallel load instead of a dependent global load per step); longer
+// programs read the same tables from global memory.
+constexpr int kColCap = 256;
 constexpr int kOffsetThreads = 1024;
 
 // Record kinds of the radix key stream (srt/context_system/ir.py:32-34).
@@ -157,6 +162,18 @@ __device__ Req request_meta(const LayoutArgs& a, int b) {
   return q;
 }
 
+// Number of entries of the increasing array a[0, n) below x; a may be in
+// shared or global memory.
+__device__ __forceinline__ int count_below_any(const int32_t* a, int n, long long x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if ((long long)a[mid] < x) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
 __device__ int tile_request(const int32_t* tile_offsets, int n, int tile) {
   int lo = 0, hi = n;  // first b with tile_offsets[b] > tile, minus one
   while (lo < hi) {
@@ -176,12 +193,20 @@ __global__ void __launch_bounds__(kThreads) layout_classify_kernel(const LayoutA
   __shared__ int s_dmin[kMaxRepositions];
   __shared__ int3 s_list[kListCap];
   __shared__ int s_nlist, s_bad;
+  __shared__ int32_t s_bnd[kColCap];
+  pdl_launch_dependents();  // the stages blocks may be scheduled; they wait for this grid
   const int tile = blockIdx.x;
   const int b = tile_request(a.b.tile_offsets, a.b.n_requests, tile);
   const Req q = request_meta(a, b);
   if (q.P > kMaxRepositions) return;  // reported by the stages kernel
   const int tl = tile - q.tile0;
   const int t0 = tl * kTile, n = min(kTile, q.T - t0);
+  const bool staged = q.P <= kColCap;
+  const int32_t* bnd = a.b.reposition_raw_boundaries + q.rep0;
+  if (staged) {
+    for (int r = threadIdx.x; r < q.P; r += blockDim.x) s_bnd[r] = bnd[r];
+    bnd = s_bnd;
+  }
   for (int i = threadIdx.x; i < kTile; i += blockDim.x) s_dt[i] = INT_MAX;
   for (int c = threadIdx.x; c <= q.P + 1; c += blockDim.x) s_hist[c] = 0;
   for (int c = threadIdx.x; c < q.P; c += blockDim.x) s_dmin[c] = INT_MAX;
@@ -219,7 +244,6 @@ __global__ void __launch_bounds__(kThreads) layout_classify_kernel(const LayoutA
   }
   __syncthreads();
 
-  const int32_t* bnd = a.b.reposition_raw_boundaries + q.rep0;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const int i = threadIdx.x * kPer + k;
@@ -227,12 +251,12 @@ __global__ void __launch_bounds__(kThreads) layout_classify_kernel(const LayoutA
     const int t = t0 + i;
     const int dt = s_dt[i];
     a.ws.dt[q.tok0 + t] = dt;
-    const int r0 = count_below(bnd, q.P, t);  // Repositions with I_r <= t
+    const int r0 = count_below_any(bnd, q.P, t);  // Repositions with I_r <= t
     int r1;
     if (dt == INT_MAX) {
       r1 = q.P;  // kept: active to the end, counted in the final column
     } else {
-      r1 = count_below(bnd, q.P, (long long)dt - 1) - 1;  // last r with I_r < drop(t)
+      r1 = count_below_any(bnd, q.P, (long long)dt - 1) - 1;  // last r with I_r < drop(t)
       const int w = r1 + 1;                              // window (I_{w-1}, I_w] holding drop(t)
       if (w < q.P) atomicMin(&s_dmin[w], t);
     }
@@ -263,6 +287,10 @@ __global__ void __launch_bounds__(kThreads) layout_classify_kernel(const LayoutA
 // 2. stages
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) layout_stages_kernel(const LayoutArgs a) {
+  __shared__ int s_bnd[kColCap], s_nA[kColCap], s_dinv[kColCap], s_rankD[kColCap],
+      s_rankI[kColCap];
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x;
   const Req q = request_meta(a, b);
   int64_t* status = a.b.status + 5 * (long long)b;
@@ -279,6 +307,13 @@ __global__ void __launch_bounds__(kThreads) layout_stages_kernel(const LayoutArg
     return;
   }
   int* counts = a.ws.counts + q.cbase;
+  const bool staged = q.P <= kColCap;
+  if (staged) {
+    for (int r = threadIdx.x; r < q.P; r += blockDim.x) {
+      s_bnd[r] = a.b.reposition_raw_boundaries[q.rep0 + r];
+      s_dinv[r] = a.ws.dinv[q.col0 + r];
+    }
+  }
 
   // Column-wise exclusive scans over the request's tiles.
   for (int c = warp; c <= q.P; c += nwarps) {
@@ -291,7 +326,10 @@ __global__ void __launch_bounds__(kThreads) layout_stages_kernel(const LayoutArg
       if (j < q.ntiles) counts[cell] = carry + inc - v;
       carry += __shfl_sync(0xffffffffu, inc, 31);
     }
-    if (lane == 0) a.ws.nA[q.col0 + c] = carry;
+    if (lane == 0) {
+      a.ws.nA[q.col0 + c] = carry;
+      if (staged && c < q.P) s_nA[c] = carry;
+    }
   }
   __syncthreads();
 
@@ -317,38 +355,47 @@ __global__ void __launch_bounds__(kThreads) layout_stages_kernel(const LayoutArg
       cnt = warp_sum<int>(cnt);
       rank = counts[(long long)r * q.ntiles + tl] + cnt;
     }
-    if (lane == 0) (which == 0 ? a.ws.rankD : a.ws.rankI)[q.col0 + r] = rank;
+    if (lane == 0) {
+      (which == 0 ? a.ws.rankD : a.ws.rankI)[q.col0 + r] = rank;
+      if (staged) (which == 0 ? s_rankD : s_rankI)[r] = rank;
+    }
   }
   __syncthreads();
 
   // The recurrence over the Repositions (context_plan.py:405-440).
   int32_t* toff = a.b.transition_offsets + q.col0;
   if (threadIdx.x == 0) {
+    // Inputs of the recurrence: shared-memory copies when staged.
+    const int* c_bnd = staged ? s_bnd : bnd;
+    const int* c_nA = staged ? s_nA : a.ws.nA + q.col0;
+    const int* c_dinv = staged ? s_dinv : a.ws.dinv + q.col0;
+    const int* c_rankD = staged ? s_rankD : a.ws.rankD + q.col0;
+    const int* c_rankI = staged ? s_rankI : a.ws.rankI + q.col0;
     long long np_prev = 0, i_prev = 0, na_prev = 0, arg = -1;
     int stage = 0, cum = 0, code = 0;
     a.ws.seg_np[q.col0] = 0;
     a.ws.seg_stage[q.col0] = 0;
     toff[0] = 0;
     for (int r = 0; r < q.P; ++r) {
-      const long long I = (long long)bnd[r] + 1;
-      const int na = a.ws.nA[q.col0 + r];
+      const long long I = (long long)c_bnd[r] + 1;
+      const int na = c_nA[r];
       const int col = q.col0 + r;
       int st = 0;
       long long np = np_prev + (I - i_prev);
       if (code == 0 && na == 0) {
         code = 1;  // "Reposition at raw boundary ... has no active tokens."
-        arg = bnd[r];
+        arg = c_bnd[r];
       }
       int F = INT_MAX, rank_f = 0;
       if (code == 0) {
-        const int dinv = a.ws.dinv[col];
+        const int dinv = c_dinv[r];
         if (dinv != 0) {
           F = INT_MAX - dinv;
-          rank_f = a.ws.rankD[col];
+          rank_f = c_rankD[r];
         }
         if (r > 0 && np_prev > na_prev && i_prev < F) {
           F = (int)i_prev;
-          rank_f = a.ws.rankI[col];
+          rank_f = c_rankI[r];
         }
         const int moved = F != INT_MAX ? na - rank_f : 0;
         a.ws.tbase[col] = cum;
@@ -430,6 +477,8 @@ __global__ void __launch_bounds__(kThreads) layout_stages_kernel(const LayoutArg
 __global__ void __launch_bounds__(kOffsetThreads) layout_offsets_kernel(const LayoutArgs a) {
   __shared__ long long s_carry[3];
   __shared__ int s_err;
+  pdl_wait();
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     s_carry[0] = s_carry[1] = s_carry[2] = 0;
     s_err = 0;
@@ -479,16 +528,76 @@ __global__ void __launch_bounds__(kOffsetThreads) layout_offsets_kernel(const La
 // ---------------------------------------------------------------------------
 // 4. emit
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads) layout_emit_kernel(const LayoutArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) layout_emit_kernel(const LayoutArgs a) {
+  // Per-Reposition tables of the request (and its Drop events), staged.
+  __shared__ int32_t s_bnd[kColCap], s_stage[kColCap], s_F[kColCap], s_rankF[kColCap],
+      s_npb[kColCap], s_tbase[kColCap], s_next[kColCap];
+  __shared__ int32_t s_cnt[kColCap + 1], s_segnp[kColCap + 1], s_segst[kColCap + 1];
+  __shared__ int32_t s_ins[kColCap], s_dro[kColCap + 1];
+  pdl_wait();
   const int tile = blockIdx.x;
   const int b = tile_request(a.b.tile_offsets, a.b.n_requests, tile);
   const Req q = request_meta(a, b);
   if (q.P > kMaxRepositions) return;
   const int tl = tile - q.tile0;
   const int t0 = tl * kTile, n = min(kTile, q.T - t0);
-  const int32_t* bnd = a.b.reposition_raw_boundaries + q.rep0;
   const int* counts = a.ws.counts + q.cbase;
   const int ibase = threadIdx.x * kPer;
+
+  // Table views: shared-memory copies (one parallel load) for requests with
+  // at most kColCap Repositions and Drop events, global memory otherwise.
+  //   cnt[r]  = rank_r at this tile's start (r = 0..P; P: kept tokens);
+  //   next[r] = rank_r at the next tile's start, or |A_r| for the last tile.
+  const bool staged = q.P <= kColCap && q.E <= kColCap;
+  const int32_t* bnd = a.b.reposition_raw_boundaries + q.rep0;
+  const int32_t* ins = a.b.drop_insert_offsets + q.ev0;
+  const int32_t* dro = a.b.drop_range_offsets + q.ev0;
+  const int* stage_of = a.ws.stage_of + q.col0;
+  const int* Fv = a.ws.F + q.col0;
+  const int* rankFv = a.ws.rankF + q.col0;
+  const int* npbv = a.ws.np_before + q.col0;
+  const int* tbasev = a.ws.tbase + q.col0;
+  const int* segnp = a.ws.seg_np + q.col0;
+  const int* segst = a.ws.seg_stage + q.col0;
+  auto cnt_at = [&](int r) -> int {
+    return staged ? s_cnt[r] : counts[(long long)r * q.ntiles + tl];
+  };
+  auto cnt_next = [&](int r) -> int {
+    if (staged) return s_next[r];
+    return tl + 1 < q.ntiles ? counts[(long long)r * q.ntiles + tl + 1] : a.ws.nA[q.col0 + r];
+  };
+  if (staged) {
+    for (int r = threadIdx.x; r <= q.P; r += blockDim.x) {
+      s_cnt[r] = counts[(long long)r * q.ntiles + tl];
+      s_segnp[r] = segnp[r];
+      s_segst[r] = segst[r];
+      if (r < q.P) {
+        s_bnd[r] = bnd[r];
+        s_stage[r] = stage_of[r];
+        s_F[r] = Fv[r];
+        s_rankF[r] = rankFv[r];
+        s_npb[r] = npbv[r];
+        s_tbase[r] = tbasev[r];
+        s_next[r] = tl + 1 < q.ntiles ? counts[(long long)r * q.ntiles + tl + 1]
+                                      : a.ws.nA[q.col0 + r];
+      }
+    }
+    for (int e = threadIdx.x; e <= q.E; e += blockDim.x) {
+      if (e < q.E) s_ins[e] = ins[e];
+      s_dro[e] = dro[e];
+    }
+    __syncthreads();
+    bnd = s_bnd;
+    ins = s_ins;
+    dro = s_dro;
+    stage_of = s_stage;
+    Fv = s_F;
+    rankFv = s_rankF;
+    npbv = s_npb;
+    tbasev = s_tbase;
+    segnp = s_segnp;
+    segst = s_segst;
+  }
 
   int dt[kPer], seg[kPer], pos[kPer], ms[kPer];
 #pragma unroll
@@ -500,10 +609,10 @@ __global__ void __launch_bounds__(kThreads) layout_emit_kernel(const LayoutArgs 
     ms[k] = 0;
     if (i >= n) continue;
     dt[k] = a.ws.dt[q.tok0 + t];
-    seg[k] = count_below(bnd, q.P, t);
+    seg[k] = count_below_any(bnd, q.P, t);
     const long long i_seg = seg[k] ? (long long)bnd[seg[k] - 1] + 1 : 0;
-    pos[k] = (int)(a.ws.seg_np[q.col0 + seg[k]] + (t - i_seg));
-    ms[k] = a.ws.seg_stage[q.col0 + seg[k]];
+    pos[k] = (int)(segnp[seg[k]] + (t - i_seg));
+    ms[k] = segst[seg[k]];
     a.b.birth_positions[q.tok0 + t] = pos[k];
     a.b.birth_stages[q.tok0 + t] = ms[k];
   }
@@ -511,15 +620,13 @@ __global__ void __launch_bounds__(kThreads) layout_emit_kernel(const LayoutArgs 
   // Transitions of every effective Reposition whose moved tokens reach here.
   const int tr_base = a.b.transition_request_offsets[b];
   const long long cap = a.b.transition_capacity;
-  for (int r = count_below(bnd, q.P, t0); r < q.P; ++r) {
-    const int col = q.col0 + r;
-    const int st = a.ws.stage_of[col];
+  for (int r = count_below_any(bnd, q.P, t0); r < q.P; ++r) {
+    const int st = stage_of[r];
     if (st == 0) continue;
-    const int F = a.ws.F[col];
+    const int F = Fv[r];
     if (F >= t0 + n) continue;
-    const int Rr = counts[(long long)r * q.ntiles + tl];
-    const int next = tl + 1 < q.ntiles ? counts[(long long)r * q.ntiles + tl + 1] : a.ws.nA[col];
-    if (next == Rr) continue;  // no token of A_r in this tile
+    const int Rr = cnt_at(r);
+    if (cnt_next(r) == Rr) continue;  // no token of A_r in this tile
     const long long I = (long long)bnd[r] + 1;
     const long long Ip = r > 0 ? (long long)bnd[r - 1] + 1 : 0;
     bool in_r[kPer], in_p[kPer];
@@ -535,9 +642,9 @@ __global__ void __launch_bounds__(kThreads) layout_emit_kernel(const LayoutArgs 
     unsigned tot;
     const unsigned ex = block_exclusive_scan<unsigned>(local, &tot);
     int er = (int)(ex & 0xffffu), ep = (int)(ex >> 16);
-    const int Rp = r > 0 ? counts[(long long)(r - 1) * q.ntiles + tl] : 0;
-    const int rank_f = a.ws.rankF[col], npb = a.ws.np_before[col];
-    const long long base = (long long)tr_base + a.ws.tbase[col] - rank_f;
+    const int Rp = r > 0 ? cnt_at(r - 1) : 0;
+    const int rank_f = rankFv[r], npb = npbv[r];
+    const long long base = (long long)tr_base + tbasev[r] - rank_f;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
       const int t = t0 + ibase + k;
@@ -561,8 +668,6 @@ __global__ void __launch_bounds__(kThreads) layout_emit_kernel(const LayoutArgs 
   }
 
   // Final per-token outputs and token records (context_plan.py:499-514).
-  const int32_t* ins = a.b.drop_insert_offsets + q.ev0;
-  const int32_t* dro = a.b.drop_range_offsets + q.ev0;
   int kept_local = 0;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
@@ -574,8 +679,8 @@ __global__ void __launch_bounds__(kThreads) layout_emit_kernel(const LayoutArgs 
     a.b.positions[f] = pos[k];
     a.b.keep_mask[f] = keep;
     a.b.materialized_stage[f] = ms[k];
-    const int ev = count_below(ins, q.E, (long long)t + 1);  // Drop events at or before t
-    const long long key = t + (dro[ev] - dro[0]) + a.ws.seg_stage[q.col0 + seg[k]];
+    const int ev = count_below_any(ins, q.E, (long long)t + 1);  // Drop events at or before t
+    const long long key = t + (dro[ev] - dro[0]) + segst[seg[k]];
     a.b.token_to_key[f] = key;
     int32_t* rec = a.b.records + 3 * (q.key0 + key);
     rec[0] = kToken;
@@ -589,8 +694,7 @@ __global__ void __launch_bounds__(kThreads) layout_emit_kernel(const LayoutArgs 
   if (a.b.active_offsets != nullptr) {
     int tot;
     int ek = block_exclusive_scan<int>(kept_local, &tot);
-    const long long kbase =
-        (long long)a.b.active_offsets[b] + counts[(long long)q.P * q.ntiles + tl] + ek;
+    const long long kbase = (long long)a.b.active_offsets[b] + cnt_at(q.P) + ek;
     int j = 0;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
@@ -648,10 +752,18 @@ extern "C" int akv_compile_layouts(const akv_layout_batch* batch, void* stream) 
   const size_t zeroed = reinterpret_cast<uintptr_t>(a.ws.dt) - reinterpret_cast<uintptr_t>(a.ws.dinv);
   if (cudaMemsetAsync(a.ws.dinv, 0, zeroed, s) != cudaSuccess)
     return AKV_ERR_CUDA;
+  // classify follows the memset as an ordinary launch; stages, offsets and
+  // emit are programmatic dependent launches (each waits for its
+  // predecessor before reading anything).
   if (x.n_tiles > 0) layout_classify_kernel<<<x.n_tiles, kThreads, 0, s>>>(a);
-  if (x.n_requests > 0) layout_stages_kernel<<<x.n_requests, kThreads, 0, s>>>(a);
-  layout_offsets_kernel<<<1, kOffsetThreads, 0, s>>>(a);
-  if (x.n_tiles > 0) layout_emit_kernel<<<x.n_tiles, kThreads, 0, s>>>(a);
+  if (x.n_requests > 0 &&
+      launch_pdl(layout_stages_kernel, x.n_requests, kThreads, 0, s, a) != cudaSuccess)
+    return AKV_ERR_CUDA;
+  if (launch_pdl(layout_offsets_kernel, 1, kOffsetThreads, 0, s, a) != cudaSuccess)
+    return AKV_ERR_CUDA;
+  if (x.n_tiles > 0 &&
+      launch_pdl(layout_emit_kernel, x.n_tiles, kThreads, 0, s, a) != cudaSuccess)
+    return AKV_ERR_CUDA;
   return launch_status();
 }
 

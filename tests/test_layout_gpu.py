@@ -75,6 +75,8 @@ REGIMES = {
     "medium": (48, 16, (100, 6000), (0, 30), (0, 30), 6, 400),
     "many_stages": (6, 3, (2000, 9000), (40, 120), (60, 200), 3, 60),
     "multi_tile": (4, 2, (60000, 70000), (10, 40), (5, 25), 8, 3000),
+    # more than 256 Repositions / Drop events: tables read from global memory
+    "wide": (3, 3, (6000, 12000), (260, 400), (280, 500), 3, 40),
 }
 
 
