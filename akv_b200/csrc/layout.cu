@@ -53,7 +53,7 @@ namespace {
 
 constexpr int kTile = 512;
 constexpr int kThreads = 256;
-constexpr int kPer = kTile / kThreads;  // contiguous tokens per thread
+constexpr int kPer = kTile / kThreads;  // tokens per thread: threadIdx.x + k * kThreads
 constexpr int kMaxRepositions = 4094;
 constexpr int kListCap = 256;  // ranges overlapping one tile, painted cooperatively
 // Requests with at most this many Repositions and Drop events keep their
@@ -244,28 +244,41 @@ __global__ void __launch_bounds__(kThreads) layout_classify_kernel(const LayoutA
   }
   __syncthreads();
 
+  // Neighbouring tokens mostly share their interval [r0, r1]: the shared
+  // histogram and minima are updated once per distinct value in a warp.
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    const int i = threadIdx.x * kPer + k;
-    if (i >= n) continue;
+    const int i = threadIdx.x + k * kThreads;
+    const bool valid = i < n;
     const int t = t0 + i;
-    const int dt = s_dt[i];
-    a.ws.dt[q.tok0 + t] = dt;
-    const int r0 = count_below_any(bnd, q.P, t);  // Repositions with I_r <= t
-    int r1;
-    if (dt == INT_MAX) {
-      r1 = q.P;  // kept: active to the end, counted in the final column
-    } else {
-      r1 = count_below_any(bnd, q.P, (long long)dt - 1) - 1;  // last r with I_r < drop(t)
-      const int w = r1 + 1;                              // window (I_{w-1}, I_w] holding drop(t)
-      if (w < q.P) atomicMin(&s_dmin[w], t);
+    int r0 = -1, r1 = -2, w = -1;
+    if (valid) {
+      const int dt = s_dt[i];
+      a.ws.dt[q.tok0 + t] = dt;
+      r0 = count_below_any(bnd, q.P, t);  // Repositions with I_r <= t
+      if (dt == INT_MAX) {
+        r1 = q.P;  // kept: active to the end, counted in the final column
+      } else {
+        r1 = count_below_any(bnd, q.P, (long long)dt - 1) - 1;  // last r with I_r < drop(t)
+        w = r1 + 1;  // window (I_{w-1}, I_w] holding drop(t)
+        if (w >= q.P) w = -1;
+      }
+      const long long id = ld_index(a.b.token_ids, q.tok0 + t, a.b.token_ids_is64);
+      if (id < 0 || id > INT_MAX) atomicMin(&s_bad, t);
     }
-    if (r1 >= r0) {
-      atomicAdd(&s_hist[r0], 1);
-      atomicAdd(&s_hist[r1 + 1], -1);
+    const bool span = r1 >= r0;
+    const int lo_key = span ? r0 : -1, hi_key = span ? r1 + 1 : -1;
+    const unsigned g_lo = __match_any_sync(full, lo_key);
+    if (lo_key >= 0 && lane == __ffs(g_lo) - 1) atomicAdd(&s_hist[lo_key], __popc(g_lo));
+    const unsigned g_hi = __match_any_sync(full, hi_key);
+    if (hi_key >= 0 && lane == __ffs(g_hi) - 1) atomicAdd(&s_hist[hi_key], -__popc(g_hi));
+    const unsigned g_w = __match_any_sync(full, w);
+    if (w >= 0) {
+      const int m = (int)__reduce_min_sync(g_w, (unsigned)t);
+      if (lane == __ffs(g_w) - 1) atomicMin(&s_dmin[w], m);
     }
-    const long long id = ld_index(a.b.token_ids, q.tok0 + t, a.b.token_ids_is64);
-    if (id < 0 || id > INT_MAX) atomicMin(&s_bad, t);
   }
   __syncthreads();
 
@@ -542,7 +555,6 @@ __global__ void __launch_bounds__(kThreads, 4) layout_emit_kernel(const LayoutAr
   const int tl = tile - q.tile0;
   const int t0 = tl * kTile, n = min(kTile, q.T - t0);
   const int* counts = a.ws.counts + q.cbase;
-  const int ibase = threadIdx.x * kPer;
 
   // Table views: shared-memory copies (one parallel load) for requests with
   // at most kColCap Repositions and Drop events, global memory otherwise.
@@ -599,10 +611,12 @@ __global__ void __launch_bounds__(kThreads, 4) layout_emit_kernel(const LayoutAr
     segst = s_segst;
   }
 
+  // Thread x holds tokens x and x + kThreads of the tile, so each store
+  // instruction of a warp covers 32 consecutive tokens.
   int dt[kPer], seg[kPer], pos[kPer], ms[kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    const int i = ibase + k, t = t0 + i;
+    const int i = threadIdx.x + k * kThreads, t = t0 + i;
     dt[k] = INT_MAX;
     seg[k] = 0;
     pos[k] = 0;
@@ -629,80 +643,97 @@ __global__ void __launch_bounds__(kThreads, 4) layout_emit_kernel(const LayoutAr
     if (cnt_next(r) == Rr) continue;  // no token of A_r in this tile
     const long long I = (long long)bnd[r] + 1;
     const long long Ip = r > 0 ? (long long)bnd[r - 1] + 1 : 0;
+    // Ranks in A_r and A_{r-1} in token order: one scan of four 16-bit
+    // counters (A_r, A_{r-1}) x (first, second token of each thread).
     bool in_r[kPer], in_p[kPer];
-    unsigned local = 0;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int i = ibase + k;
+      const int i = threadIdx.x + k * kThreads;
       const long long t = t0 + i;
       in_r[k] = i < n && t < I && dt[k] > I;
       in_p[k] = i < n && t < Ip && dt[k] > Ip;
-      local += (unsigned)in_r[k] + ((unsigned)in_p[k] << 16);
     }
-    unsigned tot;
-    const unsigned ex = block_exclusive_scan<unsigned>(local, &tot);
-    int er = (int)(ex & 0xffffu), ep = (int)(ex >> 16);
+    static_assert(kPer == 2, "four 16-bit scan fields");
+    const unsigned long long local = (unsigned long long)in_r[0] |
+                                     ((unsigned long long)in_p[0] << 16) |
+                                     ((unsigned long long)in_r[1] << 32) |
+                                     ((unsigned long long)in_p[1] << 48);
+    unsigned long long tot;
+    const unsigned long long ex = block_exclusive_scan<unsigned long long>(local, &tot);
+    const int er[kPer] = {(int)(ex & 0xffffu), (int)(tot & 0xffffu) + (int)((ex >> 32) & 0xffffu)};
+    const int ep[kPer] = {(int)((ex >> 16) & 0xffffu),
+                          (int)((tot >> 16) & 0xffffu) + (int)((ex >> 48) & 0xffffu)};
     const int Rp = r > 0 ? cnt_at(r - 1) : 0;
     const int rank_f = rankFv[r], npb = npbv[r];
     const long long base = (long long)tr_base + tbasev[r] - rank_f;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int t = t0 + ibase + k;
-      if (in_r[k]) {
-        const int rank = Rr + er;
-        if (t >= F) {
-          const long long idx = base + rank;
-          const int old = t < Ip ? Rp + ep : (int)(npb + (t - Ip));
-          if (idx >= 0 && idx < cap) {  // the capacity may be short (flagged)
-            a.b.transition_raw_tokens[idx] = t;
-            a.b.transition_old_positions[idx] = old;
-            a.b.transition_new_positions[idx] = rank;
-          }
-          pos[k] = rank;
-          ms[k] = st;
+      const int t = t0 + threadIdx.x + k * kThreads;
+      if (in_r[k] && t >= F) {
+        const int rank = Rr + er[k];
+        const long long idx = base + rank;
+        const int old = t < Ip ? Rp + ep[k] : (int)(npb + (t - Ip));
+        if (idx >= 0 && idx < cap) {  // the capacity may be short (flagged)
+          a.b.transition_raw_tokens[idx] = t;
+          a.b.transition_old_positions[idx] = old;
+          a.b.transition_new_positions[idx] = rank;
         }
-        ++er;
+        pos[k] = rank;
+        ms[k] = st;
       }
-      if (in_p[k]) ++ep;
     }
   }
 
   // Final per-token outputs and token records (context_plan.py:499-514).
-  int kept_local = 0;
+  // A record is three int32 at 12-byte stride: with an 8-byte aligned array
+  // it is one 8-byte and one 4-byte store (which comes first depends on the
+  // key's parity).
+  const bool rec8 = (reinterpret_cast<uintptr_t>(a.b.records) & 7) == 0;
+  int kept[kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    const int i = ibase + k, t = t0 + i;
+    const int i = threadIdx.x + k * kThreads, t = t0 + i;
+    kept[k] = 0;
     if (i >= n) continue;
     const long long f = q.tok0 + t;
     const bool keep = dt[k] == INT_MAX;
-    kept_local += keep;
+    kept[k] = keep;
     a.b.positions[f] = pos[k];
     a.b.keep_mask[f] = keep;
     a.b.materialized_stage[f] = ms[k];
     const int ev = count_below_any(ins, q.E, (long long)t + 1);  // Drop events at or before t
     const long long key = t + (dro[ev] - dro[0]) + segst[seg[k]];
     a.b.token_to_key[f] = key;
-    int32_t* rec = a.b.records + 3 * (q.key0 + key);
-    rec[0] = kToken;
-    rec[1] = (int32_t)ld_index(a.b.token_ids, f, a.b.token_ids_is64);
-    rec[2] = pos[k];
-    a.b.virtual_mask[q.key0 + key] = 0;
-    a.b.key_to_token[q.key0 + key] = t;
+    const long long gk = q.key0 + key;
+    int32_t* rec = a.b.records + 3 * gk;
+    const int32_t id = (int32_t)ld_index(a.b.token_ids, f, a.b.token_ids_is64);
+    if (rec8 && (gk & 1) == 0) {
+      *reinterpret_cast<int2*>(rec) = make_int2(kToken, id);
+      rec[2] = pos[k];
+    } else if (rec8) {
+      rec[0] = kToken;
+      *reinterpret_cast<int2*>(rec + 1) = make_int2(id, pos[k]);
+    } else {
+      rec[0] = kToken;
+      rec[1] = id;
+      rec[2] = pos[k];
+    }
+    a.b.virtual_mask[gk] = 0;
+    a.b.key_to_token[gk] = t;
   }
 
   // Decode view: raw = flatnonzero(keep), positions[raw] (occurrence.py:47-66).
   if (a.b.active_offsets != nullptr) {
-    int tot;
-    int ek = block_exclusive_scan<int>(kept_local, &tot);
-    const long long kbase = (long long)a.b.active_offsets[b] + cnt_at(q.P) + ek;
-    int j = 0;
+    unsigned tot;
+    const unsigned ex = block_exclusive_scan<unsigned>((unsigned)kept[0] | ((unsigned)kept[1] << 16),
+                                                       &tot);
+    const long long kbase = (long long)a.b.active_offsets[b] + cnt_at(q.P);
+    const int rank[kPer] = {(int)(ex & 0xffffu), (int)(tot & 0xffffu) + (int)(ex >> 16)};
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int i = ibase + k;
-      if (i >= n || dt[k] != INT_MAX) continue;
-      a.b.raw_indices[kbase + j] = t0 + i;
-      a.b.active_positions[kbase + j] = pos[k];
-      ++j;
+      if (!kept[k]) continue;
+      a.b.raw_indices[kbase + rank[k]] = t0 + threadIdx.x + k * kThreads;
+      a.b.active_positions[kbase + rank[k]] = pos[k];
     }
   }
 }
