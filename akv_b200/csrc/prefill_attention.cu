@@ -487,8 +487,19 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "r"(r[15])
       : "memory");
 }
-__device__ __forceinline__ void tmem_wait_ld() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// tcgen05.wait::ld that also takes the 32 loaded values as operands, so the
+// compiler cannot move their uses above the wait when other work sits
+// between the load and the wait.
+__device__ __forceinline__ void tmem_wait_ld32(float* v) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]),
+                 "+f"(v[6]), "+f"(v[7]), "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]),
+                 "+f"(v[12]), "+f"(v[13]), "+f"(v[14]), "+f"(v[15]), "+f"(v[16]), "+f"(v[17]),
+                 "+f"(v[18]), "+f"(v[19]), "+f"(v[20]), "+f"(v[21]), "+f"(v[22]), "+f"(v[23]),
+                 "+f"(v[24]), "+f"(v[25]), "+f"(v[26]), "+f"(v[27]), "+f"(v[28]), "+f"(v[29]),
+                 "+f"(v[30]), "+f"(v[31])
+               :
+               : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -641,7 +652,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
     tc_fence_after();
     float s[kHalf];
     tmem_ld32(trow + kColS + (tile & 1) * kTcKeys + half * kHalf, s);
-    tmem_wait_ld();
+    tmem_wait_ld32(s);
 
     // 2. Mask; half-row maximum of the raw scores (the scale is positive, so
     //    it is applied to the maximum only) to shared memory.  Rows past the
@@ -732,7 +743,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
     if (__any_sync(0xffffffffu, rescale)) {
       float o[32];
       tmem_ld32(trow + kColO + 32 * half, o);
-      tmem_wait_ld();
+      tmem_wait_ld32(o);
       uint32_t r[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
@@ -774,7 +785,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   if (!failed) {
     float o[32];
     tmem_ld32(trow + kColO + 32 * half, o);  // every thread: the load is warp-wide
-    tmem_wait_ld();
+    tmem_wait_ld32(o);
     float den = s_sum[row] + s_sum[128 + row];
     const float mb = m_used == -INFINITY ? 0.f : m_used;
     if (p.sinks) den += fast_exp2(p.sinks[head] * kLog2e - mb);
@@ -1052,7 +1063,18 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       const uint32_t sbuf = trow + kColS + (tile & 1) * kTcKeys;
       float s[kHalf];
       tmem_ld32(sbuf + half * kHalf, s);
-      tmem_wait_ld();
+      // While the TMEM load is in flight: tile t + kWsAhead into the stage of
+      // tile t-2 (S(t) completed after P(t-2).V(t-2), so that stage is no
+      // longer read).
+      {
+        const int nt = tile + kWsAhead;
+        if (nt < n_tiles) {
+          issue_tile(nt, next);
+          next = fetch(nt + 1);
+        }
+        cp_async_commit();
+      }
+      tmem_wait_ld32(s);
 
       // 2. Mask (key positions of tile t: acquired through its kv barrier);
       //    half-row maximum of the raw scores, four independent chains.
@@ -1117,24 +1139,14 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       f2_unpack(f2_add(rsa, rsb), rs0, rs1);
       l = l * alpha + (rs0 + rs1);
 
-      // 4. Tile t + kWsAhead into the stage of tile t-2: S(t) completed after
-      //    P(t-2).V(t-2), so that stage is no longer read.
-      {
-        const int nt = tile + kWsAhead;
-        if (nt < n_tiles) {
-          issue_tile(nt, next);
-          next = fetch(nt + 1);
-        }
-        cp_async_commit();
-      }
-      // 5. Rescale this warp's half of O after P(t-1).V(t-1) (warp-wide TMEM
+      // 4. Rescale this warp's half of O after P(t-1).V(t-1) (warp-wide TMEM
       //    access), then P(t) over S(t): hi in columns 0-31, lo in 32-63.
       if (__any_sync(0xffffffffu, rescale)) {
         ws_wait(bar_o, (uint32_t)(tile - 1) & 1u, abort);
         tc_fence_after();
         float o[32];
         tmem_ld32(trow + kColO + 32 * half, o);
-        tmem_wait_ld();
+        tmem_wait_ld32(o);
         uint32_t r[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
@@ -1159,7 +1171,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
     if (!__any_sync(0xffffffffu, *abort != 0)) {
       float o[32];
       tmem_ld32(trow + kColO + 32 * half, o);  // every lane: the load is warp-wide
-      tmem_wait_ld();
+      tmem_wait_ld32(o);
       float den = s_sum[row] + s_sum[128 + row];
       const float mb = m_used == -INFINITY ? 0.f : m_used;
       if (p.sinks) den += fast_exp2(p.sinks[head] * kLog2e - mb);
