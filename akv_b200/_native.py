@@ -76,6 +76,7 @@ SIGNATURES = {
         _P, _P, _I64, _P, _P, _I64, _P, _I64, _I32, _P, _P, _P, _P, _P,
     ],
     "akv_write_row_slots": [_P, _P, _I32, _P, _I32, _P, _I32, _I64, _P],
+    "akv_active_slots": [_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P],
     "akv_compile_layouts_max_repositions": [],
     "akv_compile_layouts_workspace_bytes": [_I32, _I64, _I64, _I64],
     "akv_compile_layouts_batch_bytes": [],

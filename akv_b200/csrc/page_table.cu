@@ -166,6 +166,26 @@ __global__ void write_row_slots_kernel(const int64_t* pointers, const void* rows
   }
 }
 
+// Active slots of one request row for an offload / load / PD transfer:
+// out[i] = row[device_indices[start + i]] for the n_prefix surviving prompt
+// tokens, then out[n_prefix + j] = row[generated_start + j] for the generated
+// tail.  A raw index or row position outside the row reads as slot -1 and
+// sets *error_flag.
+__global__ void active_slots_kernel(const int32_t* row, int64_t row_len,
+                                    const int32_t* device_indices, int64_t start,
+                                    int64_t n_prefix, int64_t generated_start, int64_t n_out,
+                                    int32_t* out, int32_t* error_flag) {
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_out; i += step) {
+    const int64_t col =
+        i < n_prefix ? (int64_t)__ldg(device_indices + start + i) : generated_start + (i - n_prefix);
+    int32_t v = -1;
+    if (col >= 0 && col < row_len) v = __ldg(row + col);
+    else if (error_flag != nullptr) *error_flag = 1;
+    out[i] = v;
+  }
+}
+
 int split_count(int batch) {
   // About 8 resident blocks per SM in total, at most 256 per request.
   long long want = (long long)kNumSMs * 8 / (batch > 0 ? batch : 1);
@@ -241,6 +261,25 @@ extern "C" int akv_write_row_slots(const int64_t* pointers, const void* rows, in
                                                                  : 1024);
   write_row_slots_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       pointers, rows, rows_is64, columns, columns_is64, values, values_is64, n);
+  return launch_status();
+}
+
+extern "C" int akv_active_slots(const int32_t* row, int64_t row_len,
+                                const int32_t* device_indices, int64_t start, int64_t n_indices,
+                                int64_t generated_start, int64_t raw_end, int32_t* out,
+                                int32_t* error_flag, void* stream) {
+  using namespace akv;
+  if (row_len < 0 || start < 0 || n_indices < start || generated_start < 0)
+    return AKV_ERR_INVALID;
+  const int64_t n_prefix = n_indices - start;
+  const int64_t n_gen = raw_end > generated_start ? raw_end - generated_start : 0;
+  const int64_t n_out = n_prefix + n_gen;
+  if (n_out == 0) return AKV_OK;
+  if (!row || !out || (n_prefix > 0 && !device_indices)) return AKV_ERR_INVALID;
+  const int64_t want = (n_out + kThreads - 1) / kThreads;
+  const int blocks = (int)(want < (int64_t)kNumSMs * 4 ? want : (int64_t)kNumSMs * 4);
+  active_slots_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      row, row_len, device_indices, start, n_prefix, generated_start, n_out, out, error_flag);
   return launch_status();
 }
 

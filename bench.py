@@ -484,6 +484,7 @@ def run_ours(args):
                                 max(5, min(args.steps // 20, 20)))
     compiler = bench_compiler(dev, world, rank, 3, 20)
     prefill = bench_prefill(dev, world, rank, 3, 5)
+    gather = bench_active_slots(dev, world, rank, 3, 20)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -530,6 +531,7 @@ def run_ours(args):
             "decode_attention": attention,
             "event_compiler": compiler,
             "prefill_attention": prefill,
+            "active_slots": gather,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
@@ -750,6 +752,57 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0)
                      "ms_per_launch": round(full_ms, 4)},
         "gpu_launches_per_step": layers,
         "cpu_baseline": cpu,
+    }
+
+
+def bench_active_slots(dev, world, rank, warmup, steps, seed=0):
+    """PD offload / transfer gather (context_transfer.py:110-128): the active
+    slots of 64 requests (c3 lengths, 1.13M prompt tokens, about 70 % kept,
+    128 generated tokens each), one ``active_slots`` launch per request as the
+    reference's per-request call.  Bytes per slot: 4 B raw index + 4 B row
+    slot read + 4 B written."""
+    from akv_b200 import workloads
+    from akv_b200.context_transfer import active_slots
+
+    prog = workloads.c3_program()
+    rng = np.random.default_rng(seed)
+    reqs = []
+    total = 0
+    for T in prog.token_counts:
+        T = int(T)
+        raw = np.flatnonzero(rng.random(T) < 0.7).astype(np.int32)
+        row = torch.from_numpy(rng.permutation(4 * (T + 128))[: T + 128].astype(np.int32))
+        reqs.append((row.to(dev), torch.from_numpy(raw).to(dev), T, T + 128))
+        total += len(raw) + 128
+    outs = [torch.empty(len(r[1]) + 128, dtype=torch.int32, device=dev) for r in reqs]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for (row, idx, gen0, end), out in zip(reqs, outs):
+            active_slots(row, idx, 0, gen0, end, out=out)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = dist_max(t0.elapsed_time(t1) / steps, world)
+    peak, peak_kind = measured_peak()
+    gbs = 12.0 * total / (ms / 1e3) / 1e9
+    return {
+        "metric": "active-slot gather slots/s", "value": round(total / (ms / 1e3), 1),
+        "unit": "slots/s", "ms_per_step": round(ms, 4), "n_gpus": world, "scaling": "replicas",
+        "config": {"workload": "c3 offload", "requests": len(reqs), "slots": total,
+                   "launches_per_step": len(reqs)},
+        "roofline": {"bound": "hbm", "kernel": "active_slots_kernel (64 launches)",
+                     "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_source": peak_kind,
+                     "algorithmic_bytes_per_step": 12 * total},
+        "gpu_launches_per_step": len(reqs),
     }
 
 

@@ -430,6 +430,23 @@ int akv_write_row_slots(const int64_t* pointers, const void* rows, int32_t rows_
                         const void* columns, int32_t columns_is64, const void* values,
                         int32_t values_is64, int64_t n, void* stream);
 
+/*
+ * Active slots of one request row, for offload / load and PD transfer.
+ * Replaces the gather of request_active_slots
+ * (akv/system/sglang/srt/disaggregation/context_transfer.py:110-128):
+ * out = concat(row[device_indices[start:n_indices]],
+ *              row[generated_start:raw_end]),
+ * n_indices - start + max(0, raw_end - generated_start) int32 slots, in one
+ * launch.  row: DEVICE int32 [row_len] (a req_to_token row); device_indices:
+ * DEVICE int32 raw indices of the surviving prompt tokens.  The caller
+ * computes start and generated_start on the host from the decode view (the
+ * window's first visible position), as the reference does.  An index outside
+ * the row reads as slot -1 and sets *error_flag (NULL: not reported).
+ */
+int akv_active_slots(const int32_t* row, int64_t row_len, const int32_t* device_indices,
+                     int64_t start, int64_t n_indices, int64_t generated_start, int64_t raw_end,
+                     int32_t* out, int32_t* error_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

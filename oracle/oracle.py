@@ -18,6 +18,8 @@ reference project root):
   this build, composed from ``compile_layout`` per request (one drop event at
   the end of the prompt, one Reposition at its last token), the decode view
   and the freed-slot rule of occurrence.py:711-714 / 936-964
+* ``active_slots``, ``active_lengths``
+                         srt/disaggregation/context_transfer.py:110-138
 * ``decode_attention``   paged GQA decode with learned sinks, the math of
   layers/attention/context_backend.py:254-272 (sink LSE correction) over the
   registry's ``kv_indptr / kv_indices``; float64.
@@ -437,3 +439,43 @@ def prefill_attention(q, k_pool, v_pool, qo_indptr, kv_indptr, kv_indices, birth
         sig = np.where(np.isfinite(lse), sig, 0.0)
         out = out * sig[:, :, None]
     return out, lse
+
+
+# --------------------------------------------------------------------------
+# Active-slot gather (offload / load / PD transfer)
+# --------------------------------------------------------------------------
+
+
+def active_slot_ranges(raw_indices, positions, prompt_length, next_position, raw_end,
+                       window=None):
+    """(start, generated_start) of srt/disaggregation/context_transfer.py:116-122:
+    the first decode-view entry a sliding window still reads and the first
+    generated raw position it reads."""
+    start = 0
+    generated_start = int(prompt_length)
+    if window is not None:
+        lower = int(next_position) + int(raw_end) - int(prompt_length) - int(window)
+        start = int(np.searchsorted(np.asarray(positions), lower))
+        generated_start += max(0, lower - int(next_position))
+    return start, generated_start
+
+
+def active_slots(row, raw_indices, positions, prompt_length, next_position, raw_end,
+                 window=None):
+    """context_transfer.py:110-128: row[raw_indices[start:]] followed by
+    row[generated_start:raw_end] (int32)."""
+    row = np.asarray(row)
+    start, generated_start = active_slot_ranges(raw_indices, positions, prompt_length,
+                                                next_position, raw_end, window)
+    prefix = row[np.asarray(raw_indices, np.int64)[start:]]
+    tail = row[generated_start:int(raw_end)]
+    return np.concatenate((prefix, tail)).astype(np.int32)
+
+
+def active_lengths(raw_indices, positions, prompt_length, next_position, raw_end, window):
+    """context_transfer.py:131-138: (full active length, windowed length)."""
+    generated = max(0, int(raw_end) - int(prompt_length))
+    full = len(raw_indices) + generated
+    lower = int(next_position) + generated - int(window)
+    start = int(np.searchsorted(np.asarray(positions), lower))
+    return full, len(raw_indices) - start + min(generated, int(window))
