@@ -77,6 +77,8 @@ SIGNATURES = {
     ],
     "akv_write_row_slots": [_P, _P, _I32, _P, _I32, _P, _I32, _I64, _P],
     "akv_active_slots": [_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P],
+    "akv_active_slots_batch": [_P, _P, _P, _I32, _P, _P, _P],
+    "akv_active_slots_chunk": [],
     "akv_compile_layouts_max_repositions": [],
     "akv_compile_layouts_workspace_bytes": [_I32, _I64, _I64, _I64],
     "akv_compile_layouts_batch_bytes": [],
@@ -103,6 +105,7 @@ RESTYPES = {
     "akv_compile_layouts_batch_bytes": _I64,
     "akv_decode_attention_ctas_per_sm": _I32,
     "akv_context_attention_query_block": _I64,
+    "akv_active_slots_chunk": _I64,
 }
 
 

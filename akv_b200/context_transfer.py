@@ -107,3 +107,75 @@ def request_active_lengths(req, raw_end, window):
     lower = view.next_position + generated - window
     start = int(np.searchsorted(view.positions, lower))
     return full, len(view.raw_indices) - start + min(generated, window)
+
+
+class ActiveSlotGather:
+    """``active_slots`` for many requests in one launch (C ABI
+    ``akv_active_slots_batch``).  ``plan`` validates the per-request ranges
+    on the host and stages them (one host-to-device copy); ``run`` launches
+    on the current stream and returns the packed int32 slots, request r's at
+    ``offsets[r]:offsets[r + 1]``.  The rows and index vectors must stay
+    alive while planned launches may run."""
+
+    def __init__(self, device):
+        device = torch.device(device)
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = device
+        self.total = 0
+        self.n = 0
+
+    def plan(self, rows, device_indices, starts, generated_starts, raw_ends, n_indices=None):
+        n = len(rows)
+        if not (len(device_indices) == len(starts) == len(generated_starts) == len(raw_ends) == n):
+            raise ValueError("one row, index vector and range per request")
+        if n_indices is None:
+            n_indices = [len(x) for x in device_indices]
+        meta = np.zeros((max(n, 1), 6), np.int64)
+        offsets = np.zeros(n + 1, np.int64)
+        for r in range(n):
+            row, idx = rows[r], device_indices[r]
+            if row.dtype != torch.int32 or row.ndim != 1 or row.device != self.device or \
+                    row.stride(0) != 1:
+                raise ValueError("rows must be contiguous int32 vectors on the device")
+            if idx.dtype != torch.int32 or idx.device != self.device or not idx.is_contiguous():
+                raise ValueError("device_indices must be contiguous int32 on the device")
+            s, g, e, k = int(starts[r]), int(generated_starts[r]), int(raw_ends[r]), \
+                int(n_indices[r])
+            if not 0 <= s <= k <= len(idx) or g < 0:
+                raise ValueError("active slot ranges out of bounds")
+            meta[r] = (row.data_ptr(), row.numel(), idx.data_ptr(), s, k - s, g)
+            offsets[r + 1] = offsets[r] + (k - s) + max(0, e - g)
+        self._keep = (list(rows), list(device_indices))
+        # One block per CHUNK outputs of a request: {request, first output}.
+        chunk = int(_native.lib.akv_active_slots_chunk())
+        lengths = np.diff(offsets)
+        counts = (lengths + chunk - 1) // chunk
+        req = np.repeat(np.arange(n, dtype=np.int64), counts)
+        first = (np.arange(len(req)) - np.repeat(np.cumsum(counts) - counts, counts)) * chunk
+        blocks = np.stack((req, first), 1).astype(np.int64)
+        staged = torch.from_numpy(np.concatenate(
+            (meta.reshape(-1), offsets, blocks.astype(np.int32).view(np.int64).reshape(-1)
+             if len(blocks) else np.zeros(0, np.int64)))).pin_memory()
+        dev = staged.to(self.device, non_blocking=True)
+        self.meta = dev[: meta.size]
+        self.offsets_dev = dev[meta.size: meta.size + n + 1]
+        self.chunks = dev[meta.size + n + 1:]
+        self.n_chunks = len(blocks)
+        self._staged = staged  # the pinned source must outlive the copy
+        self.offsets = offsets
+        self.n, self.total = n, int(offsets[-1])
+        return self
+
+    def run(self, out=None, error_flag=None):
+        if out is None:
+            out = torch.empty(self.total, dtype=torch.int32, device=self.device)
+        elif out.dtype != torch.int32 or out.device != self.device or out.numel() < self.total \
+                or not out.is_contiguous():
+            raise ValueError("out must be a contiguous int32 device vector of the packed length")
+        status = _native.lib.akv_active_slots_batch(
+            _native.ptr(self.meta), _native.ptr(self.offsets_dev), _native.ptr(self.chunks),
+            self.n_chunks, _native.ptr(out), _native.ptr(error_flag),
+            _native.stream_of(self.device))
+        _native.check(status, "active_slots_batch")
+        return out[: self.total]

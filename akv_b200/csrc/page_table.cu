@@ -186,6 +186,35 @@ __global__ void active_slots_kernel(const int32_t* row, int64_t row_len,
   }
 }
 
+// The same gather for a batch of requests in one launch.  meta holds, per
+// request, {row address, row length, raw-index address, start, n_prefix,
+// generated_start}; out_offsets is the CSR of the packed output; block b
+// covers outputs [chunk[b].y, chunk[b].y + kGatherChunk) of request
+// chunk[b].x (the host splits each request into such chunks).
+constexpr int kGatherChunk = 1024;
+
+__global__ void __launch_bounds__(kThreads) active_slots_batch_kernel(
+    const int64_t* meta, const int64_t* out_offsets, const int2* chunks, int32_t* out,
+    int32_t* error_flag) {
+  const int2 c = chunks[blockIdx.x];
+  const int64_t* m = meta + 6 * (int64_t)c.x;
+  const int32_t* row = reinterpret_cast<const int32_t*>(__ldg(m));
+  const int64_t row_len = __ldg(m + 1);
+  const int32_t* idx = reinterpret_cast<const int32_t*>(__ldg(m + 2));
+  const int64_t start = __ldg(m + 3), n_prefix = __ldg(m + 4), gen0 = __ldg(m + 5);
+  const int64_t o0 = __ldg(out_offsets + c.x), n = __ldg(out_offsets + c.x + 1) - o0;
+#pragma unroll
+  for (int j = 0; j < kGatherChunk / kThreads; ++j) {
+    const int64_t k = (int64_t)c.y + j * kThreads + threadIdx.x;
+    if (k >= n) break;
+    const int64_t col = k < n_prefix ? (int64_t)__ldg(idx + start + k) : gen0 + (k - n_prefix);
+    int32_t v = -1;
+    if (col >= 0 && col < row_len) v = __ldg(row + col);
+    else if (error_flag != nullptr) *error_flag = 1;
+    out[o0 + k] = v;
+  }
+}
+
 int split_count(int batch) {
   // About 8 resident blocks per SM in total, at most 256 per request.
   long long want = (long long)kNumSMs * 8 / (batch > 0 ? batch : 1);
@@ -280,6 +309,20 @@ extern "C" int akv_active_slots(const int32_t* row, int64_t row_len,
   const int blocks = (int)(want < (int64_t)kNumSMs * 4 ? want : (int64_t)kNumSMs * 4);
   active_slots_kernel<<<blocks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       row, row_len, device_indices, start, n_prefix, generated_start, n_out, out, error_flag);
+  return launch_status();
+}
+
+extern "C" int64_t akv_active_slots_chunk(void) { return akv::kGatherChunk; }
+
+extern "C" int akv_active_slots_batch(const int64_t* meta, const int64_t* out_offsets,
+                                      const int32_t* chunks, int32_t n_chunks, int32_t* out,
+                                      int32_t* error_flag, void* stream) {
+  using namespace akv;
+  if (n_chunks < 0) return AKV_ERR_INVALID;
+  if (n_chunks == 0) return AKV_OK;
+  if (!meta || !out_offsets || !chunks || !out) return AKV_ERR_INVALID;
+  active_slots_batch_kernel<<<n_chunks, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      meta, out_offsets, reinterpret_cast<const int2*>(chunks), out, error_flag);
   return launch_status();
 }
 

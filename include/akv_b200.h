@@ -447,6 +447,21 @@ int akv_active_slots(const int32_t* row, int64_t row_len, const int32_t* device_
                      int64_t start, int64_t n_indices, int64_t generated_start, int64_t raw_end,
                      int32_t* out, int32_t* error_flag, void* stream);
 
+/*
+ * akv_active_slots for a batch of requests in one launch (an offload or a
+ * transfer of many requests; no reference counterpart -- the reference
+ * gathers request by request).  meta: DEVICE int64 [n_requests][6] =
+ * {row address, row length, raw-index address, start, n_prefix =
+ * n_indices - start, generated_start}; out_offsets: DEVICE int64
+ * [n_requests + 1], request r's slots at out[out_offsets[r] ..], each of
+ * length n_prefix + max(0, raw_end - generated_start); chunks: DEVICE int32
+ * [n_chunks][2] = {request, first output of the request}, every request cut
+ * into pieces of akv_active_slots_chunk() outputs (one block each).
+ */
+int64_t akv_active_slots_chunk(void);
+int akv_active_slots_batch(const int64_t* meta, const int64_t* out_offsets, const int32_t* chunks,
+                           int32_t n_chunks, int32_t* out, int32_t* error_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,3 +72,26 @@ def test_empty_gather_returns_an_empty_vector():
     row = torch.arange(4, dtype=torch.int32, device=dev)
     idx = torch.tensor([0, 1], dtype=torch.int32, device=dev)
     assert active_slots(row, idx, 2, 4, 4).numel() == 0
+
+
+def test_batched_gather_matches_per_request_goldens():
+    from akv_b200.context_transfer import ActiveSlotGather
+    from oracle import oracle
+
+    dev = torch.device("cuda")
+    rows, idxs, starts, gens, ends, wants = [], [], [], [], [], []
+    for c, window, want, _ in golden_cases():
+        start, gen0 = oracle.active_slot_ranges(c["raw"], c["positions"], c["prompt"],
+                                                c["next_position"], c["raw_end"], window)
+        rows.append(torch.from_numpy(c["row"]).to(dev))
+        idxs.append(torch.from_numpy(c["raw"]).to(dev))
+        starts.append(start)
+        gens.append(gen0)
+        ends.append(c["raw_end"])
+        wants.append(want)
+    g = ActiveSlotGather(dev).plan(rows, idxs, starts, gens, ends)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = g.run(error_flag=flag).cpu().numpy()
+    assert int(flag.item()) == 0
+    for r, want in enumerate(wants):
+        np.testing.assert_array_equal(out[g.offsets[r]: g.offsets[r + 1]], want)
