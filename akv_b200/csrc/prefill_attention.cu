@@ -389,6 +389,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
   return (uint64_t)((smem_addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+// The same for an MN-major operand wider than one 64-element swizzle atom:
+// lbo_bytes is the distance between consecutive atoms along MN.
+__device__ __forceinline__ uint64_t sw128_desc_mn(uint32_t smem_addr, uint32_t lbo_bytes) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
 // Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, A
 // K-major, B K-major (b_mn = 0) or MN-major (1), M = 128, N.
 __host__ __device__ constexpr uint32_t f16_idesc(int n, int b_mn) {
@@ -851,11 +857,32 @@ int launch_prefill_tc(const PrefillParams& p, int n_items, int num_kv_heads, cud
 // frees its tensor memory.
 // ---------------------------------------------------------------------------
 constexpr int kWsThreads = 288;
-constexpr int kWsAhead = kTcStages - 2;  // tiles loaded ahead of the one in the softmax
-constexpr int kWsRowOff = kTcPosOff + kTcStages * kTcKeys * 4;  // [2][2][128] max, [2][128] sum
-constexpr int kWsBarOff = kWsRowOff + 6 * 128 * 4;
-constexpr int kWsSmemUsed = kWsBarOff + 128 + 1024;
-constexpr int kWsSmem = kWsSmemUsed > 80 * 1024 ? kWsSmemUsed : 80 * 1024;
+// Shared-memory and TMEM layout per head_dim.  Rows of D bf16 are stored as
+// D / 64 swizzle atoms of 128 bytes (atom a of every row, then atom a + 1).
+// head_dim 64: 5 stages (loads three tiles ahead), two CTAs per SM;
+// head_dim 128: 4 stages (two ahead), one CTA per SM.  TMEM: S / P buffers
+// in columns 0-63 and 64-127, O in the top D columns.
+template <int D>
+struct WsCfg {
+  static constexpr int kStages = D == 64 ? 5 : 4;
+  static constexpr int kAhead = kStages - 2;  // tiles loaded ahead of the one in the softmax
+  static constexpr int kChunks = D / 8;       // 16-byte chunks per row
+  static constexpr int kQBytes = 128 * D * 2;
+  static constexpr int kKVBytes = kTcKeys * D * 2;
+  static constexpr int kStageBytes = 2 * kKVBytes;
+  static constexpr int kPosOff = kQBytes + kStages * kStageBytes;
+  static constexpr int kRowOff = kPosOff + kStages * kTcKeys * 4;  // [2][2][128] max, [2][128] sum
+  static constexpr int kBarOff = kRowOff + 6 * 128 * 4;
+  static constexpr int kSmemUsed = kBarOff + 128 + 1024;
+  static constexpr int kSmem = D == 64 && kSmemUsed < 80 * 1024 ? 80 * 1024 : kSmemUsed;
+  static constexpr int kColO = kTcCols - D;
+  static constexpr int kMinBlocks = D == 64 ? 2 : 1;
+  static_assert(kAhead >= 2, "the loop signals tile t+1 from copies issued a tile earlier");
+};
+// Byte offset of 16-byte chunk c of row r in a swizzled tile of `rows` rows.
+__device__ __forceinline__ uint32_t sw_chunk(int rows, int r, int c) {
+  return (uint32_t)((c >> 3) * rows * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
@@ -884,8 +911,14 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
   return true;
 }
 
-__global__ void __launch_bounds__(kWsThreads, 2)
+template <int D>
+__global__ void __launch_bounds__(kWsThreads, WsCfg<D>::kMinBlocks)
 prefill_attention_tc_ws_kernel(const PrefillParams p) {
+  using C = WsCfg<D>;
+  constexpr int kTcStages = C::kStages, kWsAhead = C::kAhead;
+  constexpr int kTcQBytes = C::kQBytes, kTcKVBytes = C::kKVBytes, kTcStageBytes = C::kStageBytes;
+  constexpr int kTcPosOff = C::kPosOff, kWsRowOff = C::kRowOff, kWsBarOff = C::kBarOff;
+  constexpr int kColO = C::kColO, kOCols = D / 2;  // O columns per softmax warp
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -942,9 +975,13 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
             tc_fence_after();
             const uint32_t kb = stage_k(t);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_ss(tmem + kColS + (t & 1) * kTcKeys, sw128_desc(sQ + 32 * k),
-                     sw128_desc(kb + 32 * k), f16_idesc(kTcKeys, 0), k > 0);
+            for (int k = 0; k < D / 16; ++k) {  // 16 dims a step; atom k / 4, 32 bytes each
+              const uint32_t off = (uint32_t)(32 * (k & 3));
+              mma_ss(tmem + kColS + (t & 1) * kTcKeys,
+                     sw128_desc(sQ + (k >> 2) * 128 * 128 + off),
+                     sw128_desc(kb + (k >> 2) * kTcKeys * 128 + off), f16_idesc(kTcKeys, 0),
+                     k > 0);
+            }
             umma_commit(bar_s0 + 8 * (t & 1));
           }
         }
@@ -957,9 +994,11 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
             const uint32_t pb = tmem + kColS + (u & 1) * kTcKeys;
 #pragma unroll
             for (int k = 0; k < kTcKeys / 16; ++k) {  // 16 keys: 8 P columns, 2 KiB of V
-              mma_ts(tmem + kColO, pb + 8 * k, sw128_desc(vb + 2048 * k), f16_idesc(64, 1), 1);
-              mma_ts(tmem + kColO, pb + 32 + 8 * k, sw128_desc(vb + 2048 * k), f16_idesc(64, 1),
-                     1);
+              // V is MN-major (dims contiguous): atoms of 64 dims, 8 KiB apart.
+              const uint64_t vd = D == 64 ? sw128_desc(vb + 2048 * k)
+                                          : sw128_desc_mn(vb + 2048 * k, kTcKeys * 128);
+              mma_ts(tmem + kColO, pb + 8 * k, vd, f16_idesc(D, 1), 1);
+              mma_ts(tmem + kColO, pb + 32 + 8 * k, vd, f16_idesc(D, 1), 1);
             }
             umma_commit(bar_o);
           }
@@ -1001,15 +1040,15 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       if (my_quarter == 0) kpos[my_key] = r.pos;
       const int bytes = r.pos != INT_MAX ? 16 : 0;
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int c = my_quarter * 2 + i;
-        const uint32_t off = my_key * 128 + ((c ^ (my_key & 7)) * 16);
+      for (int i = 0; i < C::kChunks / 4; ++i) {
+        const int c = my_quarter * (C::kChunks / 4) + i;
+        const uint32_t off = sw_chunk(kTcKeys, my_key, c);
         cp_async16(kb + off, p.k + r.slot * p.k_ss + hk * p.k_sh + c * 8, bytes);
         cp_async16(vb + off, p.v + r.slot * p.v_ss + hk * p.v_sh + c * 8, bytes);
       }
     };
 
-    // Q: row r = (query r / 8, head r % 8); two threads per row, four chunks each.
+    // Q: row r = (query r / 8, head r % 8); two threads per row, half the chunks each.
     const int q_local = qb0 + (row >> 3);
     const int head = hk * kGroupP + (row & 7);
     const bool row_valid = q_local < nq_req;
@@ -1017,9 +1056,9 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       const __nv_bfloat16* src = p.q + (long long)(qo0 + (row_valid ? q_local : 0)) * p.q_st +
                                  (long long)head * p.q_sh;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = half * 4 + i;
-        cp_async16(sQ + row * 128 + ((c ^ (row & 7)) * 16), src + c * 8, row_valid ? 16 : 0);
+      for (int i = 0; i < C::kChunks / 2; ++i) {
+        const int c = half * (C::kChunks / 2) + i;
+        cp_async16(sQ + sw_chunk(128, row, c), src + c * 8, row_valid ? 16 : 0);
       }
     }
     // Groups: Q + tile 0, then tiles 1 .. kWsAhead - 1, one group each.
@@ -1029,11 +1068,12 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       cp_async_commit();
     }
     KeyRef next = fetch(kWsAhead);
-    {  // O = 0 (every P.V accumulates): this warp's 32 columns
+    {  // O = 0 (every P.V accumulates): this warp's D / 2 columns
       uint32_t z[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) z[i] = 0u;
-      tmem_st32(trow + kColO + 32 * half, z);
+#pragma unroll
+      for (int c = 0; c < kOCols; c += 32) tmem_st32(trow + kColO + kOCols * half + c, z);
       tmem_wait_st();
     }
     if (n_tiles > 0) {  // Q and tile 0 landed
@@ -1144,13 +1184,16 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       if (__any_sync(0xffffffffu, rescale)) {
         ws_wait(bar_o, (uint32_t)(tile - 1) & 1u, abort);
         tc_fence_after();
-        float o[32];
-        tmem_ld32(trow + kColO + 32 * half, o);
-        tmem_wait_ld32(o);
-        uint32_t r[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
-        tmem_st32(trow + kColO + 32 * half, r);
+        for (int c = 0; c < kOCols; c += 32) {
+          float o[32];
+          tmem_ld32(trow + kColO + kOCols * half + c, o);
+          tmem_wait_ld32(o);
+          uint32_t r[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
+          tmem_st32(trow + kColO + kOCols * half + c, r);
+        }
       }
       tmem_st16(sbuf + half * (kHalf / 2), hi);
       tmem_st16(sbuf + 32 + half * (kHalf / 2), lo);
@@ -1169,23 +1212,26 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       tc_fence_after();
     }
     if (!__any_sync(0xffffffffu, *abort != 0)) {
-      float o[32];
-      tmem_ld32(trow + kColO + 32 * half, o);  // every lane: the load is warp-wide
-      tmem_wait_ld32(o);
       float den = s_sum[row] + s_sum[128 + row];
       const float mb = m_used == -INFINITY ? 0.f : m_used;
       if (p.sinks) den += fast_exp2(p.sinks[head] * kLog2e - mb);
       const float inv = den > 0.f ? 1.f / den : 0.f;
       __nv_bfloat16* dst = p.out + (long long)(qo0 + q_local) * p.o_st +
-                           (long long)head * p.o_sh + 32 * half;
+                           (long long)head * p.o_sh + kOCols * half;
 #pragma unroll
-      for (int c = 0; c < 4 && row_valid; ++c) {
-        uint4 v;
-        v.x = pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv);
-        v.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-        v.z = pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-        v.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + 8 * c) = v;
+      for (int cb = 0; cb < kOCols; cb += 32) {
+        float o[32];
+        tmem_ld32(trow + kColO + kOCols * half + cb, o);  // every lane: warp-wide load
+        tmem_wait_ld32(o);
+#pragma unroll
+        for (int c = 0; c < 4 && row_valid; ++c) {
+          uint4 v;
+          v.x = pack_bf16(o[8 * c] * inv, o[8 * c + 1] * inv);
+          v.y = pack_bf16(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+          v.z = pack_bf16(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+          v.w = pack_bf16(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+          *reinterpret_cast<uint4*>(dst + cb + 8 * c) = v;
+        }
       }
       if (p.lse && row_valid && half == 0)
         p.lse[(long long)(qo0 + q_local) * p.num_q_heads + head] =
@@ -1202,12 +1248,15 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
   }
 }
 
+template <int D>
 int launch_prefill_tc_ws(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
-  if (cudaFuncSetAttribute(prefill_attention_tc_ws_kernel,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem) != cudaSuccess)
+  using C = WsCfg<D>;
+  if (cudaFuncSetAttribute(prefill_attention_tc_ws_kernel<D>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
     return AKV_ERR_CUDA;
   if (n_items > 0)
-    prefill_attention_tc_ws_kernel<<<dim3(n_items, num_kv_heads), kWsThreads, kWsSmem, s>>>(p);
+    prefill_attention_tc_ws_kernel<D>
+        <<<dim3(n_items, num_kv_heads), kWsThreads, C::kSmem, s>>>(p);
   return launch_status();
 }
 
@@ -1284,11 +1333,14 @@ extern "C" int akv_context_attention(
                          q_stride_head % 8 == 0 && out_stride_token % 8 == 0 &&
                          out_stride_head % 8 == 0;
   if (variant < 0 || variant > 3) return AKV_ERR_INVALID;
-  // The tcgen05 kernel takes row maxima of unscaled scores: sm_scale > 0.
-  const bool tc_ok = head_dim == 64 && aligned16 && sm_scale > 0.f;
-  if (variant >= 2 && !tc_ok) return AKV_ERR_UNSUPPORTED;
-  if (variant == 3 || (variant == 0 && tc_ok))
-    return launch_prefill_tc_ws(p, n_items, num_kv_heads, s);
+  // The tcgen05 kernels take row maxima of unscaled scores: sm_scale > 0.
+  const bool tc_ok = aligned16 && sm_scale > 0.f;
+  if (variant == 2 && !(tc_ok && head_dim == 64)) return AKV_ERR_UNSUPPORTED;
+  if (variant == 3 && !(tc_ok && (head_dim == 64 || head_dim == 128))) return AKV_ERR_UNSUPPORTED;
+  if (variant == 3 || (variant == 0 && tc_ok)) {
+    if (head_dim == 64) return launch_prefill_tc_ws<64>(p, n_items, num_kv_heads, s);
+    if (head_dim == 128) return launch_prefill_tc_ws<128>(p, n_items, num_kv_heads, s);
+  }
   if (variant == 2) return launch_prefill_tc(p, n_items, num_kv_heads, s);
   switch (head_dim) {
     case 64: return launch_prefill<64>(p, n_items, num_kv_heads, s);

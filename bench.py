@@ -637,7 +637,7 @@ def measured_tensor_peak():
         return 1590.0, "fallback"
 
 
-def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0):
+def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0, head_dim=64):
     """c4p: prefill of a new agent turn over the compacted cache -- 16
     requests, each a compacted prefix (lognormal length, median 8192, with
     position holes from dropped tokens) plus 1,024 new tokens; GPT-OSS-120B
@@ -647,7 +647,7 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0)
     from akv_b200 import workloads
     from akv_b200.context_prefill import ContextPrefillAttention
 
-    bs, new, hq_total, hkv_total, d, window = 16, 1024, 64, 8, 64, 128
+    bs, new, hq_total, hkv_total, d, window = 16, 1024, 64, 8, head_dim, 128
     hkv, hq = hkv_total // world, hq_total // world
     rng = np.random.default_rng(seed)
     prefix = workloads.c4_lengths(seed=seed, batch=bs)

@@ -97,6 +97,8 @@ CASES = [
     ([900], [130], 1, 128, 100, True),
     ([0], [1], 8, 64, -1, True),
     ([5000, 3000, 1], [96, 250, 70], 8, 64, 128, True),
+    ([2000, 5], [300, 64], 4, 128, 7, False),
+    ([3000, 700, 0], [130, 200, 33], 8, 128, 128, True),
 ]
 
 
@@ -104,10 +106,10 @@ CASES = [
 @pytest.mark.parametrize("case", range(len(CASES)))
 def test_prefill_matches_torch(case, variant):
     """variant 1 runs the mma.sync kernel, 2 the tcgen05 one (head_dim 64), 3 its
-    warp-specialised form."""
+    warp-specialised form (head_dim 64 and 128)."""
     prefix, queries, hkv, d, window, use_sinks = CASES[case]
-    if variant >= 2 and d != 64:
-        pytest.skip("the tcgen05 kernel covers head_dim 64")
+    if variant == 2 and d != 64:
+        pytest.skip("the simpler tcgen05 kernel covers head_dim 64")
     rng = np.random.default_rng(case)
     x = make_batch(rng, prefix, queries, hkv, d)
     sinks = torch.randn(8 * hkv, device="cuda") if use_sinks else None
@@ -117,12 +119,12 @@ def test_prefill_matches_torch(case, variant):
     torch.testing.assert_close(out.float(), want, atol=ATOL, rtol=RTOL)
 
 
-@pytest.mark.parametrize("variant", [1, 2, 3])
-def test_prefill_matches_float64_oracle_with_lse(variant):
+@pytest.mark.parametrize("variant,d", [(1, 64), (2, 64), (3, 64), (1, 128), (3, 128)])
+def test_prefill_matches_float64_oracle_with_lse(variant, d):
     from oracle import oracle
 
     rng = np.random.default_rng(42)
-    hkv, d, window = 2, 64, 33
+    hkv, window = 2, 33
     x = make_batch(rng, [150, 40], [37, 20], hkv, d)
     sinks = torch.randn(8 * hkv, device="cuda")
     lse = torch.empty(x["q"].shape[0], 8 * hkv, device="cuda")
