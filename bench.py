@@ -82,6 +82,9 @@ def parse_args():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     p.add_argument("--layers", type=int, default=None,
                    help="override the workload's layer count (a smaller cut for ncu captures)")
+    p.add_argument("--shard", type=int, default=1, choices=[1, 2, 4, 8],
+                   help="c4: run one rank's share of an N-way KV-head split on this GPU "
+                        "(8/N KV heads; a profiling aid, not a multi-GPU run)")
     p.add_argument("--variant", type=int, default=0,
                    help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05, "
                         "3 tcgen05 warp-specialised)")
@@ -542,7 +545,7 @@ def run_ours(args):
     return 0
 
 
-def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36):
+def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1):
     """c4: batch 128, 64 query / 8 KV heads (split 8/N per rank), head_dim 64,
     bf16, lognormal KV lengths (median 8192, sigma 1.0, max 65536), 36 layers
     alternating sliding window 128 and full attention, per-head sinks.  One
@@ -553,8 +556,8 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36):
     from akv_b200.context_attention import DecodeAttention
 
     bs, hq_total, hkv_total, d, window = 128, 64, 8, 64, 128
-    hkv = hkv_total // world
-    hq = hq_total // world
+    hkv = hkv_total // (world * shard)
+    hq = hq_total // (world * shard)
     lengths = workloads.c4_lengths(seed=seed, batch=bs)
     rng = np.random.default_rng(seed)
     total = int(lengths.sum())
@@ -980,7 +983,7 @@ def main():
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         res = bench_attention(dev, world, rank, max(3, args.warmup), max(3, args.steps // 20),
-                              layers=args.layers or 36)
+                              layers=args.layers or 36, shard=args.shard)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
