@@ -60,21 +60,31 @@ class ContextPrefillAttention:
         if len(qpos) != qo[-1] or len(kpos) != kv[-1]:
             raise ValueError("Context attention positions must align with Q/KV")
         window = -1 if window is None or window < 0 else int(window)
-        items = []
+        # Items of QUERY_BLOCK queries, paired: consecutive blocks of one
+        # request sit next to each other (a padding item {-1, 0, 0, 0}
+        # completes a request's odd block), so a CTA with two query tiles
+        # takes a pair and shares its K/V tiles; kernels with one tile per
+        # CTA skip the padding.  Pairs with the most keys come first.
+        pairs = []
         for b in range(len(qo) - 1):
             a, e, x, y = int(qo[b]), int(qo[b + 1]), int(kv[b]), int(kv[b + 1])
             n_prefix = y - x
             positions = np.concatenate((kpos[x:y], qpos[a:e]))
             if len(positions) > 1 and np.any(np.diff(positions) <= 0):
                 raise ValueError("context positions must increase along each request")
+            blocks = []
             for q0 in range(0, e - a, QUERY_BLOCK):
                 q1 = min(q0 + QUERY_BLOCK, e - a)
                 hi = n_prefix + q1
                 lo = 0
                 if window >= 0:
                     lo = int(np.searchsorted(positions[:hi], qpos[a + q0] - window))
-                items.append((b, q0, lo, hi))
-        items.sort(key=lambda it: it[2] - it[3])  # most keys first
+                blocks.append((b, q0, lo, hi))
+            for i in range(0, len(blocks), 2):
+                second = blocks[i + 1] if i + 1 < len(blocks) else (-1, 0, 0, 0)
+                pairs.append((blocks[i], second))
+        pairs.sort(key=lambda pr: -max(it[3] - it[2] for it in pr if it[0] >= 0))
+        items = [it for pr in pairs for it in pr]
         work = torch.tensor(items if items else np.zeros((0, 4)), dtype=torch.int32)
         self.work = work.reshape(-1, 4).pin_memory().to(self.device, non_blocking=True)
         self.qo_indptr = torch.from_numpy(qo.astype(np.int32)).to(self.device, non_blocking=True)
@@ -102,9 +112,10 @@ class ContextPrefillAttention:
             sinks=None, out=None, lse=None, variant=0):
         """q [tokens, Hq, D] bf16; pools [slots, Hkv, D] bf16; index and
         position vectors int32 on the device.  ``variant``: 0 the faster
-        kernel for the shape (3 for head_dim 64, else 1), 1 the mma.sync
+        kernel for the shape (3 at head_dim 64, 4 at 128), 1 the mma.sync
         kernel, 2 the tcgen05 / TMEM kernel (head_dim 64), 3 its
-        warp-specialised form."""
+        warp-specialised form (head_dim 64 and 128), 4 the warp-specialised
+        form with two query tiles per CTA."""
         if q.dtype != torch.bfloat16 or k_pool.dtype != torch.bfloat16 or \
                 v_pool.dtype != torch.bfloat16:
             raise ValueError("context attention runs on bf16 q / K / V")

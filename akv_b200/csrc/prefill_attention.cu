@@ -81,6 +81,7 @@ prefill_attention_kernel(const PrefillParams p) {
   static_assert(D % 16 == 0 && C::kCph % C::kTpk == 0, "head_dim split");
   extern __shared__ __align__(128) unsigned char smem[];
   const int4 w = p.work[blockIdx.x];
+  if (w.x < 0) return;  // padding item of a query-tile pair
   const int hk = blockIdx.y;  // KV head
   const int b = w.x, qb0 = w.y, key_lo = w.z, key_hi = w.w;
   const int qo0 = p.qo_indptr[b], nq_req = p.qo_indptr[b + 1] - qo0;
@@ -525,6 +526,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   __shared__ int s_abort;
 
   const int4 w = p.work[blockIdx.x];
+  if (w.x < 0) return;  // padding item of a query-tile pair
   const int hk = blockIdx.y;
   const int b = w.x, qb0 = w.y, key_lo = w.z, key_hi = w.w;
   const int qo0 = p.qo_indptr[b], nq_req = p.qo_indptr[b + 1] - qo0;
@@ -856,28 +858,38 @@ int launch_prefill_tc(const PrefillParams& p, int n_items, int num_kv_heads, cud
 // each named barrier and the end, where the CTA sets *error_flag = 2 and
 // frees its tensor memory.
 // ---------------------------------------------------------------------------
-constexpr int kWsThreads = 288;
-// Shared-memory and TMEM layout per head_dim.  Rows of D bf16 are stored as
-// D / 64 swizzle atoms of 128 bytes (atom a of every row, then atom a + 1).
-// head_dim 64: 5 stages (loads three tiles ahead), two CTAs per SM;
-// head_dim 128: 4 stages (two ahead), one CTA per SM.  TMEM: S / P buffers
-// in columns 0-63 and 64-127, O in the top D columns.
-template <int D>
+// Shared-memory and TMEM layout per head_dim D and query tiles per CTA QT
+// (one query tile = 16 queries x 8 heads = 128 rows).  Rows of D bf16 are
+// stored as D / 64 swizzle atoms of 128 bytes (atom a of every row, then
+// atom a + 1).  head_dim 64: 5 stages (loads three tiles ahead); head_dim
+// 128: 4 stages (two ahead).  QT = 1: two CTAs per SM at head_dim 64, one at
+// 128; QT = 2: one CTA per SM whose two query tiles share every K/V tile.
+// TMEM per query tile: 256 columns, S / P buffers in columns 0-63 and
+// 64-127, O in the top D columns.
+template <int D, int QT>
 struct WsCfg {
+  static constexpr int kThreads = 32 * (8 * QT + 1);  // 8 softmax warps per tile + the MMA warp
+  static constexpr int kLoaders = 256 * QT;           // softmax threads, which also load
   static constexpr int kStages = D == 64 ? 5 : 4;
   static constexpr int kAhead = kStages - 2;  // tiles loaded ahead of the one in the softmax
   static constexpr int kChunks = D / 8;       // 16-byte chunks per row
-  static constexpr int kQBytes = 128 * D * 2;
+  static constexpr int kTpk = kLoaders / kTcKeys;     // loader threads per key
+  static constexpr int kCpt = kChunks / kTpk;         // chunks of K (and of V) per loader thread
+  static constexpr int kQBytes = 128 * D * 2;         // one query tile
   static constexpr int kKVBytes = kTcKeys * D * 2;
   static constexpr int kStageBytes = 2 * kKVBytes;
-  static constexpr int kPosOff = kQBytes + kStages * kStageBytes;
-  static constexpr int kRowOff = kPosOff + kStages * kTcKeys * 4;  // [2][2][128] max, [2][128] sum
-  static constexpr int kBarOff = kRowOff + 6 * 128 * 4;
-  static constexpr int kSmemUsed = kBarOff + 128 + 1024;
-  static constexpr int kSmem = D == 64 && kSmemUsed < 80 * 1024 ? 80 * 1024 : kSmemUsed;
-  static constexpr int kColO = kTcCols - D;
-  static constexpr int kMinBlocks = D == 64 ? 2 : 1;
+  static constexpr int kStageOff = QT * kQBytes;
+  static constexpr int kPosOff = kStageOff + kStages * kStageBytes;
+  static constexpr int kRowOff = kPosOff + kStages * kTcKeys * 4;
+  static constexpr int kRowBytes = 6 * 128 * 4;       // per tile: [2][2][128] max, [2][128] sum
+  static constexpr int kBarOff = kRowOff + QT * kRowBytes;
+  static constexpr int kSmemUsed = kBarOff + 256 + 1024;
+  static constexpr int kSmem = QT == 1 && D == 64 && kSmemUsed < 80 * 1024 ? 80 * 1024 : kSmemUsed;
+  static constexpr int kCols = 256 * QT;              // TMEM columns allocated
+  static constexpr int kColO = 256 - D;               // within a query tile's 256 columns
+  static constexpr int kMinBlocks = QT == 1 && D == 64 ? 2 : 1;
   static_assert(kAhead >= 2, "the loop signals tile t+1 from copies issued a tile earlier");
+  static_assert(kCpt >= 1 && kChunks % kTpk == 0, "K/V chunks split over the loaders");
 };
 // Byte offset of 16-byte chunk c of row r in a swizzled tile of `rows` rows.
 __device__ __forceinline__ uint32_t sw_chunk(int rows, int r, int c) {
@@ -887,14 +899,19 @@ __device__ __forceinline__ uint32_t sw_chunk(int rows, int r, int c) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// 64-thread named barrier 1 + q of the two warps of lane quadrant q
-// (immediate barrier ids, so the kernel reserves five barriers, not sixteen).
+// 64-thread named barrier 1 + q of the two warps of pair q (query tile
+// q / 4, lane quadrant q % 4); immediate ids, so the kernel reserves only the
+// barriers it uses.
 __device__ __forceinline__ void pair_sync(int q) {
   switch (q) {
     case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
     case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
     case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
-    default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+    case 3: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+    case 4: asm volatile("bar.sync 5, 64;" ::: "memory"); break;
+    case 5: asm volatile("bar.sync 6, 64;" ::: "memory"); break;
+    case 6: asm volatile("bar.sync 7, 64;" ::: "memory"); break;
+    default: asm volatile("bar.sync 8, 64;" ::: "memory"); break;
   }
 }
 // Bounded wait that gives up at once after the CTA aborted.
@@ -911,50 +928,76 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
   return true;
 }
 
-template <int D>
-__global__ void __launch_bounds__(kWsThreads, WsCfg<D>::kMinBlocks)
+template <int D, int QT>
+__global__ void __launch_bounds__(WsCfg<D, QT>::kThreads, WsCfg<D, QT>::kMinBlocks)
 prefill_attention_tc_ws_kernel(const PrefillParams p) {
-  using C = WsCfg<D>;
+  using C = WsCfg<D, QT>;
   constexpr int kTcStages = C::kStages, kWsAhead = C::kAhead;
-  constexpr int kTcQBytes = C::kQBytes, kTcKVBytes = C::kKVBytes, kTcStageBytes = C::kStageBytes;
-  constexpr int kTcPosOff = C::kPosOff, kWsRowOff = C::kRowOff, kWsBarOff = C::kBarOff;
+  constexpr int kTcKVBytes = C::kKVBytes, kTcStageBytes = C::kStageBytes;
+  constexpr int kTcPosOff = C::kPosOff, kWsBarOff = C::kBarOff;
   constexpr int kColO = C::kColO, kOCols = D / 2;  // O columns per softmax warp
+  constexpr int kIssuer = 8 * QT;                  // the MMA warp
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* smem = smem_raw + (base - raw);
-  const uint32_t sQ = base;
+  // Barriers: kv[S] (tile landed), then per query tile s[2] and p[2] (by
+  // tile parity), o (every P.V) and done (the last P.V).  A waiter on a
+  // phase parity must never be two phases behind the barrier: P(t) arrives
+  // on p[t & 1] because a warp can store P(t) while the MMA warp still
+  // waits for P(t-1), and the epilogue waits on `done`, whose only phase
+  // completes with the last P.V, because o may be anywhere from two phases
+  // behind that to complete when a warp gets there.
   const uint32_t bars = base + kWsBarOff;
-  const uint32_t bar_s0 = bars + 8 * kTcStages, bar_p = bar_s0 + 16, bar_o = bar_p + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kWsBarOff + 8 * kTcStages + 32);
-  float* s_max = reinterpret_cast<float*>(smem + kWsRowOff);  // [tile parity][half][128]
-  float* s_sum = s_max + 4 * 128;                             // [half][128]
+  auto bar_s = [&](int qt, int buf) { return bars + 8u * (kTcStages + 2 * qt + buf); };
+  auto bar_p = [&](int qt, int buf) { return bars + 8u * (kTcStages + 2 * QT + 2 * qt + buf); };
+  auto bar_o = [&](int qt) { return bars + 8u * (kTcStages + 4 * QT + qt); };
+  auto bar_done = [&](int qt) { return bars + 8u * (kTcStages + 5 * QT + qt); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kWsBarOff + 8 * (kTcStages + 6 * QT));
   __shared__ int s_abort;
   volatile int* abort = &s_abort;
   auto bar_kv = [&](int tile) { return bars + 8u * (uint32_t)(tile % kTcStages); };
   auto kv_parity = [&](int tile) { return (uint32_t)(tile / kTcStages) & 1u; };
 
-  const int4 w = p.work[blockIdx.x];
+  // Work items: query tile q of this CTA takes item QT * blockIdx.x + q.  The
+  // host pairs consecutive 16-query blocks of one request; a second item
+  // with a negative request is padding (its rows are past the request's
+  // queries).  The CTA walks the union of the items' key ranges.
+  const int4 w0 = p.work[QT * blockIdx.x];
+  if (w0.x < 0) return;
   const int hk = blockIdx.y;
-  const int b = w.x, qb0 = w.y, key_lo = w.z, key_hi = w.w;
+  const int b = w0.x;
+  int key_lo = w0.z, key_hi = w0.w;
+#pragma unroll
+  for (int q = 1; q < QT; ++q) {
+    const int4 wq = p.work[QT * blockIdx.x + q];
+    if (wq.x >= 0) {
+      key_lo = min(key_lo, wq.z);
+      key_hi = max(key_hi, wq.w);
+    }
+  }
   const int qo0 = p.qo_indptr[b], nq_req = p.qo_indptr[b + 1] - qo0;
   const int kv0 = p.kv_indptr[b], n_prefix = p.kv_indptr[b + 1] - kv0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tiles = (key_hi - key_lo + kTcKeys - 1) / kTcKeys;
   if (p.error_flag != nullptr && *reinterpret_cast<volatile int*>(p.error_flag) == 2) return;
 
-  if (warp == 0) {  // TMEM: two S / P buffers and O
+  if (warp == 0) {  // TMEM: per query tile two S / P buffers and O
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(kTcCols));
+                 "r"(C::kCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    for (int st = 0; st < kTcStages; ++st) mbar_init(bars + 8 * st, 256);
-    mbar_init(bar_s0, 1);
-    mbar_init(bar_s0 + 8, 1);
-    mbar_init(bar_p, 8);
-    mbar_init(bar_o, 1);
+    for (int st = 0; st < kTcStages; ++st) mbar_init(bars + 8 * st, C::kLoaders);
+    for (int q = 0; q < QT; ++q) {
+      mbar_init(bar_s(q, 0), 1);
+      mbar_init(bar_s(q, 1), 1);
+      mbar_init(bar_p(q, 0), 8);
+      mbar_init(bar_p(q, 1), 8);
+      mbar_init(bar_o(q), 1);
+      mbar_init(bar_done(q), 1);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_abort = 0;
   }
@@ -962,54 +1005,78 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  auto stage_k = [&](int tile) { return base + kTcQBytes + (tile % kTcStages) * kTcStageBytes; };
+  auto stage_k = [&](int tile) {
+    return base + C::kStageOff + (tile % kTcStages) * kTcStageBytes;
+  };
 
-  if (warp == 8) {
+  if (warp == kIssuer) {
     // ---- MMA issuer (one thread) ----
     if (lane == 0) {
       for (int t = 0; t <= n_tiles; ++t) {
-        if (t < n_tiles) {  // S(t): K(t) landed; buffer t & 1 free once P(t-2).V(t-2) is done
+        if (t < n_tiles) {  // S(t): K(t) landed; buffers t & 1 free once every P(t-2).V(t-2) is done
           ws_wait(bar_kv(t), kv_parity(t), abort);
-          if (t >= 2) ws_wait(bar_o, (uint32_t)(t - 2) & 1u, abort);
+          if (t >= 2)
+            for (int q = 0; q < QT; ++q) ws_wait(bar_o(q), (uint32_t)(t - 2) & 1u, abort);
           if (!*abort) {
             tc_fence_after();
             const uint32_t kb = stage_k(t);
 #pragma unroll
-            for (int k = 0; k < D / 16; ++k) {  // 16 dims a step; atom k / 4, 32 bytes each
-              const uint32_t off = (uint32_t)(32 * (k & 3));
-              mma_ss(tmem + kColS + (t & 1) * kTcKeys,
-                     sw128_desc(sQ + (k >> 2) * 128 * 128 + off),
-                     sw128_desc(kb + (k >> 2) * kTcKeys * 128 + off), f16_idesc(kTcKeys, 0),
-                     k > 0);
+            for (int q = 0; q < QT; ++q) {
+              const uint32_t sq = base + q * C::kQBytes;
+#pragma unroll
+              for (int k = 0; k < D / 16; ++k) {  // 16 dims a step; atom k / 4, 32 bytes each
+                const uint32_t off = (uint32_t)(32 * (k & 3));
+                mma_ss(tmem + 256 * q + kColS + (t & 1) * kTcKeys,
+                       sw128_desc(sq + (k >> 2) * 128 * 128 + off),
+                       sw128_desc(kb + (k >> 2) * kTcKeys * 128 + off), f16_idesc(kTcKeys, 0),
+                       k > 0);
+              }
+              umma_commit(bar_s(q, t & 1));
             }
-            umma_commit(bar_s0 + 8 * (t & 1));
           }
         }
-        if (t >= 1) {  // O += P(t-1) V(t-1) once every warp has stored P(t-1)
+        if (t >= 1) {  // O += P(t-1) V(t-1) once every warp of the tile has stored P(t-1)
           const int u = t - 1;
-          ws_wait(bar_p, (uint32_t)u & 1u, abort);
-          if (!*abort) {
+          const uint32_t vb = stage_k(u) + kTcKVBytes;
+#pragma unroll
+          for (int q = 0; q < QT; ++q) {
+            ws_wait(bar_p(q, u & 1), (uint32_t)(u >> 1) & 1u, abort);
+            if (*abort) continue;
             tc_fence_after();
-            const uint32_t vb = stage_k(u) + kTcKVBytes;
-            const uint32_t pb = tmem + kColS + (u & 1) * kTcKeys;
+            const uint32_t pb = tmem + 256 * q + kColS + (u & 1) * kTcKeys;
 #pragma unroll
             for (int k = 0; k < kTcKeys / 16; ++k) {  // 16 keys: 8 P columns, 2 KiB of V
               // V is MN-major (dims contiguous): atoms of 64 dims, 8 KiB apart.
               const uint64_t vd = D == 64 ? sw128_desc(vb + 2048 * k)
                                           : sw128_desc_mn(vb + 2048 * k, kTcKeys * 128);
-              mma_ts(tmem + kColO, pb + 8 * k, vd, f16_idesc(D, 1), 1);
-              mma_ts(tmem + kColO, pb + 32 + 8 * k, vd, f16_idesc(D, 1), 1);
+              mma_ts(tmem + 256 * q + kColO, pb + 8 * k, vd, f16_idesc(D, 1), 1);
+              mma_ts(tmem + 256 * q + kColO, pb + 32 + 8 * k, vd, f16_idesc(D, 1), 1);
             }
-            umma_commit(bar_o);
+            umma_commit(bar_o(q));
+            if (u == n_tiles - 1) umma_commit(bar_done(q));
           }
         }
       }
     }
     __syncwarp();
   } else {
-    // ---- loaders + softmax: warp w serves TMEM lanes 32 (w % 4) .., column half w / 4 ----
-    const int row = ((warp & 3) << 5) | lane, half = warp >> 2;
-    const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    // ---- loaders + softmax: warp w serves query tile w / 8, TMEM lanes
+    //      32 (w % 4) .. and column half (w / 4) % 2 ----
+    const int qt = warp >> 3;
+    const int row = ((warp & 3) << 5) | lane, half = (warp >> 2) & 1;
+    const uint32_t trow = tmem + 256 * qt + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t sQ = base + qt * C::kQBytes;
+    float* s_max = reinterpret_cast<float*>(smem + C::kRowOff + qt * C::kRowBytes);  // [parity][half][128]
+    float* s_sum = s_max + 4 * 128;                                                 // [half][128]
+    // This tile's queries: its item, or the 16 after the first item when the
+    // item is padding (all of those rows are past the request's queries).
+    int qb0 = w0.y;
+#pragma unroll
+    for (int q = 1; q < QT; ++q)
+      if (qt == q) {
+        const int4 wq = p.work[QT * blockIdx.x + q];
+        qb0 = wq.x >= 0 ? wq.y : w0.y + q * kQBlock;
+      }
     auto key_slot_pos = [&](int j, long long& slot, int& pos) {
       if (j < n_prefix) {
         slot = __ldg(p.kv_indices + kv0 + j);
@@ -1023,7 +1090,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
         slot = 0;
       }
     };
-    const int my_key = tid >> 2, my_quarter = tid & 3;
+    const int my_key = tid / C::kTpk, my_quarter = tid % C::kTpk;
     struct KeyRef {
       long long slot;
       int pos;
@@ -1040,8 +1107,8 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       if (my_quarter == 0) kpos[my_key] = r.pos;
       const int bytes = r.pos != INT_MAX ? 16 : 0;
 #pragma unroll
-      for (int i = 0; i < C::kChunks / 4; ++i) {
-        const int c = my_quarter * (C::kChunks / 4) + i;
+      for (int i = 0; i < C::kCpt; ++i) {
+        const int c = my_quarter * C::kCpt + i;
         const uint32_t off = sw_chunk(kTcKeys, my_key, c);
         cp_async16(kb + off, p.k + r.slot * p.k_ss + hk * p.k_sh + c * 8, bytes);
         cp_async16(vb + off, p.v + r.slot * p.v_ss + hk * p.v_sh + c * 8, bytes);
@@ -1098,7 +1165,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
         mbar_arrive(bar_kv(tile + 1));
       }
       // 1. S(t) -> this thread's 32 values of its row.
-      ws_wait(bar_s0 + 8 * (tile & 1), (uint32_t)(tile >> 1) & 1u, abort);
+      ws_wait(bar_s(qt, tile & 1), (uint32_t)(tile >> 1) & 1u, abort);
       tc_fence_after();
       const uint32_t sbuf = trow + kColS + (tile & 1) * kTcKeys;
       float s[kHalf];
@@ -1142,7 +1209,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       // Both warps of the quadrant have their maxima in place and have read
       // S(t), which P(t) overwrites below.
       tc_fence_before();
-      pair_sync(warp & 3);
+      pair_sync(warp & 3 | qt << 2);
       tc_fence_after();
       const float bm = fmaxf(mx[row], mx[128 + row]);
 
@@ -1182,7 +1249,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       // 4. Rescale this warp's half of O after P(t-1).V(t-1) (warp-wide TMEM
       //    access), then P(t) over S(t): hi in columns 0-31, lo in 32-63.
       if (__any_sync(0xffffffffu, rescale)) {
-        ws_wait(bar_o, (uint32_t)(tile - 1) & 1u, abort);
+        ws_wait(bar_o(qt), (uint32_t)(tile - 1) & 1u, abort);
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < kOCols; c += 32) {
@@ -1200,15 +1267,15 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p);
+      if (lane == 0) mbar_arrive(bar_p(qt, tile & 1));
     }
     cp_async_wait<0>();
 
     // ---- epilogue ----
     s_sum[half * 128 + row] = l;
-    pair_sync(warp & 3);
-    if (n_tiles > 0) {
-      ws_wait(bar_o, (uint32_t)(n_tiles - 1) & 1u, abort);
+    pair_sync(warp & 3 | qt << 2);
+    if (n_tiles > 0) {  // O is final once the last P.V is done
+      ws_wait(bar_done(qt), 0u, abort);
       tc_fence_after();
     }
     if (!__any_sync(0xffffffffu, *abort != 0)) {
@@ -1244,21 +1311,25 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTcCols));
+                 "r"(C::kCols));
   }
 }
 
-template <int D>
+// n_items counts 16-query items; with QT = 2 they come in pairs (the host
+// pads the list to an even length).
+template <int D, int QT>
 int launch_prefill_tc_ws(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
-  using C = WsCfg<D>;
-  if (cudaFuncSetAttribute(prefill_attention_tc_ws_kernel<D>,
+  using C = WsCfg<D, QT>;
+  if (n_items % QT) return AKV_ERR_INVALID;
+  if (cudaFuncSetAttribute(prefill_attention_tc_ws_kernel<D, QT>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
     return AKV_ERR_CUDA;
   if (n_items > 0)
-    prefill_attention_tc_ws_kernel<D>
-        <<<dim3(n_items, num_kv_heads), kWsThreads, C::kSmem, s>>>(p);
+    prefill_attention_tc_ws_kernel<D, QT>
+        <<<dim3(n_items / QT, num_kv_heads), C::kThreads, C::kSmem, s>>>(p);
   return launch_status();
 }
+
 
 template <int D>
 int launch_prefill(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
@@ -1332,14 +1403,22 @@ extern "C" int akv_context_attention(
                          (reinterpret_cast<uintptr_t>(out) & 15) == 0 && q_stride_token % 8 == 0 &&
                          q_stride_head % 8 == 0 && out_stride_token % 8 == 0 &&
                          out_stride_head % 8 == 0;
-  if (variant < 0 || variant > 3) return AKV_ERR_INVALID;
+  if (variant < 0 || variant > 4) return AKV_ERR_INVALID;
   // The tcgen05 kernels take row maxima of unscaled scores: sm_scale > 0.
   const bool tc_ok = aligned16 && sm_scale > 0.f;
   if (variant == 2 && !(tc_ok && head_dim == 64)) return AKV_ERR_UNSUPPORTED;
-  if (variant == 3 && !(tc_ok && (head_dim == 64 || head_dim == 128))) return AKV_ERR_UNSUPPORTED;
+  if (variant >= 3 && !(tc_ok && (head_dim == 64 || head_dim == 128))) return AKV_ERR_UNSUPPORTED;
+  // Default: one query tile per CTA at head_dim 64 (two CTAs per SM), two
+  // query tiles per CTA at head_dim 128 (one CTA per SM either way).
+  if (variant == 0 && tc_ok && head_dim == 128 && n_items % 2 == 0)
+    return launch_prefill_tc_ws<128, 2>(p, n_items, num_kv_heads, s);
   if (variant == 3 || (variant == 0 && tc_ok)) {
-    if (head_dim == 64) return launch_prefill_tc_ws<64>(p, n_items, num_kv_heads, s);
-    if (head_dim == 128) return launch_prefill_tc_ws<128>(p, n_items, num_kv_heads, s);
+    if (head_dim == 64) return launch_prefill_tc_ws<64, 1>(p, n_items, num_kv_heads, s);
+    if (head_dim == 128) return launch_prefill_tc_ws<128, 1>(p, n_items, num_kv_heads, s);
+  }
+  if (variant == 4) {
+    if (head_dim == 64) return launch_prefill_tc_ws<64, 2>(p, n_items, num_kv_heads, s);
+    if (head_dim == 128) return launch_prefill_tc_ws<128, 2>(p, n_items, num_kv_heads, s);
   }
   if (variant == 2) return launch_prefill_tc(p, n_items, num_kv_heads, s);
   switch (head_dim) {

@@ -87,7 +87,7 @@ def parse_args():
                         "(8/N KV heads; a profiling aid, not a multi-GPU run)")
     p.add_argument("--variant", type=int, default=0,
                    help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05, "
-                        "3 tcgen05 warp-specialised)")
+                        "3 tcgen05 warp-specialised, 4 the same with two query tiles per CTA)")
     return p.parse_args()
 
 
@@ -747,7 +747,8 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0,
                    "head_dim": d, "layers": layers, "sliding_window": window, "sinks": True,
                    "positions": "prefix with holes (about a third dropped)"},
         "roofline": {"bound": "tensor",
-                     "kernel": {1: "prefill_attention_kernel", 2: "prefill_attention_tc_kernel"}
+                     "kernel": {1: "prefill_attention_kernel", 2: "prefill_attention_tc_kernel",
+                                4: "prefill_attention_tc_ws_kernel, two query tiles"}
                      .get(variant, "prefill_attention_tc_ws_kernel") + " (full layer)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,

@@ -398,10 +398,14 @@ int akv_decode_attention(
  * (key_hi = P_b + last query + 1; key_lo = first key the window can reach);
  * built on the host from the CPU positions (akv_b200/context_prefill.py).
  * A slot outside [0, num_slots) is read as slot 0 and sets *error_flag.
- * variant: 0 = the faster kernel for the shape (variant 3 where it
- * applies, else 1), 1 = the mma.sync kernel, 2 = the tcgen05 / TMEM kernel,
- * 3 = its warp-specialised form (2 and 3: head_dim 64, 16-byte aligned q
- * and out rows, sm_scale > 0; AKV_ERR_UNSUPPORTED otherwise).  A tcgen05
+ * work may hold padding items {-1, 0, 0, 0}; items 2i and 2i + 1 are two
+ * consecutive blocks of one request or a block and a padding item (the plan
+ * of akv_b200/context_prefill.py lays them out so), which variant 4 needs.
+ * variant: 0 = the faster kernel for the shape, 1 = the mma.sync kernel,
+ * 2 = the tcgen05 / TMEM kernel (head_dim 64), 3 = its warp-specialised
+ * form (head_dim 64 and 128), 4 = the warp-specialised form with the two
+ * items of a pair in one CTA (n_items even); 2-4 need 16-byte aligned q and
+ * out rows and sm_scale > 0 (AKV_ERR_UNSUPPORTED otherwise).  A tcgen05
  * wait that does not complete sets *error_flag to 2 (the CTA frees its
  * tensor memory and returns).
  */

@@ -102,11 +102,13 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3], ids=["auto", "mma_sync", "tcgen05", "tcgen05_ws"])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4],
+                         ids=["auto", "mma_sync", "tcgen05", "tcgen05_ws", "tcgen05_ws_2tiles"])
 @pytest.mark.parametrize("case", range(len(CASES)))
 def test_prefill_matches_torch(case, variant):
     """variant 1 runs the mma.sync kernel, 2 the tcgen05 one (head_dim 64), 3 its
-    warp-specialised form (head_dim 64 and 128)."""
+    warp-specialised form (head_dim 64 and 128), 4 that form with two query
+    tiles per CTA."""
     prefix, queries, hkv, d, window, use_sinks = CASES[case]
     if variant == 2 and d != 64:
         pytest.skip("the simpler tcgen05 kernel covers head_dim 64")
@@ -119,7 +121,8 @@ def test_prefill_matches_torch(case, variant):
     torch.testing.assert_close(out.float(), want, atol=ATOL, rtol=RTOL)
 
 
-@pytest.mark.parametrize("variant,d", [(1, 64), (2, 64), (3, 64), (1, 128), (3, 128)])
+@pytest.mark.parametrize("variant,d", [(1, 64), (2, 64), (3, 64), (4, 64), (1, 128), (3, 128),
+                                       (4, 128)])
 def test_prefill_matches_float64_oracle_with_lse(variant, d):
     from oracle import oracle
 
