@@ -1062,7 +1062,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
   } else {
     // ---- loaders + softmax: warp w serves query tile w / 8, TMEM lanes
     //      32 (w % 4) .. and column half (w / 4) % 2 ----
-    const int qt = warp >> 3;
+    const int qt = QT == 1 ? 0 : warp >> 3;
     const int row = ((warp & 3) << 5) | lane, half = (warp >> 2) & 1;
     const uint32_t trow = tmem + 256 * qt + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t sQ = base + qt * C::kQBytes;
@@ -1209,7 +1209,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       // Both warps of the quadrant have their maxima in place and have read
       // S(t), which P(t) overwrites below.
       tc_fence_before();
-      pair_sync(warp & 3 | qt << 2);
+      pair_sync(warp & 3 | qt << 2);  // qt is 0 when QT == 1: barriers 1-4 only
       tc_fence_after();
       const float bm = fmaxf(mx[row], mx[128 + row]);
 
