@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libakv_b200
 
 AKV_OK, AKV_ERR_INVALID, AKV_ERR_CUDA, AKV_ERR_UNSUPPORTED = 0, 1, 2, 3
 AKV_F16, AKV_BF16, AKV_F32 = 0, 1, 2
+GATHER_OUT64, GATHER_LITERAL, GATHER_SEG64 = 1, 2, 4
 DROP_RING_UNDERFLOW, DROP_RING_OVERFLOW, DROP_BAD_RANGE, DROP_NO_ACTIVE = 1, 2, 4, 8
 
 DTYPE_CODE = {torch.float16: AKV_F16, torch.bfloat16: AKV_BF16, torch.float32: AKV_F32}
@@ -79,6 +80,8 @@ SIGNATURES = {
     "akv_active_slots": [_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P],
     "akv_active_slots_batch": [_P, _P, _P, _I32, _P, _P, _P],
     "akv_active_slots_chunk": [],
+    "akv_gather_slots_chunk": [],
+    "akv_gather_slots": [_P, _P, _I32, _P, _P, _P],
     "akv_compile_layouts_max_repositions": [],
     "akv_compile_layouts_workspace_bytes": [_I32, _I64, _I64, _I64],
     "akv_compile_layouts_batch_bytes": [],
@@ -106,6 +109,7 @@ RESTYPES = {
     "akv_decode_attention_ctas_per_sm": _I32,
     "akv_context_attention_query_block": _I64,
     "akv_active_slots_chunk": _I64,
+    "akv_gather_slots_chunk": _I64,
 }
 
 

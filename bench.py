@@ -488,6 +488,7 @@ def run_ours(args):
     compiler = bench_compiler(dev, world, rank, 3, 20)
     prefill = bench_prefill(dev, world, rank, 3, 5)
     gather = bench_active_slots(dev, world, rank, 3, 20)
+    occurrence = bench_occurrence(dev, world, rank, 3, 20)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -535,6 +536,7 @@ def run_ours(args):
             "event_compiler": compiler,
             "prefill_attention": prefill,
             "active_slots": gather,
+            "occurrence_binding": occurrence,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
@@ -852,6 +854,145 @@ def bench_active_slots(dev, world, rank, warmup, steps, seed=0, copies=12):
         "eager_call_ms": round(ms_eager, 4),
         "per_request_launches_ms": round(ms_per_request, 4),
         "gpu_launches_per_step": 1,
+    }
+
+
+def bench_occurrence(dev, world, rank, warmup, steps, seed=0, requests=16, prefix=9000,
+                     queries=1024, copies=600):
+    """Occurrence binding of one prefill forward (the device part of
+    OccurrenceState.advance, srt/context_system/occurrence.py:644-755, and
+    the scheduler's concatenation, sglang.patch:3133-3180), c4p shape:
+    ``requests`` requests, each with ``prefix`` slots of earlier chunks,
+    ``queries`` new query slots and ``copies`` extra slots for repositioned
+    copies.  Per request: occurrence slots (all rows, mostly in order),
+    copy sources and destinations, retained and retired slots, copy position
+    pairs.  The index arrays are synthetic with those sizes (the ownership
+    decisions that produce them are scheduler CPU work, the same in both
+    arms).  Timed: this build's one copy + one launch (host packing
+    included), the kernel alone (graph replay over prepacked programs), and
+    the reference's per-request torch sequence (concatenation, one pageable
+    copy, gathers, int32 casts, then four batch concatenations).  Bytes per
+    output: 8 B index + 8 B slot read + 8 B written (4 B for int32 fields)."""
+    from akv_b200 import _native
+    from akv_b200.context_occurrence import SlotGather
+
+    rng = np.random.default_rng(seed)
+    stream = torch.cuda.current_stream(dev)
+    reqs = []
+    for _ in range(requests):
+        old = torch.from_numpy(rng.permutation(40 * prefix)[:prefix]).to(dev)
+        q = torch.from_numpy(rng.permutation(40 * queries)[:queries]).to(dev)
+        e = torch.from_numpy(rng.permutation(40 * copies)[:copies]).to(dev)
+        total = prefix + queries + copies
+        occ = np.arange(total)
+        swap = rng.random(total) < 0.1
+        occ[swap] = rng.integers(0, total, int(swap.sum()))
+        src = rng.integers(0, prefix, copies)
+        dst = np.arange(prefix + queries, total)
+        keep = np.sort(rng.choice(total, total - copies, replace=False))
+        release = np.setdiff1d(np.arange(total), keep)
+        pairs = rng.integers(0, 10**5, 2 * copies)
+        reqs.append(dict(seg=(old, q, e), occ=occ, src=src, dst=dst, keep=keep,
+                         release=release, pairs=pairs))
+    n_slots = sum(len(r["occ"]) for r in reqs)
+    n_copy = requests * copies
+    out_slots = torch.empty(n_slots, dtype=torch.int64, device=dev)
+    i32 = torch.empty(4 * n_copy, dtype=torch.int32, device=dev)
+    succ = [torch.empty(len(r["keep"]), dtype=torch.int64, device=dev) for r in reqs]
+    retired = [torch.empty(len(r["release"]), dtype=torch.int64, device=dev) for r in reqs]
+
+    def queue():
+        g = SlotGather(dev)
+        s = c = 0
+        for j, r in enumerate(reqs):
+            k = len(r["occ"])
+            g.add(out_slots[s:s + k], r["occ"], r["seg"])
+            g.add(i32[c:c + copies], r["src"], r["seg"])
+            g.add(i32[n_copy + c:n_copy + c + copies], r["dst"], r["seg"])
+            g.add(i32[2 * n_copy + 2 * c:2 * n_copy + 2 * c + 2 * copies], r["pairs"],
+                  literal=True)
+            g.add(succ[j], r["keep"], r["seg"])
+            g.add(retired[j], r["release"], r["seg"])
+            s, c = s + k, c + copies
+        return g
+
+    def ours():
+        queue().launch()
+
+    def reference_sequence():
+        slots, sources, dests, positions = [], [], [], []
+        for r in reqs:
+            all_slots = torch.cat(r["seg"])
+            fields = (r["occ"], r["src"], r["dst"], r["keep"], r["release"], r["pairs"])
+            offsets = np.r_[0, np.cumsum([len(f) for f in fields])]
+            packed = torch.from_numpy(np.concatenate(fields).astype(np.int64)).to(
+                dev, non_blocking=True)
+            o, sr, ds, kp, rl, pr = (packed[a:b] for a, b in zip(offsets[:-1], offsets[1:]))
+            slots.append(all_slots[o])
+            sources.append(all_slots[sr].to(torch.int32))
+            dests.append(all_slots[ds].to(torch.int32))
+            all_slots[kp], all_slots[rl]  # noqa: B018 - successor slots, retired slots
+            positions.append(pr.reshape(-1, 2).to(torch.int32))
+        torch.cat(slots), torch.cat(sources), torch.cat(dests), torch.cat(positions)  # noqa: B018
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return dist_max(t0.elapsed_time(t1) / steps, world)
+
+    ms_ours = timed(ours)
+    ms_ref = timed(reference_sequence)
+    # kernel alone: the packed program resident on the device, graph replay
+    words, n_tasks, n_chunks = queue().pack()
+    prog = torch.from_numpy(words).to(dev)
+    base = prog.data_ptr()
+
+    def kernel():
+        st = _native.lib.akv_gather_slots(base, base + 96 * n_tasks, n_chunks,
+                                          base + 8 * (12 * n_tasks + n_chunks), None,
+                                          _native.stream_of(dev))
+        assert st == 0
+
+    kernel()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(steps):
+            kernel()
+    graph.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    graph.replay()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms_kernel = dist_max(t0.elapsed_time(t1) / steps, world)
+    del graph
+    n_out64 = n_slots + sum(len(r["keep"]) + len(r["release"]) for r in reqs)
+    gathered32 = 2 * n_copy
+    alg = 24 * n_out64 + 20 * gathered32 + 12 * 2 * n_copy
+    peak, peak_kind = measured_peak()
+    gbs = alg / (ms_kernel / 1e3) / 1e9
+    return {
+        "metric": "occurrence binding ms per forward", "value": round(ms_ours, 4),
+        "unit": "ms", "higher_is_better": False, "n_gpus": world, "scaling": "replicas",
+        "config": {"workload": "c4p forward", "requests": requests, "prefix_slots": prefix,
+                   "query_slots": queries, "copies": copies, "occurrence_slots": n_slots,
+                   "index_data": "synthetic, sizes of the c4p forward"},
+        "reference_torch_sequence_ms": round(ms_ref, 4),
+        "kernel_ms": round(ms_kernel, 4),
+        "roofline": {"bound": "hbm", "kernel": "gather_slots_kernel", "achieved": round(gbs, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": alg},
+        "gpu_launches_per_step": 1,
+        "reference_launches_per_step": requests * 10 + 4,
     }
 
 

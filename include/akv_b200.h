@@ -466,6 +466,39 @@ int64_t akv_active_slots_chunk(void);
 int akv_active_slots_batch(const int64_t* meta, const int64_t* out_offsets, const int32_t* chunks,
                            int32_t n_chunks, int32_t* out, int32_t* error_flag, void* stream);
 
+/*
+ * Occurrence slot gathers: the device binding of request-local page
+ * ownership between prefill forwards, for every request of a forward in one
+ * launch.  Replaces the per-request torch concatenation, gathers and casts of
+ * OccurrenceMaterialization.bind
+ * (akv/system/sglang/srt/context_system/occurrence.py:315-357),
+ * OccurrenceState.advance (:644-755) and OccurrenceState.terminal_slots
+ * (:757-768), and the scheduler's concatenation of their results
+ * (akv/system/sglang.patch:3133-3180).  The scheduler CPU keeps every
+ * ownership decision; only the slot binding runs here.
+ *
+ * tasks: DEVICE int64 [n_tasks][12], one output vector each:
+ *   [0] first index of the task in `indices`   [1] n outputs
+ *   [2] output address                         [3] flags (AKV_GATHER_*)
+ *       | n_segments << 8 (0..4)
+ *   [4..7] segment addresses                   [8..11] cumulative segment
+ *                                                      lengths
+ * For i < n: v = indices[first + i]; with AKV_GATHER_LITERAL, out[i] = v;
+ * else out[i] = -1 if v < 0, else element v of the concatenation of the
+ * segments (an index at or past its end writes -1 and sets *error_flag).
+ * Segments are int64 with AKV_GATHER_SEG64, else int32; out is int64 with
+ * AKV_GATHER_OUT64, else int32 (the low 32 bits, as a torch int32 cast).
+ * chunks: DEVICE int32 [n_chunks][2] = {task, first output of the task},
+ * every task cut into pieces of akv_gather_slots_chunk() outputs (one block
+ * each).  indices: DEVICE int64.  No reference counterpart as one call.
+ */
+#define AKV_GATHER_OUT64 1
+#define AKV_GATHER_LITERAL 2
+#define AKV_GATHER_SEG64 4
+int64_t akv_gather_slots_chunk(void);
+int akv_gather_slots(const int64_t* tasks, const int32_t* chunks, int32_t n_chunks,
+                     const int64_t* indices, int32_t* error_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,6 +20,11 @@ reference project root):
   and the freed-slot rule of occurrence.py:711-714 / 936-964
 * ``active_slots``, ``active_lengths``
                          srt/disaggregation/context_transfer.py:110-138
+* ``occurrence_advance``, ``occurrence_bind``, ``terminal_slots``
+                         srt/context_system/occurrence.py:644-755, 315-357,
+                         757-768 (request-local page ownership)
+* ``gather_slots``       the contract of ``akv_gather_slots`` (include/akv_b200.h)
+                         run over a packed program, to check the host packing
 * ``decode_attention``   paged GQA decode with learned sinks, the math of
   layers/attention/context_backend.py:254-272 (sink LSE correction) over the
   registry's ``kv_indptr / kv_indices``; float64.
@@ -479,3 +484,132 @@ def active_lengths(raw_indices, positions, prompt_length, next_position, raw_end
     lower = int(next_position) + generated - int(window)
     start = int(np.searchsorted(np.asarray(positions), lower))
     return full, len(raw_indices) - start + min(generated, int(window))
+
+
+def gather_slots(words, n_tasks, n_chunks, memory, chunk):
+    """The contract of ``akv_gather_slots`` (include/akv_b200.h) executed on
+    the CPU over a packed program: ``memory`` maps each address in the task
+    table to a writable numpy vector.  Returns how many times each output
+    element was written (every element must be written exactly once)."""
+    words = np.asarray(words, np.int64)
+    table = words[: 12 * n_tasks].reshape(n_tasks, 12)
+    chunks = words[12 * n_tasks: 12 * n_tasks + n_chunks].view(np.int32).reshape(-1, 2)
+    indices = words[12 * n_tasks + n_chunks:]
+    writes = {t: np.zeros(int(table[t, 1]), np.int64) for t in range(n_tasks)}
+    for task, first in chunks:
+        first_idx, n, out_addr, flags = (int(x) for x in table[task, :4])
+        n_seg = (flags >> 8) & 0xFF
+        ends = [int(e) for e in table[task, 8:8 + n_seg]]
+        segs = [memory[int(a)] if e > b else None
+                for a, e, b in zip(table[task, 4:4 + n_seg], ends, [0] + ends[:-1])]
+        out = memory[out_addr]
+        for k in range(first, min(first + chunk, n)):
+            v = int(indices[first_idx + k])
+            if not flags & 2:
+                if v < 0:
+                    v = -1
+                else:
+                    s = next((i for i, e in enumerate(ends) if v < e), None)
+                    if s is None:
+                        raise IndexError("slot gather index past its segments")
+                    v = int(segs[s][v - (ends[s - 1] if s else 0)])
+            out[k] = np.int64(v).astype(out.dtype)  # int32: the low 32 bits
+            writes[task][k] += 1
+    return writes
+
+
+def occurrence_advance(state, window, plan, query_slots, extra_slots, visible_until):
+    """srt/context_system/occurrence.py:644-755 (``OccurrenceState.advance``)
+    over numpy dicts: ``state`` holds slots, owned, canonical_rows,
+    terminal_rows, canonical_positions, exact_prefix_len and optionally
+    swa_resident; ``window`` and ``plan`` hold the fields of
+    ``OccurrenceWindow`` / ``OccurrenceMaterialization``.  Returns the
+    advance's fields and the successor state as numpy values."""
+    n = len(window["birth_occurrences"])
+    start, end = len(state["canonical_rows"]), len(plan["terminal_occurrences"])
+    n_old, n_q = len(state["slots"]), len(query_slots)
+    all_slots = np.concatenate((state["slots"], query_slots, extra_slots))
+    all_owned = np.r_[state["owned"], np.ones(n_q + len(extra_slots), bool)]
+    canonical = np.full(n, -1, np.int64)
+    canonical[:start] = state["canonical_rows"]
+    canonical[start:end] = np.arange(n_old, n_old + n_q)
+    terminal = np.full(n, -1, np.int64)
+    terminal[:start] = state["terminal_rows"]
+    source_rows = np.r_[canonical, terminal]
+    rows = plan["source_rows"]
+    occurrences = np.full(len(rows), -1, np.int64)
+    occurrences[rows >= 0] = source_rows[rows[rows >= 0]]
+    occurrences[plan["allocated_occurrences"]] = np.arange(n_old + n_q, len(all_slots))
+    copy_rows = source_rows[plan["copy_source_rows"]]
+    swa = state.get("swa_resident")
+    unused = None
+    if swa is not None:
+        swa = np.r_[swa, np.ones(n_q + len(extra_slots), bool)]
+        dst = occurrences[plan["copy_occurrences"]]
+        swa[dst] = swa[copy_rows]
+        unused = dst[~swa[dst]]
+    picked = plan["terminal_occurrences"]
+    kept = picked >= 0
+    terminal = np.full(end, -1, np.int64)
+    terminal[kept] = occurrences[picked[kept]]
+    pos = window["occurrence_positions"]
+    positions = pos[window["birth_occurrences"][:end]].copy()
+    positions[:start] = state["canonical_positions"]
+    same = positions == pos[window["terminal_occurrences"][:end]]
+    canonical = np.where(kept & same, terminal, canonical[:end])
+    future = visible_until[:end] > end
+    if end == n:
+        future[:] = False
+    canonical = np.where(future, canonical, -1)
+    retained = np.unique(np.r_[canonical[canonical >= 0], terminal[terminal >= 0]])
+    live = np.zeros(len(all_slots), bool)
+    live[retained] = True
+    retired = np.flatnonzero(all_owned & ~live)
+    remap = np.full(len(all_slots), -1, np.int64)
+    remap[retained] = np.arange(len(retained))
+    next_canonical = np.full(end, -1, np.int64)
+    next_canonical[canonical >= 0] = remap[canonical[canonical >= 0]]
+    next_terminal = np.full(end, -1, np.int64)
+    next_terminal[kept] = remap[terminal[kept]]
+    out = {
+        "occurrence_slots": all_slots[np.maximum(occurrences, 0)],
+        "copy_source_slots": all_slots[copy_rows].astype(np.int32),
+        "copy_destination_slots":
+            all_slots[occurrences[plan["copy_occurrences"]]].astype(np.int32),
+        "copy_position_pairs": np.asarray(plan["copy_position_pairs"]).reshape(-1, 2)
+        .astype(np.int32),
+        "retired_slots": all_slots[retired],
+        "successor": {
+            "slots": all_slots[retained], "owned": all_owned[retained],
+            "canonical_rows": next_canonical, "terminal_rows": next_terminal,
+            "canonical_positions": positions, "exact_prefix_len": state["exact_prefix_len"],
+        },
+    }
+    if swa is not None:
+        out["unused_swa_slots"] = all_slots[unused]
+        out["retired_swa_resident"] = swa[retired]
+        out["successor"]["swa_resident"] = swa[retained]
+    return out
+
+
+def occurrence_bind(plan, canonical_slots, terminal_slots, allocated_slots):
+    """srt/context_system/occurrence.py:315-357 (``OccurrenceMaterialization.bind``):
+    (slots, copy sources int32, copy destinations int32, pairs int32 [k, 2])."""
+    rows = plan["source_rows"]
+    sources = np.r_[canonical_slots, terminal_slots]
+    slots = np.full(len(rows), -1, np.asarray(canonical_slots).dtype)
+    reused = np.flatnonzero(rows >= 0)
+    slots[reused] = sources[rows[reused]]
+    slots[plan["allocated_occurrences"]] = allocated_slots
+    return (slots, sources[plan["copy_source_rows"]].astype(np.int32),
+            slots[plan["copy_occurrences"]].astype(np.int32),
+            np.asarray(plan["copy_position_pairs"]).reshape(-1, 2).astype(np.int32))
+
+
+def terminal_slots(slots, terminal_rows):
+    """srt/context_system/occurrence.py:757-768: slots[terminal_rows], -1 at holes."""
+    rows = np.asarray(terminal_rows)
+    out = np.full(len(rows), -1, np.asarray(slots).dtype)
+    present = rows >= 0
+    out[present] = np.asarray(slots)[rows[present]]
+    return out
