@@ -52,74 +52,99 @@ class SlotGather:
     def __init__(self, device):
         self.device = torch.device(device)
         self._tasks = []
+        self._rows = []
+        self._segments = {}
 
     def add(self, out: torch.Tensor, indices, segments=(), *, literal: bool = False):
         """out[i] = concat(segments)[indices[i]] (-1 where the index is
         negative), or indices[i] itself with ``literal``; out is int32 or
         int64 (int64 values are cast to int32 as torch does)."""
-        idx = np.ascontiguousarray(np.asarray(indices, dtype=np.int64).reshape(-1))
+        idx = np.asarray(indices, dtype=np.int64).reshape(-1)
         if out.dtype not in (torch.int32, torch.int64) or out.device != self.device or \
                 not out.is_contiguous() or out.numel() != len(idx):
             raise ValueError("gather output must be a contiguous int32/int64 vector on the "
                              "device with one element per index")
         segments = tuple(segments)
-        if len(segments) > _MAX_SEGMENTS or (not literal and not segments and len(idx)):
-            raise ValueError("a slot gather reads one to four segments")
-        for s in segments:
-            if s.ndim != 1 or s.dtype != segments[0].dtype or s.dtype not in (
-                    torch.int32, torch.int64) or s.device != self.device or \
-                    not s.is_contiguous():
-                raise ValueError("gather segments must be contiguous int32/int64 vectors of "
-                                 "one dtype on the device")
+        key = tuple(id(s) for s in segments)
+        info = self._segments.get(key)
+        if info is None:
+            if len(segments) > _MAX_SEGMENTS or (not literal and not segments and len(idx)):
+                raise ValueError("a slot gather reads one to four segments")
+            for s in segments:
+                if s.ndim != 1 or s.dtype != segments[0].dtype or s.dtype not in (
+                        torch.int32, torch.int64) or s.device != self.device or \
+                        not s.is_contiguous():
+                    raise ValueError("gather segments must be contiguous int32/int64 vectors "
+                                     "of one dtype on the device")
+            ptrs, ends, end = [0] * _MAX_SEGMENTS, [0] * _MAX_SEGMENTS, 0
+            for i, seg in enumerate(segments):
+                size = seg.numel()
+                end += size
+                ptrs[i] = seg.data_ptr() if size else 0
+                ends[i] = end
+            flags = len(segments) << 8
+            if segments and segments[0].dtype == torch.int64:
+                flags |= _native.GATHER_SEG64
+            info = (flags, ptrs + ends)
+            # the task list holds the segments, so their ids stay unique
+            self._segments[key] = info
         if len(idx) > 2**31 - 1:
             raise ValueError("a slot gather task holds at most 2^31 - 1 outputs")
+        flags = info[0] | (_native.GATHER_OUT64 if out.dtype == torch.int64 else 0) | \
+            (_native.GATHER_LITERAL if literal else 0)
+        self._rows.append([0, len(idx), out.data_ptr() if len(idx) else 0, flags, *info[1]])
         self._tasks.append((out, idx, segments, literal))
 
     def __len__(self):
         return len(self._tasks)
 
-    def pack(self, address=lambda t: t.data_ptr()):
-        """(words, n_tasks, n_chunks): the int64 task table, the chunk table
-        (int32 pairs {task, first output}) and the indices, in that order."""
+    def _sizes(self):
         chunk = int(_native.lib.akv_gather_slots_chunk())
-        n = len(self._tasks)
-        table = np.zeros((n, _TASK_WORDS), np.int64)
-        first = 0
-        chunks = []
-        for t, (out, idx, segments, literal) in enumerate(self._tasks):
-            flags = (_native.GATHER_OUT64 if out.dtype == torch.int64 else 0)
-            flags |= _native.GATHER_LITERAL if literal else 0
-            if segments and segments[0].dtype == torch.int64:
-                flags |= _native.GATHER_SEG64
-            flags |= len(segments) << 8
-            table[t, 0], table[t, 1] = first, len(idx)
-            table[t, 2] = address(out) if len(idx) else 0
-            table[t, 3] = flags
-            end = 0
-            for s, seg in enumerate(segments):
-                end += seg.numel()
-                table[t, 4 + s] = address(seg) if seg.numel() else 0
-                table[t, 8 + s] = end
-            for c in range(0, len(idx), chunk):
-                chunks.append((t, c))
-            first += len(idx)
-        if len(chunks) > 2**31 - 1:
+        lengths = np.fromiter((len(t[1]) for t in self._tasks), np.int64, len(self._tasks))
+        counts = (lengths + chunk - 1) // chunk
+        return chunk, lengths, counts
+
+    def words(self):
+        """Length of the packed program in int64 words."""
+        _, lengths, counts = self._sizes()
+        return _TASK_WORDS * len(self._tasks) + int(counts.sum()) + int(lengths.sum())
+
+    def pack(self, out: np.ndarray | None = None):
+        """(words, n_tasks, n_chunks): the int64 task table, the chunk table
+        (one word per chunk: the int32 pair {task, first output}) and the
+        indices, in that order; written into ``out`` when given."""
+        chunk, lengths, counts = self._sizes()
+        n, n_chunks = len(self._tasks), int(counts.sum())
+        if n_chunks > 2**31 - 1:
             raise ValueError("too many slot gather chunks for one launch")
-        # one int64 word per chunk: the int32 pair {task, first output}
-        pairs = np.asarray(chunks, np.int32).reshape(-1, 2)
-        words = np.concatenate([table.reshape(-1), pairs.reshape(-1).view(np.int64)] +
-                               [idx for _, idx, _, _ in self._tasks])
-        return words, n, len(chunks)
+        total = _TASK_WORDS * n + n_chunks + int(lengths.sum())
+        words = np.empty(total, np.int64) if out is None else out[:total]
+        if n:
+            table = words[:_TASK_WORDS * n].reshape(n, _TASK_WORDS)
+            table[:] = np.asarray(self._rows, np.int64)
+            table[:, 0] = np.cumsum(lengths) - lengths
+        task = np.repeat(np.arange(n, dtype=np.int32), counts)
+        start = np.repeat(np.cumsum(counts) - counts, counts)
+        pairs = words[_TASK_WORDS * n:_TASK_WORDS * n + n_chunks].view(np.int32).reshape(-1, 2)
+        pairs[:, 0] = task
+        pairs[:, 1] = (np.arange(n_chunks) - start) * chunk
+        at = _TASK_WORDS * n + n_chunks
+        for _, idx, _, _ in self._tasks:
+            words[at:at + len(idx)] = idx
+            at += len(idx)
+        return words, n, n_chunks
 
     def launch(self, error_flag: torch.Tensor | None = None):
         """Copy the packed program to the device and launch; no host sync."""
         if not self._tasks:
             return
-        words, n_tasks, n_chunks = self.pack()
+        # torch's caching host allocator keeps the pinned block until the
+        # copy that reads it has run
+        host = torch.empty(self.words(), dtype=torch.int64, pin_memory=True)
+        _, n_tasks, n_chunks = self.pack(out=host.numpy())
+        self._tasks, self._rows, self._segments = [], [], {}
         if n_chunks == 0:
             return
-        host = torch.empty(len(words), dtype=torch.int64, pin_memory=True)
-        host.numpy()[:] = words
         dev = host.to(self.device, non_blocking=True)
         base = dev.data_ptr()
         status = _native.lib.akv_gather_slots(
@@ -127,7 +152,6 @@ class SlotGather:
             base + 8 * (_TASK_WORDS * n_tasks + n_chunks), _native.ptr(error_flag),
             _native.stream_of(self.device))
         _native.check(status, "gather_slots")
-        self._tasks = []
 
 
 @dataclass(frozen=True)
