@@ -70,6 +70,7 @@ WORKLOADS = {
     "c4": (36, 8, 64, None),  # decode attention only (see bench_attention)
     "c3m": (0, 0, 0, None),   # event compiler only (see bench_compiler)
     "c4p": (36, 8, 64, None),  # prefill attention only (see bench_prefill)
+    "c4o": (0, 0, 0, None),   # occurrence binding of a c4p forward only (bench_occurrence)
 }
 
 
@@ -1112,6 +1113,19 @@ def main():
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         res = bench_compiler(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return 0
+    if args.workload == "c4o" and args.impl == "ours":
+        # Occurrence binding of one forward alone.
+        world, rank, local = dist_setup()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = bench_occurrence(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
