@@ -49,40 +49,53 @@ __global__ void __launch_bounds__(kSlotThreads) gather_slots_kernel(
     seg_end[s] = s < n_seg ? __ldg(t + 8 + s) : -1;
   }
   void* out = reinterpret_cast<void*>(__ldg(t + 2));
+  // Every index of the thread is loaded, then every slot, then every store
+  // is made: two dependent memory round trips per thread, not eight.
+  constexpr int kPer = kSlotChunk / kSlotThreads;
+  int64_t v[kPer];
+  bool live[kPer];
 #pragma unroll
-  for (int j = 0; j < kSlotChunk / kSlotThreads; ++j) {
+  for (int j = 0; j < kPer; ++j) {
     const int64_t k = (int64_t)c.y + j * kSlotThreads + threadIdx.x;
-    if (k >= n) break;
-    int64_t v = __ldg(indices + first + k);
-    if (!literal) {
-      if (v < 0) {
-        v = -1;
-      } else {
-        int64_t base = 0, local = -1;
-        int s_hit = -1;
+    live[j] = k < n;
+    v[j] = live[j] ? __ldg(indices + first + k) : -1;
+  }
+  if (!literal) {
 #pragma unroll
-        for (int s = 0; s < kMaxSegments; ++s) {
-          if (s_hit < 0 && v < seg_end[s]) {
-            s_hit = s;
-            local = v - base;
-          }
-          if (s < n_seg) base = seg_end[s];
-        }
-        if (s_hit < 0) {
-          if (error_flag != nullptr) *error_flag = 1;
-          v = -1;
-        } else {
-          const void* p = seg[0];
-#pragma unroll
-          for (int s = 1; s < kMaxSegments; ++s)
-            if (s_hit == s) p = seg[s];
-          v = seg64 ? __ldg(static_cast<const int64_t*>(p) + local)
-                    : (int64_t)__ldg(static_cast<const int32_t*>(p) + local);
-        }
+    for (int j = 0; j < kPer; ++j) {
+      if (!live[j] || v[j] < 0) {
+        v[j] = -1;
+        continue;
       }
+      int64_t base = 0, local = -1;
+      int s_hit = -1;
+#pragma unroll
+      for (int s = 0; s < kMaxSegments; ++s) {
+        if (s_hit < 0 && v[j] < seg_end[s]) {
+          s_hit = s;
+          local = v[j] - base;
+        }
+        if (s < n_seg) base = seg_end[s];
+      }
+      if (s_hit < 0) {
+        if (error_flag != nullptr) *error_flag = 1;
+        v[j] = -1;
+        continue;
+      }
+      const void* p = seg[0];
+#pragma unroll
+      for (int s = 1; s < kMaxSegments; ++s)
+        if (s_hit == s) p = seg[s];
+      v[j] = seg64 ? __ldg(static_cast<const int64_t*>(p) + local)
+                   : (int64_t)__ldg(static_cast<const int32_t*>(p) + local);
     }
-    if (out64) static_cast<int64_t*>(out)[k] = v;
-    else static_cast<int32_t*>(out)[k] = (int32_t)v;
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (!live[j]) continue;
+    const int64_t k = (int64_t)c.y + j * kSlotThreads + threadIdx.x;
+    if (out64) static_cast<int64_t*>(out)[k] = v[j];
+    else static_cast<int32_t*>(out)[k] = (int32_t)v[j];
   }
 }
 
