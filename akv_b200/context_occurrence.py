@@ -51,6 +51,10 @@ class SlotGather:
 
     def __init__(self, device):
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        # what Tensor.get_device() returns for a tensor on this device
+        self._index = self.device.index if self.device.type == "cuda" else -1
         self._tasks = []
         self._rows = []
         self._segments = {}
@@ -60,19 +64,20 @@ class SlotGather:
         negative), or indices[i] itself with ``literal``; out is int32 or
         int64 (int64 values are cast to int32 as torch does)."""
         idx = np.asarray(indices, dtype=np.int64).reshape(-1)
-        if out.dtype not in (torch.int32, torch.int64) or out.device != self.device or \
-                not out.is_contiguous() or out.numel() != len(idx):
+        m = len(idx)
+        if out.dtype not in (torch.int32, torch.int64) or out.get_device() != self._index or \
+                not out.is_contiguous() or out.numel() != m:
             raise ValueError("gather output must be a contiguous int32/int64 vector on the "
                              "device with one element per index")
         segments = tuple(segments)
         key = tuple(id(s) for s in segments)
         info = self._segments.get(key)
         if info is None:
-            if len(segments) > _MAX_SEGMENTS or (not literal and not segments and len(idx)):
+            if len(segments) > _MAX_SEGMENTS or (not literal and not segments and m):
                 raise ValueError("a slot gather reads one to four segments")
             for s in segments:
                 if s.ndim != 1 or s.dtype != segments[0].dtype or s.dtype not in (
-                        torch.int32, torch.int64) or s.device != self.device or \
+                        torch.int32, torch.int64) or s.get_device() != self._index or \
                         not s.is_contiguous():
                     raise ValueError("gather segments must be contiguous int32/int64 vectors "
                                      "of one dtype on the device")
@@ -88,11 +93,11 @@ class SlotGather:
             info = (flags, ptrs + ends)
             # the task list holds the segments, so their ids stay unique
             self._segments[key] = info
-        if len(idx) > 2**31 - 1:
+        if m > 2**31 - 1:
             raise ValueError("a slot gather task holds at most 2^31 - 1 outputs")
         flags = info[0] | (_native.GATHER_OUT64 if out.dtype == torch.int64 else 0) | \
             (_native.GATHER_LITERAL if literal else 0)
-        self._rows.append([0, len(idx), out.data_ptr() if len(idx) else 0, flags, *info[1]])
+        self._rows.append([0, m, out.data_ptr() if m else 0, flags, *info[1]])
         self._tasks.append((out, idx, segments, literal))
 
     def __len__(self):
