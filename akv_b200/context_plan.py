@@ -316,13 +316,14 @@ class LayoutCompiler:
             offs.append(o)
             host[o: o + len(part)] = part
             o += len(part) + (len(part) & 1)  # even word offsets
-        ids = np.concatenate([np.asarray(p.token_ids) for p in programs] + [np.zeros(0, np.int64)])
-        ids_host = self._ids_host.numpy()
-        ids_host[: len(ids)] = ids  # int64 -> the staging dtype
+        n_ids = int(tokens[-1])
+        if n_ids:  # one pass straight into the pinned staging buffer
+            np.concatenate([np.asarray(p.token_ids) for p in programs],
+                           out=self._ids_host.numpy()[:n_ids], casting="unsafe")
         stream = torch.cuda.current_stream(self.device)
         self._meta_dev[:o].copy_(self._meta_host[:o], non_blocking=True)
-        if len(ids):
-            self.token_ids[: len(ids)].copy_(self._ids_host[: len(ids)], non_blocking=True)
+        if n_ids:
+            self.token_ids[:n_ids].copy_(self._ids_host[:n_ids], non_blocking=True)
         self._copied.record(stream)
         md = self._meta_dev
         addr = lambda i: md.data_ptr() + 4 * offs[i]  # noqa: E731
@@ -359,7 +360,7 @@ class LayoutCompiler:
             raise ValueError("batch exceeds the compiler's workspace")
         plan = dict(n=n, tokens=tokens.tolist(), events=events.tolist(), ranges=ranges.tolist(),
                     reps=reps.tolist(), programs=programs,
-                    h2d_bytes=4 * o + ids_host.itemsize * len(ids))
+                    h2d_bytes=4 * o + self._ids_host.element_size() * n_ids)
         return b, plan
 
 
