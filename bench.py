@@ -432,10 +432,14 @@ def run_ours(args):
     # stage (one pinned H2D copy), launch, and read the decode view back.
     # Like a serving loop, the host issues step i+1 before it waits for the
     # read-back of step i (two pinned result buffers), so host work overlaps
-    # the GPU; every step still pays its own H2D and D2H.
+    # the GPU; every step still pays its own H2D and D2H.  The decode view
+    # is final once the drop kernels end, so its read-back runs on a second
+    # stream beside the reposition launch; the next step's drop waits for it.
     n_out = 2 * kept + prog.requests + 5
     a_host = [torch.empty(n_out, dtype=torch.int32, pin_memory=True) for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
+    viewed = torch.cuda.Event()
+    readback = torch.cuda.Stream(dev)
     d2h = 4 * n_out
     h2d = prepared["h2d_bytes"]
 
@@ -451,20 +455,26 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
+        if i > 0:
+            stream.wait_event(done[(i - 1) % 2])  # the last read-back has left
         res = comp.run(prog.token_counts, prog.range_offsets, prog.ranges, req_to_token,
                        row_ids, ring)
+        viewed.record(stream)
         reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
                              res.transition_destination, res.transition_pairs, cache,
                              count_device=res.transition_count)
         buf = a_host[i % 2]
-        buf[:kept].copy_(res.raw_indices[:kept], non_blocking=True)
-        buf[kept: 2 * kept].copy_(res.active_positions[:kept], non_blocking=True)
-        buf[2 * kept: 2 * kept + prog.requests].copy_(res.next_position, non_blocking=True)
-        buf[2 * kept + prog.requests:].copy_(comp.counters, non_blocking=True)
-        done[i % 2].record(stream)
+        readback.wait_event(viewed)
+        with torch.cuda.stream(readback):
+            buf[:kept].copy_(res.raw_indices[:kept], non_blocking=True)
+            buf[kept: 2 * kept].copy_(res.active_positions[:kept], non_blocking=True)
+            buf[2 * kept: 2 * kept + prog.requests].copy_(res.next_position, non_blocking=True)
+            buf[2 * kept + prog.requests:].copy_(comp.counters, non_blocking=True)
+            done[i % 2].record(readback)
         if i > 0:
             done[(i - 1) % 2].synchronize()
             check(a_host[(i - 1) % 2])
+    stream.wait_event(done[(args.steps - 1) % 2])
     e1.record(stream)
     done[(args.steps - 1) % 2].synchronize()
     e1.synchronize()

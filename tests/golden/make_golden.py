@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory by running the REFERENCE.
 
-Run in a container that has the reference tree (default /root/reference,
-override with AKV_REFERENCE_ROOT):
+Run in a container that has the reference tree (its root in
+AKV_REFERENCE_ROOT, else the default of oracle/build_oracle.py):
 
     python tests/golden/make_golden.py
 

@@ -4,8 +4,8 @@
 CPU, with its own ``request_row`` (srt/context_system/request_storage.py)
 and ``ContextDecodeLayout.from_layout`` (srt/context_system/occurrence.py).
 
-Run in a container that has the reference tree (default /root/reference,
-override with AKV_REFERENCE_ROOT):
+Run in a container that has the reference tree (its root in
+AKV_REFERENCE_ROOT, else the default of oracle/build_oracle.py):
 
     python tests/golden/make_transfer_golden.py
 
