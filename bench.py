@@ -494,12 +494,16 @@ def run_ours(args):
     # Second metric: paged GQA decode attention over the compacted cache (c4).
     del k_pools, v_pools
     torch.cuda.empty_cache()
-    attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
-                                max(5, min(args.steps // 20, 20)))
-    compiler = bench_compiler(dev, world, rank, 3, 20)
-    prefill = bench_prefill(dev, world, rank, 3, 5)
-    gather = bench_active_slots(dev, world, rank, 3, 20)
-    occurrence = bench_occurrence(dev, world, rank, 3, 20)
+    # The other sections have workloads of their own; they run beside the
+    # default (c2) line only.
+    attention = compiler = prefill = gather = occurrence = None
+    if args.workload == "c2":
+        attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
+                                    max(5, min(args.steps // 20, 20)))
+        compiler = bench_compiler(dev, world, rank, 3, 20)
+        prefill = bench_prefill(dev, world, rank, 3, 5)
+        gather = bench_active_slots(dev, world, rank, 3, 20)
+        occurrence = bench_occurrence(dev, world, rank, 3, 20)
 
     cpu = None
     if rank == 0 and world == 1:
