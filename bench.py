@@ -2,7 +2,7 @@
 """Benchmark of the AKV cache-operation hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c1|c5|c4|c3m|c4p] [--layers L]
+                    [--workload c2|c1|c5|c4|c3m|c4p|c4o|c4m|c3g] [--layers L]
 
 Metric: reposition+drop retained-KV GB/s (algorithmic bytes / time).  At
 N = 1 the workload is c2, the GPT-OSS-120B-shaped cache: one 65536-token
@@ -71,6 +71,8 @@ WORKLOADS = {
     "c3m": (0, 0, 0, None),   # event compiler only (see bench_compiler)
     "c4p": (36, 8, 64, None),  # prefill attention only (see bench_prefill)
     "c4o": (0, 0, 0, None),   # occurrence binding of a c4p forward only (bench_occurrence)
+    "c4m": (0, 0, 0, None),   # decode metadata of the c4 batch only (bench_decode_metadata)
+    "c3g": (0, 0, 0, None),   # active-slot gather of the c3 batch only (bench_active_slots)
 }
 
 
@@ -496,7 +498,7 @@ def run_ours(args):
     torch.cuda.empty_cache()
     # The other sections have workloads of their own; they run beside the
     # default (c2) line only.
-    attention = compiler = prefill = gather = occurrence = None
+    attention = compiler = prefill = gather = occurrence = metadata = None
     if args.workload == "c2":
         attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                     max(5, min(args.steps // 20, 20)))
@@ -504,6 +506,7 @@ def run_ours(args):
         prefill = bench_prefill(dev, world, rank, 3, 5)
         gather = bench_active_slots(dev, world, rank, 3, 20)
         occurrence = bench_occurrence(dev, world, rank, 3, 20)
+        metadata = bench_decode_metadata(dev, world, rank, 3, 20)
 
     cpu = None
     if rank == 0 and world == 1:
@@ -552,6 +555,7 @@ def run_ours(args):
             "prefill_attention": prefill,
             "active_slots": gather,
             "occurrence_binding": occurrence,
+            "decode_metadata": metadata,
             "clocks": clock_info,
         }
         print(json.dumps(line), flush=True)
@@ -1011,6 +1015,83 @@ def bench_occurrence(dev, world, rank, warmup, steps, seed=0, requests=16, prefi
     }
 
 
+def bench_decode_metadata(dev, world, rank, warmup, steps, seed=0, generated=4):
+    """Per-step decode metadata of the c4 batch (ContextDecodeRegistry.fill /
+    fill_window, srt/layers/attention/context_backend.py:754-809): 128
+    requests with lognormal prompt lengths (median 8K, max 64K), about 70 %
+    of each prompt kept (a sorted random decode view at compact positions),
+    ``generated`` generated tokens each; every step builds the full-attention
+    metadata and the sliding-window (128) metadata, two launches each
+    (``build_decode_metadata``).  Bytes per key: 4 B decode-view raw index
+    + 4 B req_to_token slot read + 4 B kv_indices written (generated keys
+    have no raw-index read).  Registry rows, decode views and the table
+    are synthetic with those shapes."""
+    from akv_b200 import workloads
+    from akv_b200.context_page_table import build_decode_metadata
+
+    rng = np.random.default_rng(seed)
+    lengths = workloads.c4_lengths(seed=seed)
+    batch = len(lengths)
+    max_ctx = int(lengths.max()) + generated
+    table = torch.from_numpy(rng.integers(1, 1 << 24, size=(batch, max_ctx)).astype(
+        np.int32)).to(dev)
+    registry = torch.zeros((batch, 6), dtype=torch.int64, device=dev)
+    keep, seq, prefix_keys = [], [], 0
+    for b, t in enumerate(lengths.tolist()):
+        raw = np.flatnonzero(rng.random(t) < 0.7).astype(np.int32)
+        if len(raw) == 0:
+            raw = np.zeros(1, np.int32)
+        packed = torch.from_numpy(np.concatenate((raw, np.arange(len(raw), dtype=np.int32))))
+        packed = packed.to(dev)
+        keep.append(packed)
+        registry[b] = torch.tensor([packed.data_ptr(), packed.data_ptr() + 4 * len(raw), t,
+                                    len(raw), len(raw), 0], dtype=torch.int64)
+        seq.append(len(raw) + generated)
+        prefix_keys += len(raw)
+    rows = torch.arange(batch, dtype=torch.int64, device=dev)
+    seq_lens = torch.tensor(seq, dtype=torch.int64, device=dev)
+    n_full = int(sum(seq))
+    kv_indptr = torch.empty(batch + 1, dtype=torch.int32, device=dev)
+    kv_indices = torch.empty(n_full, dtype=torch.int32, device=dev)
+    w_indptr = torch.empty(batch + 1, dtype=torch.int32, device=dev)
+    w_indices = torch.empty(batch * 128, dtype=torch.int32, device=dev)
+    w_len = torch.empty(batch, dtype=torch.int64, device=dev)
+    w_start = torch.empty(batch, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        build_decode_metadata(registry, table, rows, seq_lens, kv_indptr, kv_indices)
+        build_decode_metadata(registry, table, rows, seq_lens, w_indptr, w_indices, window=128,
+                              lengths_out=w_len, starts_out=w_start)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    assert int(kv_indptr[-1].item()) == n_full
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = dist_max(t0.elapsed_time(t1) / steps, world)
+    n_window = int(w_len.sum().item())
+    alg = 12 * prefix_keys + 8 * (n_full - prefix_keys) + 12 * n_window
+    peak, peak_kind = measured_peak()
+    gbs = alg / (ms / 1e3) / 1e9
+    return {
+        "metric": "decode metadata keys/s", "value": round((n_full + n_window) / (ms / 1e3), 1),
+        "unit": "keys/s", "ms_per_step": round(ms, 4), "n_gpus": world, "scaling": "replicas",
+        "config": {"workload": "c4 decode metadata", "requests": batch, "full_keys": n_full,
+                   "window_keys": n_window, "launches_per_step": 4},
+        "roofline": {"bound": "hbm", "kernel": "decode_indices_kernel + decode_lengths_scan",
+                     "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_source": peak_kind,
+                     "algorithmic_bytes_per_step": alg},
+        "gpu_launches_per_step": 4,
+    }
+
+
 def bench_compiler(dev, world, rank, warmup, steps, seed=0):
     """c3m: the general event compiler over 64 multi-turn agent programs
     (c3 request lengths, 8 turns each: a Drop event then a Reposition at the
@@ -1127,6 +1208,19 @@ def main():
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         res = bench_compiler(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return 0
+    if args.workload in ("c4m", "c3g") and args.impl == "ours":
+        world, rank, local = dist_setup()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        fn = bench_decode_metadata if args.workload == "c4m" else bench_active_slots
+        res = fn(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
