@@ -81,6 +81,83 @@ __global__ void __launch_bounds__(kThreads) decode_indices_kernel(const IndexArg
   }
 }
 
+// The fused metadata path (akv_build_decode_metadata) spreads the batch's
+// keys evenly over the grid instead of splitting each request a fixed number
+// of ways: a block takes 1,024 consecutive keys of kv_indices at a time and
+// finds each key's request by a binary search over kv_indptr in shared
+// memory, so a 64K-key request does not leave a few blocks running long
+// after the rest.  Each thread loads its four raw indices, then its four
+// slots, then stores.  Used where kv_indptr is the scan of the lengths
+// (the fused path computes both), so the keys tile [0, kv_indptr[batch]).
+constexpr int kFlatChunk = 1024;
+constexpr int kFlatPer = kFlatChunk / kThreads;
+constexpr int kFlatMaxBatch = 1024;
+
+struct FlatRequest {
+  const int32_t* raw_ids;  // null: ordinary request
+  const int32_t* row;
+  int64_t start;
+  int32_t active;
+  int32_t prompt;
+};
+
+__global__ void __launch_bounds__(kThreads) decode_indices_flat_kernel(const IndexArgs a,
+                                                                       int batch) {
+  extern __shared__ __align__(16) unsigned char flat_smem[];
+  int64_t* s_off = reinterpret_cast<int64_t*>(flat_smem);                   // [batch + 1]
+  FlatRequest* s_req = reinterpret_cast<FlatRequest*>(s_off + batch + 1);  // [batch]
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+    const int64_t row = ld_index(a.row_ids, b, a.row_ids_is64);
+    const Entry e = load_entry(a.registry, row);
+    FlatRequest r;
+    r.raw_ids = e.raw_ids;
+    r.row = e.row != nullptr ? e.row : a.table + row * a.row_stride;
+    r.start = a.starts ? ld_index(a.starts, b, a.starts_is64) : 0;
+    r.active = e.active;
+    r.prompt = e.prompt;
+    s_req[b] = r;
+    s_off[b] = ld_index(a.indptr, b, a.indptr_is64);
+  }
+  if (threadIdx.x == 0) s_off[batch] = ld_index(a.indptr, batch, a.indptr_is64);
+  __syncthreads();
+  const int64_t total = s_off[batch];
+  for (int64_t base = (int64_t)blockIdx.x * kFlatChunk; base < total;
+       base += (int64_t)gridDim.x * kFlatChunk) {
+    int64_t raw[kFlatPer];
+    const int32_t* rowp[kFlatPer];
+#pragma unroll
+    for (int j = 0; j < kFlatPer; ++j) {
+      const int64_t k = base + j * kThreads + threadIdx.x;
+      rowp[j] = nullptr;
+      raw[j] = 0;
+      if (k >= total) continue;
+      int lo = 0, hi = batch;  // the last request whose first key is at or before k
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_off[mid] <= k) lo = mid;
+        else hi = mid;
+      }
+      const FlatRequest& r = s_req[lo];
+      const int64_t logical = r.start + (k - s_off[lo]);
+      rowp[j] = r.row;
+      raw[j] = r.raw_ids == nullptr ? logical
+               : logical < r.active ? (int64_t)__ldg(r.raw_ids + logical)
+                                    : (int64_t)r.prompt + logical - r.active;
+    }
+    int64_t slot[kFlatPer];
+#pragma unroll
+    for (int j = 0; j < kFlatPer; ++j) slot[j] = rowp[j] ? (int64_t)__ldg(rowp[j] + raw[j]) : 0;
+    if (a.mapping) {
+#pragma unroll
+      for (int j = 0; j < kFlatPer; ++j)
+        if (rowp[j]) slot[j] = ld_index(a.mapping, slot[j], a.mapping_is64) * a.multiplier;
+    }
+#pragma unroll
+    for (int j = 0; j < kFlatPer; ++j)
+      if (rowp[j]) st_index(a.output, base + j * kThreads + threadIdx.x, a.output_is64, slot[j]);
+  }
+}
+
 __device__ __forceinline__ int64_t window_length(const Entry& e, int64_t length, int64_t window) {
   if (e.raw_ids == nullptr) return length < window ? length : window;
   const int64_t generated = length - e.active;
@@ -106,22 +183,72 @@ __global__ void __launch_bounds__(kThreads) window_lengths_kernel(
 }
 
 // One block: lengths (windowed or not), their exclusive scan into kv_indptr,
-// and starts = seq_len - length.
+// and starts = seq_len - length.  Windowed lengths are found first, eight
+// lanes per request: each round the eight lanes probe eight evenly spaced
+// positions of the request's active range and keep the ninth part that
+// holds the first position at or above the window's lower edge, so a 64K
+// range takes six dependent loads instead of sixteen.  They go to
+// lengths_out, which the scan then reads.
 __global__ void __launch_bounds__(1024) decode_lengths_scan_kernel(
     const int64_t* registry, const int64_t* row_ids, const int64_t* seq_lens, int64_t window,
     int batch, int32_t* kv_indptr, int64_t* lengths_out, int64_t* starts_out) {
   __shared__ long long warp_sums[32];
   __shared__ long long carry;
   if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (window >= 0) {
+    const int sub = threadIdx.x & 7, first_lane = lane & 24;
+    const unsigned group = 0xffu << first_lane;
+    for (int b0 = 0; b0 < batch; b0 += blockDim.x >> 3) {
+      const int b = b0 + (threadIdx.x >> 3);
+      const bool has = b < batch;
+      Entry e{};
+      long long seq = 0, lower = 0, generated = 0;
+      int32_t lo = 0, hi = 0;
+      if (has) {
+        seq = seq_lens[b];
+        e = load_entry(registry, row_ids[b]);
+        if (e.raw_ids != nullptr) {
+          generated = seq - e.active;
+          // the window is the inclusive distance q_pos - k_pos
+          lower = (long long)e.next_pos + generated - 1 - window;
+          hi = e.active;
+        }
+      }
+      while (__any_sync(0xffffffffu, hi > lo)) {
+        int32_t probe = lo;
+        bool below = false;
+        if (hi > lo) {
+          probe = lo + (int32_t)(((long long)(hi - lo) * (sub + 1)) / 9);
+          below = (long long)__ldg(e.positions + probe) < lower;
+        }
+        const int c = __popc(__ballot_sync(0xffffffffu, below) & group);
+        const int32_t p_below = __shfl_sync(0xffffffffu, probe, first_lane + (c > 0 ? c - 1 : 0));
+        const int32_t p_above = __shfl_sync(0xffffffffu, probe, first_lane + (c < 8 ? c : 7));
+        if (hi > lo) {
+          if (c > 0) lo = p_below + 1;
+          if (c < 8) hi = p_above;
+        }
+      }
+      if (has && sub == 0) {
+        long long len;
+        if (e.raw_ids == nullptr) {
+          len = seq < window ? seq : window;
+        } else {
+          const long long skipped = lower - e.next_pos > 0 ? lower - e.next_pos : 0;
+          len = (long long)e.active - lo + generated - skipped;
+        }
+        lengths_out[b] = len;
+      }
+    }
+  }
+  __syncthreads();
   for (int b0 = 0; b0 < batch; b0 += blockDim.x) {
     const int b = b0 + threadIdx.x;
     long long len = 0, seq = 0;
     if (b < batch) {
       seq = seq_lens[b];
-      len = seq;
-      if (window >= 0) len = window_length(load_entry(registry, row_ids[b]), seq, window);
+      len = window >= 0 ? lengths_out[b] : seq;
     }
     long long inc = len;
 #pragma unroll
@@ -275,8 +402,15 @@ extern "C" int akv_build_decode_metadata(
   IndexArgs a{registry, req_to_token, row_stride, row_ids, 1,
               window >= 0 ? (const void*)lengths_out : (const void*)seq_lens, 1, kv_indptr, 0,
               kv_indices, 0, window >= 0 ? starts_out : nullptr, 1, mapping, 1, multiplier};
-  dim3 grid(split_count(batch), batch);
-  decode_indices_kernel<<<grid, kThreads, 0, s>>>(a);
+  if (batch <= kFlatMaxBatch) {
+    // about four resident blocks per SM, fewer for a small batch
+    const int blocks = batch * 8 < kNumSMs * 4 ? batch * 8 : kNumSMs * 4;
+    const size_t smem = sizeof(int64_t) * (batch + 1) + sizeof(FlatRequest) * batch;
+    decode_indices_flat_kernel<<<blocks, kThreads, smem, s>>>(a, batch);
+  } else {
+    dim3 grid(split_count(batch), batch);
+    decode_indices_kernel<<<grid, kThreads, 0, s>>>(a);
+  }
   return launch_status();
 }
 

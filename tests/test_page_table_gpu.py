@@ -123,13 +123,13 @@ def test_write_row_slots_match_reference():
     np.testing.assert_array_equal(torch.stack(arrays).cpu().numpy(), z["after"])
 
 
-def _c4_registry(dev, rng, batch=128, gapped=False):
+def _c4_registry(dev, rng, batch=128, gapped=False, median=8192):
     """A c4-shaped batch: lognormal prompt lengths, drops applied through the
     oracle compiler, a few generated tokens per request."""
     from oracle import oracle
     from akv_b200 import workloads
 
-    lengths = workloads.c4_lengths(batch=batch)
+    lengths = workloads.c4_lengths(batch=batch, median=median)
     max_ctx = int(lengths.max()) + 64
     table = rng.integers(1, 1 << 24, size=(batch + 1, max_ctx)).astype(np.int32)
     host = oracle.HostRegistry(batch + 1)
@@ -158,15 +158,19 @@ def _c4_registry(dev, rng, batch=128, gapped=False):
     return host, reg, table, rows, np.asarray(seq, np.int64)
 
 
-@pytest.mark.parametrize("window", [None, 128])
+@pytest.mark.parametrize("window", [None, 128, 1])
 @pytest.mark.parametrize("gapped", [False, True])
-def test_build_decode_metadata_c4_matches_oracle(window, gapped):
+@pytest.mark.parametrize("batch,median", [(128, 8192), (1, 8192), (3, 300), (1100, 200)])
+def test_build_decode_metadata_c4_matches_oracle(window, gapped, batch, median):
+    """Batches up to 1,024 requests take the key-balanced kernel, larger ones
+    the per-request split; both against the oracle."""
     from oracle import oracle
     from akv_b200.context_page_table import build_decode_metadata
 
     dev = torch.device("cuda")
-    rng = np.random.default_rng(11)
-    host, reg, table, rows, seq = _c4_registry(dev, rng, gapped=gapped)
+    rng = np.random.default_rng(11 + batch)
+    host, reg, table, rows, seq = _c4_registry(dev, rng, batch=batch, gapped=gapped,
+                                               median=median)
     if window is None:
         lengths = seq
         starts = None
