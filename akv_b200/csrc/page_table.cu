@@ -403,10 +403,16 @@ extern "C" int akv_build_decode_metadata(
               window >= 0 ? (const void*)lengths_out : (const void*)seq_lens, 1, kv_indptr, 0,
               kv_indices, 0, window >= 0 ? starts_out : nullptr, 1, mapping, 1, multiplier};
   if (batch <= kFlatMaxBatch) {
-    // about four resident blocks per SM, fewer for a small batch
-    const int blocks = batch * 8 < kNumSMs * 4 ? batch * 8 : kNumSMs * 4;
+    // About four resident blocks per SM, fewer for a small batch.  A window
+    // keeps at most window + 1 keys of a request (the positions from
+    // q_pos - window to q_pos), which bounds the chunks the grid needs.
+    long long blocks = batch * 8 < kNumSMs * 4 ? batch * 8 : kNumSMs * 4;
+    if (window >= 0 && window < (1LL << 40)) {
+      const long long chunks = ((long long)batch * (window + 1) + kFlatChunk - 1) / kFlatChunk;
+      if (chunks < blocks) blocks = chunks > 0 ? chunks : 1;
+    }
     const size_t smem = sizeof(int64_t) * (batch + 1) + sizeof(FlatRequest) * batch;
-    decode_indices_flat_kernel<<<blocks, kThreads, smem, s>>>(a, batch);
+    decode_indices_flat_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(a, batch);
   } else {
     dim3 grid(split_count(batch), batch);
     decode_indices_kernel<<<grid, kThreads, 0, s>>>(a);
