@@ -83,13 +83,13 @@ __global__ void __launch_bounds__(kThreads) decode_indices_kernel(const IndexArg
 
 // The fused metadata path (akv_build_decode_metadata) spreads the batch's
 // keys evenly over the grid instead of splitting each request a fixed number
-// of ways: a block takes 2,048 consecutive keys of kv_indices at a time and
+// of ways: a block takes 1,024 consecutive keys of kv_indices at a time and
 // finds each key's request by a binary search over kv_indptr in shared
 // memory, so a 64K-key request does not leave a few blocks running long
-// after the rest.  Each thread loads its eight raw indices, then its eight
+// after the rest.  Each thread loads its four raw indices, then its four
 // slots, then stores.  Used where kv_indptr is the scan of the lengths
 // (the fused path computes both), so the keys tile [0, kv_indptr[batch]).
-constexpr int kFlatChunk = 2048;
+constexpr int kFlatChunk = 1024;
 constexpr int kFlatPer = kFlatChunk / kThreads;
 constexpr int kFlatMaxBatch = 1024;
 
