@@ -330,15 +330,24 @@ __global__ void __launch_bounds__(kThreads) active_slots_batch_kernel(
   const int32_t* idx = reinterpret_cast<const int32_t*>(__ldg(m + 2));
   const int64_t start = __ldg(m + 3), n_prefix = __ldg(m + 4), gen0 = __ldg(m + 5);
   const int64_t o0 = __ldg(out_offsets + c.x), n = __ldg(out_offsets + c.x + 1) - o0;
+  // Every raw index of the thread, then every slot, then the stores: two
+  // dependent memory round trips per thread instead of one per output.
+  constexpr int kPer = kGatherChunk / kThreads;
+  int64_t col[kPer];
 #pragma unroll
-  for (int j = 0; j < kGatherChunk / kThreads; ++j) {
+  for (int j = 0; j < kPer; ++j) {
+    const int64_t k = (int64_t)c.y + j * kThreads + threadIdx.x;
+    col[j] = k >= n ? -1 : k < n_prefix ? (int64_t)__ldg(idx + start + k) : gen0 + (k - n_prefix);
+  }
+  int32_t v[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) v[j] = col[j] >= 0 && col[j] < row_len ? __ldg(row + col[j]) : -1;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
     const int64_t k = (int64_t)c.y + j * kThreads + threadIdx.x;
     if (k >= n) break;
-    const int64_t col = k < n_prefix ? (int64_t)__ldg(idx + start + k) : gen0 + (k - n_prefix);
-    int32_t v = -1;
-    if (col >= 0 && col < row_len) v = __ldg(row + col);
-    else if (error_flag != nullptr) *error_flag = 1;
-    out[o0 + k] = v;
+    if ((col[j] < 0 || col[j] >= row_len) && error_flag != nullptr) *error_flag = 1;
+    out[o0 + k] = v[j];
   }
 }
 
