@@ -81,22 +81,28 @@ __global__ void __launch_bounds__(kThreads) decode_indices_kernel(const IndexArg
   }
 }
 
-// The fused metadata path (akv_build_decode_metadata) spreads the batch's
-// keys evenly over the grid instead of splitting each request a fixed number
-// of ways: a block takes 1,024 consecutive keys of kv_indices at a time and
-// finds each key's request by a binary search over kv_indptr in shared
-// memory, so a 64K-key request does not leave a few blocks running long
-// after the rest.  Each thread loads its four raw indices, then its four
-// slots, then stores.  Used where kv_indptr is the scan of the lengths
-// (the fused path computes both), so the keys tile [0, kv_indptr[batch]).
+// Key-balanced decode indices: the batch's keys are spread evenly over the
+// grid instead of splitting each request a fixed number of ways.  Each block
+// scans the lengths into shared memory (key k of the batch belongs to the
+// last request whose first key is at or before k), takes 1,024 consecutive
+// keys at a time, finds each key's request by a binary search of that scan
+// and writes it at kv_indptr[request] + its index in the request, exactly
+// where the per-request kernel writes it for any lengths and indptr
+// (padded tables included).  A 64K-key request thus does not leave a few
+// blocks running long after the rest.  Each thread loads its four raw
+// indices, then its four slots, then stores.  Batches up to kFlatMaxBatch.
 constexpr int kFlatChunk = 1024;
 constexpr int kFlatPer = kFlatChunk / kThreads;
-constexpr int kFlatMaxBatch = 1024;
+// The request table of 1,000 requests and their scan fill 48,008 bytes, under
+// the 48 KiB a launch gets without opting in.
+constexpr int kFlatMaxBatch = 1000;
+constexpr int kFlatScanPer = (kFlatMaxBatch + kThreads - 1) / kThreads;  // lengths per thread
 
 struct FlatRequest {
   const int32_t* raw_ids;  // null: ordinary request
   const int32_t* row;
   int64_t start;
+  int64_t out;             // kv_indptr[b]
   int32_t active;
   int32_t prompt;
 };
@@ -104,42 +110,76 @@ struct FlatRequest {
 __global__ void __launch_bounds__(kThreads) decode_indices_flat_kernel(const IndexArgs a,
                                                                        int batch) {
   extern __shared__ __align__(16) unsigned char flat_smem[];
-  int64_t* s_off = reinterpret_cast<int64_t*>(flat_smem);                   // [batch + 1]
-  FlatRequest* s_req = reinterpret_cast<FlatRequest*>(s_off + batch + 1);  // [batch]
-  for (int b = threadIdx.x; b < batch; b += blockDim.x) {
-    const int64_t row = ld_index(a.row_ids, b, a.row_ids_is64);
-    const Entry e = load_entry(a.registry, row);
-    FlatRequest r;
-    r.raw_ids = e.raw_ids;
-    r.row = e.row != nullptr ? e.row : a.table + row * a.row_stride;
-    r.start = a.starts ? ld_index(a.starts, b, a.starts_is64) : 0;
-    r.active = e.active;
-    r.prompt = e.prompt;
-    s_req[b] = r;
-    s_off[b] = ld_index(a.indptr, b, a.indptr_is64);
+  int64_t* s_cum = reinterpret_cast<int64_t*>(flat_smem);                   // [batch + 1]
+  FlatRequest* s_req = reinterpret_cast<FlatRequest*>(s_cum + batch + 1);  // [batch]
+  __shared__ int64_t s_warp[kThreads / 32];
+  // Per-request table and the exclusive scan of the lengths (negative: 0).
+  int64_t len[kFlatScanPer];
+  int64_t mine = 0;
+#pragma unroll
+  for (int j = 0; j < kFlatScanPer; ++j) {
+    const int b = threadIdx.x * kFlatScanPer + j;
+    len[j] = 0;
+    if (b < batch) {
+      const int64_t row = ld_index(a.row_ids, b, a.row_ids_is64);
+      const Entry e = load_entry(a.registry, row);
+      FlatRequest r;
+      r.raw_ids = e.raw_ids;
+      r.row = e.row != nullptr ? e.row : a.table + row * a.row_stride;
+      r.start = a.starts ? ld_index(a.starts, b, a.starts_is64) : 0;
+      r.out = ld_index(a.indptr, b, a.indptr_is64);
+      r.active = e.active;
+      r.prompt = e.prompt;
+      s_req[b] = r;
+      const int64_t l = ld_index(a.lengths, b, a.lengths_is64);
+      len[j] = l > 0 ? l : 0;
+    }
+    mine += len[j];
   }
-  if (threadIdx.x == 0) s_off[batch] = ld_index(a.indptr, batch, a.indptr_is64);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int64_t inc = mine;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int64_t o = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += o;
+  }
+  if (lane == 31) s_warp[warp] = inc;
   __syncthreads();
-  const int64_t total = s_off[batch];
+  int64_t before = 0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w)
+    if (w < warp) before += s_warp[w];
+  int64_t run = before + inc - mine;
+#pragma unroll
+  for (int j = 0; j < kFlatScanPer; ++j) {
+    const int b = threadIdx.x * kFlatScanPer + j;
+    if (b < batch) s_cum[b] = run;
+    run += len[j];
+  }
+  if (threadIdx.x == kThreads - 1) s_cum[batch] = run;  // the last thread ends the scan
+  __syncthreads();
+  const int64_t total = s_cum[batch];
   for (int64_t base = (int64_t)blockIdx.x * kFlatChunk; base < total;
        base += (int64_t)gridDim.x * kFlatChunk) {
-    int64_t raw[kFlatPer];
+    int64_t raw[kFlatPer], dst[kFlatPer];
     const int32_t* rowp[kFlatPer];
 #pragma unroll
     for (int j = 0; j < kFlatPer; ++j) {
       const int64_t k = base + j * kThreads + threadIdx.x;
       rowp[j] = nullptr;
-      raw[j] = 0;
+      raw[j] = dst[j] = 0;
       if (k >= total) continue;
       int lo = 0, hi = batch;  // the last request whose first key is at or before k
       while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
-        if (s_off[mid] <= k) lo = mid;
+        if (s_cum[mid] <= k) lo = mid;
         else hi = mid;
       }
       const FlatRequest& r = s_req[lo];
-      const int64_t logical = r.start + (k - s_off[lo]);
+      const int64_t i = k - s_cum[lo];
+      const int64_t logical = r.start + i;
       rowp[j] = r.row;
+      dst[j] = r.out + i;
       raw[j] = r.raw_ids == nullptr ? logical
                : logical < r.active ? (int64_t)__ldg(r.raw_ids + logical)
                                     : (int64_t)r.prompt + logical - r.active;
@@ -154,7 +194,7 @@ __global__ void __launch_bounds__(kThreads) decode_indices_flat_kernel(const Ind
     }
 #pragma unroll
     for (int j = 0; j < kFlatPer; ++j)
-      if (rowp[j]) st_index(a.output, base + j * kThreads + threadIdx.x, a.output_is64, slot[j]);
+      if (rowp[j]) st_index(a.output, dst[j], a.output_is64, slot[j]);
   }
 }
 
@@ -359,6 +399,25 @@ int split_count(int batch) {
   return (int)want;
 }
 
+// Launch decode indices: the key-balanced kernel up to kFlatMaxBatch
+// requests, else the per-request split.  max_keys (< 0: unknown) bounds the
+// keys and so the chunks the key-balanced grid needs.
+void launch_decode_indices(const IndexArgs& a, int batch, long long max_keys, cudaStream_t s) {
+  if (batch <= kFlatMaxBatch) {
+    // about four resident blocks per SM, fewer for a small batch
+    long long blocks = batch * 8 < kNumSMs * 4 ? batch * 8 : kNumSMs * 4;
+    if (max_keys >= 0) {
+      const long long chunks = (max_keys + kFlatChunk - 1) / kFlatChunk;
+      if (chunks < blocks) blocks = chunks > 0 ? chunks : 1;
+    }
+    const size_t smem = sizeof(int64_t) * (batch + 1) + sizeof(FlatRequest) * batch;
+    decode_indices_flat_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(a, batch);
+  } else {
+    dim3 grid(split_count(batch), batch);
+    decode_indices_kernel<<<grid, kThreads, 0, s>>>(a);
+  }
+}
+
 }  // namespace
 }  // namespace akv
 
@@ -376,8 +435,7 @@ extern "C" int akv_context_decode_indices(
   IndexArgs a{registry, req_to_token, row_stride, row_ids, row_ids_is64, lengths, lengths_is64,
               indptr, indptr_is64, output, output_is64, starts, starts_is64, mapping,
               mapping_is64, multiplier};
-  dim3 grid(split_count(batch), batch);
-  decode_indices_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  launch_decode_indices(a, batch, -1, static_cast<cudaStream_t>(stream));
   return launch_status();
 }
 
@@ -411,21 +469,11 @@ extern "C" int akv_build_decode_metadata(
   IndexArgs a{registry, req_to_token, row_stride, row_ids, 1,
               window >= 0 ? (const void*)lengths_out : (const void*)seq_lens, 1, kv_indptr, 0,
               kv_indices, 0, window >= 0 ? starts_out : nullptr, 1, mapping, 1, multiplier};
-  if (batch <= kFlatMaxBatch) {
-    // About four resident blocks per SM, fewer for a small batch.  A window
-    // keeps at most window + 1 keys of a request (the positions from
-    // q_pos - window to q_pos), which bounds the chunks the grid needs.
-    long long blocks = batch * 8 < kNumSMs * 4 ? batch * 8 : kNumSMs * 4;
-    if (window >= 0 && window < (1LL << 40)) {
-      const long long chunks = ((long long)batch * (window + 1) + kFlatChunk - 1) / kFlatChunk;
-      if (chunks < blocks) blocks = chunks > 0 ? chunks : 1;
-    }
-    const size_t smem = sizeof(int64_t) * (batch + 1) + sizeof(FlatRequest) * batch;
-    decode_indices_flat_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(a, batch);
-  } else {
-    dim3 grid(split_count(batch), batch);
-    decode_indices_kernel<<<grid, kThreads, 0, s>>>(a);
-  }
+  // A window keeps at most window + 1 keys of a request (the positions from
+  // q_pos - window to q_pos).
+  const long long max_keys =
+      window >= 0 && window < (1LL << 40) ? (long long)batch * (window + 1) : -1;
+  launch_decode_indices(a, batch, max_keys, s);
   return launch_status();
 }
 

@@ -192,3 +192,37 @@ def test_build_decode_metadata_c4_matches_oracle(window, gapped, batch, median):
     if window is not None:
         np.testing.assert_array_equal(lens.cpu().numpy(), lengths)
         np.testing.assert_array_equal(sts.cpu().numpy(), starts)
+
+
+@pytest.mark.parametrize("window", [None, 128])
+@pytest.mark.parametrize("batch,median", [(128, 2000), (1100, 100)])
+def test_decode_indices_padded_table_matches_oracle(window, batch, median):
+    """The registry's fill_table layout (context_backend.py:785-796): one
+    table row per request, kv_indptr = arange(bs + 1) * row stride, so the
+    index space has gaps that must stay untouched.  Up to 1,000 requests
+    take the key-balanced kernel, more the per-request split."""
+    from oracle import oracle
+    from akv_b200.context_page_table import context_decode_indices
+
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(5 + batch)
+    host, reg, table, rows, seq = _c4_registry(dev, rng, batch=batch, median=median)
+    if window is None:
+        lengths, starts = seq, None
+    else:
+        lengths = oracle.window_lengths(host, rows, seq, window)
+        starts = seq - lengths
+    stride = int(seq.max()) + 5
+    indptr = np.arange(batch + 1, dtype=np.int64) * stride
+    want = oracle.decode_indices(host, table, rows, lengths, indptr, batch * stride,
+                                 starts=starts)
+    out = torch.zeros(batch * stride, dtype=torch.int32, device=dev)
+    t = lambda a, dt: torch.from_numpy(np.asarray(a)).to(dev, dt)  # noqa: E731
+    context_decode_indices[(batch,)](
+        reg.rows, torch.from_numpy(table).to(dev), t(rows, torch.int64),
+        t(lengths, torch.int64), t(indptr, torch.int32), out,
+        None if starts is None else t(starts, torch.int64), None,
+        ROW_STRIDE=table.shape[1], TRANSLATE=False, MULTIPLIER=1,
+        HAS_START=starts is not None)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), want.astype(np.int32))
