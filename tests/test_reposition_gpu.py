@@ -151,15 +151,18 @@ def test_reposition_random_matches_oracle(dtype, neox, in_place):
 
 
 @pytest.mark.parametrize(
-    "heads,dim,rot,pad,cache_dtype",
-    [(4, 128, 128, 0, torch.float32), (2, 128, 64, 0, torch.bfloat16), (3, 96, 32, 8,
-                                                                           torch.float32),
-     (1, 40, 24, 0, torch.float16), (8, 64, 64, 4, torch.float32), (5, 80, 80, 0, torch.float32)],
+    "heads,dim,rot,pad,cache_dtype,layers",
+    [(4, 128, 128, 0, torch.float32, 5), (2, 128, 64, 0, torch.bfloat16, 5),
+     (3, 96, 32, 8, torch.float32, 5), (1, 40, 24, 0, torch.float16, 5),
+     (8, 64, 64, 4, torch.float32, 5), (5, 80, 80, 0, torch.float32, 5),
+     # one rank's share of 8-way KV-head sharding: c2 (36 layers) and c5 (80 layers)
+     (1, 64, 64, 0, torch.float32, 36), (1, 128, 128, 0, torch.float32, 80),
+     (2, 128, 128, 0, torch.float32, 80)],
 )
-def test_reposition_shapes_match_oracle(heads, dim, rot, pad, cache_dtype):
+def test_reposition_shapes_match_oracle(heads, dim, rot, pad, cache_dtype, layers):
     rng = np.random.default_rng(heads * 1000 + dim)
     for in_place in (True, False):
-        _random_case(rng, dtype=torch.bfloat16, layers=5, heads=heads, dim=dim, rot=rot,
+        _random_case(rng, dtype=torch.bfloat16, layers=layers, heads=heads, dim=dim, rot=rot,
                      neox=True, n=257, slots=800, in_place=in_place, pad=pad,
                      cache_dtype=cache_dtype)
 
