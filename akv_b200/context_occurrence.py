@@ -64,11 +64,17 @@ class SlotGather:
         negative), or indices[i] itself with ``literal``; out is int32 or
         int64 (int64 values are cast to int32 as torch does)."""
         idx = np.asarray(indices, dtype=np.int64).reshape(-1)
-        m = len(idx)
         if out.dtype not in (torch.int32, torch.int64) or out.get_device() != self._index or \
-                not out.is_contiguous() or out.numel() != m:
+                not out.is_contiguous() or out.numel() != len(idx):
             raise ValueError("gather output must be a contiguous int32/int64 vector on the "
                              "device with one element per index")
+        self._add(out, idx, segments, literal)
+
+    def _add(self, out, idx, segments=(), literal=False):
+        """``add`` for an output this module allocated (contiguous, on the
+        device, one element per index): the segments are still checked."""
+        idx = np.asarray(idx, dtype=np.int64).reshape(-1)
+        m = len(idx)
         segments = tuple(segments)
         key = tuple(id(s) for s in segments)
         info = self._segments.get(key)
@@ -141,6 +147,9 @@ class SlotGather:
 
     def launch(self, error_flag: torch.Tensor | None = None):
         """Copy the packed program to the device and launch; no host sync."""
+        if self.device.type != "cuda":
+            raise ValueError("slot gathers launch on a CUDA device; this one holds "
+                             f"{self.device} tensors")
         if not self._tasks:
             return
         # torch's caching host allocator keeps the pinned block until the
@@ -274,16 +283,16 @@ class _AdvancePlan:
         succ_slots = torch.empty(len(self.retained), dtype=dt, device=dev)
         retired = torch.empty(len(self.retired), dtype=dt, device=dev)
         seg = self.segments
-        gather.add(occurrence_out, self.occurrences, seg)
-        gather.add(src_out, self.copy_src, seg)
-        gather.add(dst_out, self.copy_dst, seg)
-        gather.add(pairs_out, self.pairs, literal=True)
-        gather.add(succ_slots, self.retained, seg)
-        gather.add(retired, self.retired, seg)
+        gather._add(occurrence_out, self.occurrences, seg)
+        gather._add(src_out, self.copy_src, seg)
+        gather._add(dst_out, self.copy_dst, seg)
+        gather._add(pairs_out, self.pairs, literal=True)
+        gather._add(succ_slots, self.retained, seg)
+        gather._add(retired, self.retired, seg)
         unused = None
         if self.swa is not None:
             unused = torch.empty(len(self.unused_swa), dtype=dt, device=dev)
-            gather.add(unused, self.unused_swa, seg)
+            gather._add(unused, self.unused_swa, seg)
         owned, canon, term, positions = self.successor
         state = self.state_type(
             succ_slots, owned, canon, term, positions, self.exact_prefix_len,
@@ -317,7 +326,7 @@ def terminal_slots(state, *, error_flag: torch.Tensor | None = None):
     slots = state.slots
     out = slots.new_empty((len(rows),))
     gather = SlotGather(slots.device)
-    gather.add(out, rows, (slots,) if len(slots) else (slots.new_empty(0),))
+    gather._add(out, rows, (slots,) if len(slots) else (slots.new_empty(0),))
     gather.launch(error_flag)
     return out
 
@@ -361,10 +370,10 @@ def bind(materialization, canonical_slots, terminal_slots, allocated_slots, *,
                       device=dev)
     a, b = len(copy_rows), len(copy_rows) + len(copy_ids)
     gather = SlotGather(dev)
-    gather.add(slots, index, segments)
-    gather.add(i32[:a], copy_rows, segments)
-    gather.add(i32[a:b], index[copy_ids], segments)
-    gather.add(i32[b:], pairs, literal=True)
+    gather._add(slots, index, segments)
+    gather._add(i32[:a], copy_rows, segments)
+    gather._add(i32[a:b], index[copy_ids], segments)
+    gather._add(i32[b:], pairs, literal=True)
     gather.launch(error_flag)
     return slots, i32[:a], i32[a:b], i32[b:].view(-1, 2)
 
@@ -432,7 +441,7 @@ class OccurrenceBatch:
                 prefix, birth = p
                 k = len(prefix) + len(birth)
                 seg = tuple(x for x in (prefix, birth) if len(x)) or (birth,)
-                gather.add(slots[s:s + k], np.arange(k), seg)
+                gather._add(slots[s:s + k], np.arange(k), seg)
                 advances.append(None)
                 s += k
         self._items = []

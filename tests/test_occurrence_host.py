@@ -255,3 +255,10 @@ def test_host_checks_and_messages():
         g.add(torch.empty(2, dtype=torch.int64), [0, 1, 2], (cs,))
     with pytest.raises(ValueError, match="cannot be empty"):
         co.OccurrenceBatch("cpu").launch()
+    # host tensors never reach the kernel
+    g = co.SlotGather("cpu")
+    g.add(torch.empty(2, dtype=torch.int64), [0, 1], (cs,))
+    with pytest.raises(ValueError, match="CUDA device"):
+        g.launch()
+    with pytest.raises(ValueError, match="CUDA device"):
+        co.terminal_slots(torch_state(z, f"{key}/successor"))
