@@ -91,6 +91,8 @@ def parse_args():
     p.add_argument("--variant", type=int, default=0,
                    help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05, "
                         "3 tcgen05 warp-specialised, 4 the same with two query tiles per CTA)")
+    p.add_argument("--head-dim", type=int, default=64, choices=[64, 128],
+                   help="c4p: head_dim of the prefill shape")
     return p.parse_args()
 
 
@@ -1209,7 +1211,7 @@ def main():
         torch.cuda.set_device(dev)
         res = bench_prefill(dev, world, rank, max(3, min(args.warmup, 5)),
                             max(3, min(args.steps, 20)), layers=args.layers or 36,
-                            variant=args.variant)
+                            variant=args.variant, head_dim=args.head_dim)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
