@@ -42,7 +42,11 @@ class ContextPrefillAttention:
         self.device = device
         self.hq, self.hkv, self.d = num_q_heads, num_kv_heads, head_dim
         self.sm_scale = 1.0 / math.sqrt(head_dim) if sm_scale is None else float(sm_scale)
-        self.error_flag = torch.zeros(1, dtype=torch.int32, device=device)
+        # [0]: error bits kept across launches until check() clears them
+        # (1: a slot outside the pools was read as slot 0; 2: a tensor-core
+        # wait ran out and that launch's output is invalid); [1]: the abort
+        # word of the current launch, cleared by every launch.
+        self.error_flag = torch.zeros(2, dtype=torch.int32, device=device)
         self.n_items = 0
         self.tokens = 0
         self.window = -1
@@ -145,3 +149,20 @@ class ContextPrefillAttention:
         )
         _native.check(status, "context_attention")
         return out
+
+    ERRORS = {1: "a key slot outside the KV pools was read as slot 0",
+              2: "a tensor-core wait ran out; the output of that launch is invalid"}
+
+    def errors(self) -> int:
+        """Error bits of the launches since the last ``check`` (reads the
+        device flag: synchronises with the current stream)."""
+        return int(self.error_flag[0].item())
+
+    def check(self):
+        """Raise RuntimeError if any launch since the last check reported
+        an error, and clear the error bits."""
+        bits = self.errors()
+        if bits:
+            self.error_flag[0].zero_()
+            why = "; ".join(msg for bit, msg in self.ERRORS.items() if bits & bit)
+            raise RuntimeError(f"context attention: {why}")

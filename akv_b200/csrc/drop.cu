@@ -475,6 +475,8 @@ void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of g_drop_scratch on the current device, looked up once
 // per device (cudaGetSymbolAddress; the host-side name is only a stand-in).
+// The address is that of the primary context current at the first call; a
+// cudaDeviceReset destroys it, and the library does not look it up again.
 int static_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AKV_ERR_CUDA;

@@ -101,7 +101,7 @@ prefill_attention_kernel(const PrefillParams p) {
       pos = __ldg(p.q_positions + qo0 + (j - n_prefix));
     }
     if (slot < 0 || slot >= p.num_slots) {  // never touch memory outside the pools
-      if (p.error_flag) *p.error_flag = 1;
+      if (p.error_flag) atomicOr(p.error_flag, 1);
       slot = 0;
     }
   };
@@ -535,8 +535,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   // Warp w serves TMEM lanes 32 * (w % 4) .. (its rows) and column half w / 4.
   const int row = ((warp & 3) << 5) | lane, half = warp >> 2;
   const int n_tiles = (key_hi - key_lo + kTcKeys - 1) / kTcKeys;
-  // After a wait ran out anywhere in the grid, later CTAs do nothing.
-  if (p.error_flag != nullptr && *reinterpret_cast<volatile int*>(p.error_flag) == 2) return;
+  // After a wait ran out anywhere in this launch, later CTAs do nothing.  One
+  // thread reads the launch's abort word and the CTA leaves as a whole: the
+  // TMEM allocation below is warp-collective and the barriers count every
+  // thread.
+  __shared__ int s_skip;
+  if (tid == 0)
+    s_skip = p.error_flag != nullptr && reinterpret_cast<volatile int*>(p.error_flag)[1] != 0;
+  __syncthreads();
+  if (s_skip) return;
 
   if (warp == 0) {  // TMEM: two S buffers, P (hi, lo) and O
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -567,7 +574,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
       pos = __ldg(p.q_positions + qo0 + (j - n_prefix));
     }
     if (slot < 0 || slot >= p.num_slots) {
-      if (p.error_flag) *p.error_flag = 1;
+      if (p.error_flag) atomicOr(p.error_flag, 1);
       slot = 0;
     }
   };
@@ -789,7 +796,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
     tc_fence_after();
   }
   const bool failed = __syncthreads_or(timed_out || s_abort);  // uniform over the CTA
-  if (failed && tid == 0 && p.error_flag) *p.error_flag = 2;
+  if (failed && tid == 0 && p.error_flag) {
+    atomicOr(p.error_flag, 2);
+    reinterpret_cast<volatile int*>(p.error_flag)[1] = 1;  // later CTAs of this launch skip
+  }
   if (!failed) {
     float o[32];
     tmem_ld32(trow + kColO + 32 * half, o);  // every thread: the load is warp-wide
@@ -980,7 +990,15 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
   const int kv0 = p.kv_indptr[b], n_prefix = p.kv_indptr[b + 1] - kv0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tiles = (key_hi - key_lo + kTcKeys - 1) / kTcKeys;
-  if (p.error_flag != nullptr && *reinterpret_cast<volatile int*>(p.error_flag) == 2) return;
+  // After a wait ran out anywhere in this launch, later CTAs do nothing.  One
+  // thread reads the launch's abort word and the CTA leaves as a whole: the
+  // TMEM allocation below is warp-collective and the barriers count every
+  // thread.
+  __shared__ int s_skip;
+  if (tid == 0)
+    s_skip = p.error_flag != nullptr && reinterpret_cast<volatile int*>(p.error_flag)[1] != 0;
+  __syncthreads();
+  if (s_skip) return;
 
   if (warp == 0) {  // TMEM: per query tile two S / P buffers and O
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -1086,7 +1104,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
         pos = __ldg(p.q_positions + qo0 + (j - n_prefix));
       }
       if (slot < 0 || slot >= p.num_slots) {
-        if (p.error_flag) *p.error_flag = 1;
+        if (p.error_flag) atomicOr(p.error_flag, 1);
         slot = 0;
       }
     };
@@ -1307,7 +1325,10 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
   }
   tc_fence_before();
   __syncthreads();
-  if (tid == 0 && s_abort && p.error_flag) *p.error_flag = 2;
+  if (tid == 0 && s_abort && p.error_flag) {
+    atomicOr(p.error_flag, 2);
+    reinterpret_cast<volatile int*>(p.error_flag)[1] = 1;  // later CTAs of this launch skip
+  }
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -1398,6 +1419,11 @@ extern "C" int akv_context_attention(
   p.num_q_heads = num_q_heads;
   p.error_flag = error_flag;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Word 1 of the flag is this launch's abort word: cleared here so that a
+  // wait that ran out in an earlier launch does not stop this one.  Word 0
+  // keeps the error bits until the caller clears it.
+  if (error_flag != nullptr && cudaMemsetAsync(error_flag + 1, 0, sizeof(int32_t), s) != cudaSuccess)
+    return AKV_ERR_CUDA;
   // tcgen05 path: head_dim 64 with 16-byte aligned q / out rows.
   const bool aligned16 = (reinterpret_cast<uintptr_t>(q) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(out) & 15) == 0 && q_stride_token % 8 == 0 &&

@@ -726,8 +726,7 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0,
     t1.record(stream)
     torch.cuda.synchronize()
     for att in (full, swa):
-        if int(att.error_flag.item()) != 0:
-            raise RuntimeError(f"prefill attention error flag {int(att.error_flag.item())}")
+        att.check()
     ms = dist_max(t0.elapsed_time(t1) / steps, world)
     full_ms = statistics.median(a.elapsed_time(b) for a, b in ev_full)
     full_flops = 4.0 * d * hq * full.visible

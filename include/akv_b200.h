@@ -163,7 +163,11 @@ int akv_drop_compact(
  * 2.4 MB) is held by every GPU that loads the library until exit.  The first
  * call on a device looks the array's device address up
  * (cudaGetSymbolAddress) and caches it; make that first call before any
- * stream capture.  All calls on a device share the array, which keeps the
+ * stream capture.  The cached address belongs to the device's primary
+ * context as it was at that first call: after cudaDeviceReset (or anything
+ * else that destroys that context) it is stale, so a process that resets a
+ * device must not call this entry point on it again.  All calls on a device
+ * share the array, which keeps the
  * last call's contents (nothing in it needs to start at zero): calls whose
  * kernels may overlap on the GPU race and must be ordered by the caller.
  */
@@ -397,7 +401,13 @@ int akv_decode_attention(
  * block's queries read keys [key_lo, key_hi) of the request's key list
  * (key_hi = P_b + last query + 1; key_lo = first key the window can reach);
  * built on the host from the CPU positions (akv_b200/context_prefill.py).
- * A slot outside [0, num_slots) is read as slot 0 and sets *error_flag.
+ * error_flag: DEVICE int32[2] or NULL.  Word 0 collects error bits and is
+ * never cleared by the library: bit 1 = a slot outside [0, num_slots) was
+ * read as slot 0; bit 2 = a tcgen05 wait did not complete (the CTA freed its
+ * tensor memory and returned; the output of that launch is not valid).
+ * Word 1 is the launch's abort word: this call clears it on the stream
+ * before launching, a CTA whose wait ran out sets it, and CTAs that start
+ * after that skip their work.
  * work may hold padding items {-1, 0, 0, 0}; items 2i and 2i + 1 are two
  * consecutive blocks of one request or a block and a padding item (the plan
  * of akv_b200/context_prefill.py lays them out so), which variant 4 needs.
@@ -405,9 +415,7 @@ int akv_decode_attention(
  * 2 = the tcgen05 / TMEM kernel (head_dim 64), 3 = its warp-specialised
  * form (head_dim 64 and 128), 4 = the warp-specialised form with the two
  * items of a pair in one CTA (n_items even); 2-4 need 16-byte aligned q and
- * out rows and sm_scale > 0 (AKV_ERR_UNSUPPORTED otherwise).  A tcgen05
- * wait that does not complete sets *error_flag to 2 (the CTA frees its
- * tensor memory and returns).
+ * out rows and sm_scale > 0 (AKV_ERR_UNSUPPORTED otherwise).
  */
 int64_t akv_context_attention_query_block(void);
 int akv_context_attention(

@@ -29,7 +29,12 @@ ORACLE_SO = os.path.join(HERE, "_build", "libakv_oracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_NAME = "akv_ref_context_plan"
 REF_SO = os.path.join(REF_DIR, REF_NAME + ".so")
-REFERENCE_ROOT = os.environ.get("AKV_REFERENCE_ROOT", "/root/reference")
+# Root of a tree that holds akv/system/sglang: AKV_REFERENCE_ROOT when set,
+# else the reference package installed into baseline/_ref (pip --target of
+# the reference's akv/system project, which keeps that layout).
+REFERENCE_ROOT = os.environ.get(
+    "AKV_REFERENCE_ROOT", os.path.join(os.path.dirname(HERE), "baseline", "_ref")
+)
 REF_PLAN = os.path.join(
     REFERENCE_ROOT, "akv/system/sglang/kernels/ops/attention/context_plan.py"
 )

@@ -23,7 +23,8 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REFERENCE_ROOT = os.environ.get("AKV_REFERENCE_ROOT", "/root/reference")
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle.build_oracle import REFERENCE_ROOT  # noqa: E402
 SG = os.path.join(REFERENCE_ROOT, "akv/system/sglang")
 
 
