@@ -18,6 +18,7 @@ AKV_OK, AKV_ERR_INVALID, AKV_ERR_CUDA, AKV_ERR_UNSUPPORTED = 0, 1, 2, 3
 AKV_F16, AKV_BF16, AKV_F32 = 0, 1, 2
 GATHER_OUT64, GATHER_LITERAL, GATHER_SEG64 = 1, 2, 4
 DROP_RING_UNDERFLOW, DROP_RING_OVERFLOW, DROP_BAD_RANGE, DROP_NO_ACTIVE = 1, 2, 4, 8
+DROP_BAD_PAGE = 16
 
 DTYPE_CODE = {torch.float16: AKV_F16, torch.bfloat16: AKV_BF16, torch.float32: AKV_F32}
 
@@ -61,6 +62,10 @@ SIGNATURES = {
     "akv_drop_compact": [
         _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _I32, _P, _I64, _P, _P, _P, _P, _P, _P,
         _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+    ],
+    "akv_drop_compact_paged": [
+        _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P, _I64, _P, _P, _P, _P, _P,
+        _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
     ],
     "akv_drop_compact_static_max_requests": [],
     "akv_drop_compact_static_max_tiles": [],

@@ -109,6 +109,10 @@ class DropResult:
             msgs.append("a drop range lies outside its request")
         if st & _native.DROP_NO_ACTIVE:
             msgs.append("Reposition of a request with no active tokens")
+        if st & _native.DROP_BAD_PAGE:
+            msgs.append("a req_to_token row breaks the page layout (a token's slot offset "
+                        "differs from its offset in the page, or one page holds two pages' "
+                        "tokens)")
         raise RuntimeError("drop_compact failed: " + "; ".join(msgs))
 
 
@@ -199,19 +203,32 @@ class DropCompactor:
         return views, off
 
     def run(self, token_counts, range_offsets, ranges, req_to_token, row_ids, ring,
-            shared_prefix=None, reposition=True, validate=True) -> DropResult:
+            shared_prefix=None, reposition=True, validate=True, page_size=1) -> DropResult:
         """Validate and stage the program (one packed host-to-device copy),
         then launch: ``prepare`` followed by ``launch``."""
         prepared = self.prepare(token_counts, range_offsets, ranges, row_ids,
                                 shared_prefix=shared_prefix, reposition=reposition,
-                                validate=validate)
+                                validate=validate, page_size=page_size)
         return self.launch(prepared, req_to_token, ring)
 
     def prepare(self, token_counts, range_offsets, ranges, row_ids, shared_prefix=None,
-                reposition=True, validate=True) -> dict:
+                reposition=True, validate=True, page_size=1) -> dict:
         """Host half: validation, packing and the host-to-device copy.  The
         returned handle can be launched any number of times while the
-        staged program stays resident on the device."""
+        staged program stays resident on the device.
+
+        ``page_size`` > 1 (a power of two from 4 to 128) runs the paged form
+        (``akv_drop_compact_paged``): the ring holds page ids, a private
+        page is freed once all its tokens are dropped, and a radix-shared
+        page holding a moved token is copied whole to a fresh page.  The
+        rows must keep each token at offset ``token % page_size`` of its
+        page, and every shared prefix must be a whole number of pages."""
+        page_size = int(page_size)
+        if page_size != 1 and (page_size < 4 or page_size > 128 or page_size & (page_size - 1)):
+            raise ValueError("page_size must be 1 or a power of two from 4 to 128")
+        if page_size != 1 and shared_prefix is not None and \
+                np.any(np.asarray(shared_prefix, np.int64) % page_size):
+            raise ValueError("a radix-shared prefix must be a whole number of pages")
         token_counts = np.asarray(token_counts, np.int64)
         nreq = len(token_counts)
         range_offsets = np.asarray(range_offsets, np.int64)
@@ -247,7 +264,7 @@ class DropCompactor:
                for name, (off, count, dt) in views.items()}
         return dict(dev=dev, nreq=nreq, n_tiles=n_tiles, total=total,
                     shared=shared_prefix is not None, reposition=bool(reposition),
-                    h2d_bytes=used)
+                    page_size=page_size, h2d_bytes=used)
 
     def launch(self, prepared, req_to_token, ring) -> DropResult:
         """Device half: the three kernels of ``akv_drop_compact`` over a
@@ -263,7 +280,12 @@ class DropCompactor:
             cached = (key,) + self._launch_args(prepared, req_to_token, ring)
             prepared["_launch"] = cached
         _, args, result = cached
-        status = _native.lib.akv_drop_compact(*args, _native.stream_of(self.device))
+        page_size = prepared.get("page_size", 1)
+        if page_size == 1:
+            status = _native.lib.akv_drop_compact(*args, _native.stream_of(self.device))
+        else:
+            status = _native.lib.akv_drop_compact_paged(*args[:11], page_size, *args[11:],
+                                                        _native.stream_of(self.device))
         _native.check(status, "drop_compact")
         return result
 
@@ -350,10 +372,10 @@ def launch_static(compactor, prepared, req_to_token, ring) -> DropResult:
 
 
 def drop_compact(token_counts, range_offsets, ranges, req_to_token, row_ids, ring,
-                 shared_prefix=None, reposition=True) -> DropResult:
+                 shared_prefix=None, reposition=True, page_size=1) -> DropResult:
     """One-shot ``DropCompactor`` sized to this program."""
     token_counts = np.asarray(token_counts, np.int64)
     comp = DropCompactor(int(token_counts.sum()), len(token_counts),
                          max(1, len(np.asarray(ranges)) // 2), req_to_token.device)
     return comp.run(token_counts, range_offsets, ranges, req_to_token, row_ids, ring,
-                    shared_prefix=shared_prefix, reposition=reposition)
+                    shared_prefix=shared_prefix, reposition=reposition, page_size=page_size)

@@ -49,7 +49,7 @@ __device__ __forceinline__ int field(unsigned long long v, int f) {
 }
 
 struct Workspace {
-  int* tile_sums;   // [n_tiles][5]: four counters + bad-range flag
+  int* tile_sums;   // [n_tiles][5]: four counters + bad-input bits (1 range, 2 page layout)
   int* tile_base;   // [n_tiles][4]: exclusive scan of the counters
   int* first_drop;  // [R]: smallest drop start of the request (INT_MAX if none)
   long long* plan;  // {ring head, ring tail, status}
@@ -88,6 +88,7 @@ struct DropArgs {
   const int64_t* row_ids;
   int64_t row_stride;
   int reposition;
+  int page_shift;  // 0: page_size 1; else log2(page_size), page_size in [4, 128]
   int32_t* ring;
   int64_t ring_capacity;
   int64_t* ring_state;
@@ -136,6 +137,81 @@ __device__ TileCtx tile_context(const DropArgs& a, int tile) {
   c.P = a.shared_prefix ? a.shared_prefix[c.r] : 0;
   c.flat0 = begin + c.t0;
   return c;
+}
+
+// ---- page mode (page_size = 2^page_shift, 4 <= page_size <= 128) ----
+// Slot s of a request's token t lies in page s >> page_shift at offset
+// s & (page_size - 1), and the layout keeps offset == t mod page_size, so
+// the tokens [g * page_size, (g + 1) * page_size) of a request share one
+// page.  A thread's four tokens lie in one page; a page is page_size / 4
+// consecutive lanes of a warp (tiles and requests start on page
+// boundaries).  The radix-shared prefix P is a whole number of pages.
+//   * A private page is freed when every token it holds is dropped (its id
+//     goes to freed_slots and the free ring, in token order).
+//   * A shared page that holds a moved token is copied to one fresh page
+//     popped from the ring: every kept token of the page gets a transition
+//     to the same offset of the new page (moved tokens rotated, tokens
+//     before the first drop copied bit for bit, old == new position), and
+//     the row entries of all its tokens are rewritten, so the layout rule
+//     holds for the next call.
+//   * Private moved tokens rotate in place, as with page_size 1.
+struct PageFlags {
+  bool keep[kPerThread], mv[kPerThread];
+  bool lead;  // first lane of the page and the page holds a token of the request
+  bool cow;   // shared page with a moved token
+  bool freed; // private page whose tokens are all dropped
+};
+
+__device__ __forceinline__ unsigned page_or(unsigned v, int lanes) {
+  for (int o = 1; o < lanes; o <<= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ unsigned page_and(unsigned v, int lanes) {
+  for (int o = 1; o < lanes; o <<= 1) v &= __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Every thread of the block calls this (warp shuffles over whole warps).
+__device__ PageFlags page_flags(const DropArgs& a, const TileCtx& c, int first_drop, int base) {
+  PageFlags f;
+  const int lanes = (1 << a.page_shift) / kPerThread;
+  bool any_mv = false, all_drop = true;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = base + k;
+    const int t = c.t0 + i;
+    f.keep[k] = i < c.n && a.keep_mask[c.flat0 + i] != 0;
+    f.mv[k] = a.reposition && f.keep[k] && t > first_drop;
+    any_mv |= f.mv[k];
+    if (i < c.n) all_drop &= !f.keep[k];
+  }
+  const bool shared = c.t0 + base < c.P;  // pages never straddle P
+  f.lead = ((threadIdx.x & (lanes - 1)) == 0) && base < c.n;
+  f.cow = shared && page_or(any_mv, lanes) != 0;
+  f.freed = !shared && page_and(all_drop, lanes) != 0;
+  return f;
+}
+
+// True if this thread's tokens break the page layout rule.
+__device__ bool page_layout_bad(const DropArgs& a, const TileCtx& c, int base) {
+  const int mask = (1 << a.page_shift) - 1;
+  const int lanes = (1 << a.page_shift) / kPerThread;
+  const int32_t* row = a.req_to_token + a.row_ids[c.r] * a.row_stride;
+  int page = -1;
+  bool bad = false;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = base + k;
+    if (i >= c.n) break;
+    const int t = c.t0 + i;
+    const int slot = row[t];
+    bad |= (slot & mask) != (t & mask);
+    if (k == 0) page = slot >> a.page_shift;
+    bad |= (slot >> a.page_shift) != page;
+  }
+  const int lead_lane = (threadIdx.x & 31) & ~(lanes - 1);
+  const int lead_page = __shfl_sync(0xffffffffu, page, lead_lane);
+  return bad || (base < c.n && page != lead_page);
 }
 
 __global__ void __launch_bounds__(kThreads) drop_count_kernel(const DropArgs a) {
@@ -192,6 +268,28 @@ __global__ void __launch_bounds__(kThreads) drop_count_kernel(const DropArgs a) 
       a.keep_mask[c.flat0 + i] = keep ? 1 : 0;
     }
   }
+  if (a.page_shift != 0) {
+    // Page mode: the counters of the tile are recomputed per page (the
+    // token loop above still wrote the keep mask).
+    __shared__ int s_bad_page;
+    if (threadIdx.x == 0) s_bad_page = c.P & ((1 << a.page_shift) - 1) ? 1 : 0;
+    __syncthreads();
+    const PageFlags f = page_flags(a, c, first_drop, base);
+    const bool bad = page_layout_bad(a, c, base);
+    kept = moved = cow = freed = 0;
+#pragma unroll
+    for (int k = 0; k < kPerThread; ++k) {
+      if (base + k >= c.n) break;
+      kept += f.keep[k];
+      moved += f.keep[k] && (f.mv[k] || f.cow);
+    }
+    cow = f.lead && f.cow;
+    freed = f.lead && f.freed;
+    if (bad) atomicOr(&s_bad_page, 1);
+    __syncthreads();
+    if (threadIdx.x == 0 && s_bad_page) atomicOr(&s_bad, 2);
+    __syncthreads();
+  }
   unsigned long long tot;
   block_exclusive_scan<unsigned long long>(pack4(kept, moved, cow, freed), &tot);
   if (threadIdx.x == 0) {
@@ -219,7 +317,7 @@ __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs 
     if (t < a.n_tiles) {
       const int* ts = a.ws.tile_sums + 5 * (size_t)t;
       for (int f = 0; f < kFields; ++f) v[f] = ts[f];
-      if (ts[4]) atomicOr(&s_bad, 1);
+      if (ts[4]) atomicOr(&s_bad, ts[4]);
     }
     for (int f = 0; f < kFields; ++f) {
       int tot;
@@ -261,7 +359,8 @@ __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs 
     a.totals[2] = (int)total_cow;
     a.totals[3] = (int)total_freed;
     int st = 0;
-    if (s_bad) st |= AKV_DROP_BAD_RANGE;
+    if (s_bad & 1) st |= AKV_DROP_BAD_RANGE;
+    if (s_bad & 2) st |= AKV_DROP_BAD_PAGE;
     if (s_no_active) st |= AKV_DROP_NO_ACTIVE;
     const long long head = a.ring_state[0], tail = a.ring_state[1];
     if (total_cow > tail - head) st |= AKV_DROP_RING_UNDERFLOW;
@@ -283,6 +382,69 @@ __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs 
   }
 }
 
+// Scatter of one tile in page mode (the rules above drop_count_kernel).
+__device__ void scatter_pages(const DropArgs& a, const TileCtx& c, int tile, int first_drop,
+                              int base) {
+  const int shift = a.page_shift, mask = (1 << shift) - 1;
+  const int lanes = (1 << shift) / kPerThread;
+  const PageFlags f = page_flags(a, c, first_drop, base);
+  int kept = 0, moved = 0;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    if (base + k >= c.n) break;
+    kept += f.keep[k];
+    moved += f.keep[k] && (f.mv[k] || f.cow);
+  }
+  unsigned long long tot;
+  const unsigned long long ex = block_exclusive_scan<unsigned long long>(
+      pack4(kept, moved, f.lead && f.cow, f.lead && f.freed), &tot);
+  const int* tb = a.ws.tile_base + 4 * (size_t)tile;
+  int gk = tb[0] + field(ex, 0);
+  int gm = tb[1] + field(ex, 1);
+  const int gc = tb[2] + field(ex, 2);  // ring index of this page's copy (lead lane)
+  const int gf = tb[3] + field(ex, 3);
+  const int lead_lane = (threadIdx.x & 31) & ~(lanes - 1);
+  const int page_gc = __shfl_sync(0xffffffffu, gc, lead_lane);
+  const int req_kept_base = a.active_offsets[c.r];
+  int32_t* row = a.req_to_token + a.row_ids[c.r] * a.row_stride;
+  const long long head = a.ws.plan[0], tail = a.ws.plan[1];
+  int slots[kPerThread];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) slots[k] = base + k < c.n ? row[c.t0 + base + k] : 0;
+  const int new_page = f.cow ? a.ring[(head + page_gc) % a.ring_capacity] : 0;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = base + k;
+    if (i >= c.n) break;
+    const int t = c.t0 + i;
+    const int fresh = (new_page << shift) | (t & mask);
+    if (f.keep[k]) {
+      const int rank = gk - req_kept_base;
+      const int pos = a.reposition ? rank : t;
+      a.positions[c.flat0 + i] = pos;
+      a.raw_indices[gk] = t;
+      a.active_positions[gk] = pos;
+      ++gk;
+      if (f.mv[k] || f.cow) {
+        a.transition_source[gm] = slots[k];
+        a.transition_destination[gm] = f.cow ? fresh : slots[k];
+        a.transition_pairs[2 * (size_t)gm] = t;
+        a.transition_pairs[2 * (size_t)gm + 1] = pos;
+        a.transition_raw[gm] = t;
+        ++gm;
+      }
+    } else {
+      a.positions[c.flat0 + i] = t;
+    }
+    if (f.cow) row[t] = fresh;
+  }
+  if (f.lead && f.freed) {
+    const int page = slots[0] >> shift;
+    a.freed_slots[gf] = page;
+    a.ring[(tail + gf) % a.ring_capacity] = page;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a) {
   pdl_wait();
   pdl_launch_dependents();  // lets a following reposition launch be scheduled
@@ -291,6 +453,10 @@ __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a
   const TileCtx c = tile_context(a, tile);
   const int first_drop = a.ws.first_drop[c.r];
   const int base = threadIdx.x * kPerThread;
+  if (a.page_shift != 0) {
+    scatter_pages(a, c, tile, first_drop, base);
+    return;
+  }
   bool keep[kPerThread];
   int kept = 0, moved = 0, cow = 0, freed = 0;
 #pragma unroll
@@ -371,17 +537,26 @@ extern "C" int64_t akv_drop_compact_workspace_bytes(int32_t n_requests, int32_t 
   return (int64_t)akv::workspace_bytes(n_requests, n_tiles);
 }
 
-extern "C" int akv_drop_compact(
+namespace akv {
+namespace {
+int drop_compact(
     int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
     int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
     const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
-    int64_t row_stride, int32_t reposition, int32_t* ring, int64_t ring_capacity,
-    int64_t* ring_state, uint8_t* keep_mask, int32_t* positions, int32_t* active_offsets,
-    int32_t* raw_indices, int32_t* active_positions, int32_t* next_position,
-    int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
-    int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
-    int32_t* freed_slots, int32_t* totals, int32_t* status, void* workspace, void* stream) {
-  using namespace akv;
+    int64_t row_stride, int32_t reposition, int32_t page_size, int32_t* ring,
+    int64_t ring_capacity, int64_t* ring_state, uint8_t* keep_mask, int32_t* positions,
+    int32_t* active_offsets, int32_t* raw_indices, int32_t* active_positions,
+    int32_t* next_position, int32_t* transition_offsets, int32_t* transition_source,
+    int32_t* transition_destination, int32_t* transition_pairs, int32_t* transition_raw,
+    int32_t* freed_offsets, int32_t* freed_slots, int32_t* totals, int32_t* status,
+    void* workspace, void* stream) {
+  int page_shift = 0;
+  if (page_size != 1) {
+    // Powers of two from 4 to 128: a thread's four tokens lie in one page
+    // and a page is at most one warp; tiles (512 tokens) hold whole pages.
+    if (page_size < 4 || page_size > 128 || (page_size & (page_size - 1))) return AKV_ERR_INVALID;
+    while ((1 << page_shift) < page_size) ++page_shift;
+  }
   if (n_requests < 0 || n_tiles < 0 || ring_capacity <= 0 || !token_offsets || !tile_offsets ||
       !range_offsets || !req_to_token || !row_ids || !ring || !ring_state || !keep_mask ||
       !positions || !active_offsets || !raw_indices || !active_positions || !next_position ||
@@ -402,6 +577,7 @@ extern "C" int akv_drop_compact(
   a.row_ids = row_ids;
   a.row_stride = row_stride;
   a.reposition = reposition != 0;
+  a.page_shift = page_shift;
   a.ring = ring;
   a.ring_capacity = ring_capacity;
   a.ring_state = ring_state;
@@ -431,6 +607,47 @@ extern "C" int akv_drop_compact(
       launch_pdl(drop_scatter_kernel, n_tiles, kThreads, 0, s, a) != cudaSuccess)
     return AKV_ERR_CUDA;
   return launch_status();
+}
+}  // namespace
+}  // namespace akv
+
+extern "C" int akv_drop_compact(
+    int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
+    int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
+    const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
+    int64_t row_stride, int32_t reposition, int32_t* ring, int64_t ring_capacity,
+    int64_t* ring_state, uint8_t* keep_mask, int32_t* positions, int32_t* active_offsets,
+    int32_t* raw_indices, int32_t* active_positions, int32_t* next_position,
+    int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
+    int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
+    int32_t* freed_slots, int32_t* totals, int32_t* status, void* workspace, void* stream) {
+  return akv::drop_compact(n_requests, token_offsets, tile_offsets, n_tiles, range_offsets,
+                           ranges, shared_prefix, req_to_token, row_ids, row_stride, reposition,
+                           1, ring, ring_capacity, ring_state, keep_mask, positions,
+                           active_offsets, raw_indices, active_positions, next_position,
+                           transition_offsets, transition_source, transition_destination,
+                           transition_pairs, transition_raw, freed_offsets, freed_slots, totals,
+                           status, workspace, stream);
+}
+
+extern "C" int akv_drop_compact_paged(
+    int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
+    int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
+    const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
+    int64_t row_stride, int32_t reposition, int32_t page_size, int32_t* ring,
+    int64_t ring_capacity, int64_t* ring_state, uint8_t* keep_mask, int32_t* positions,
+    int32_t* active_offsets, int32_t* raw_indices, int32_t* active_positions,
+    int32_t* next_position, int32_t* transition_offsets, int32_t* transition_source,
+    int32_t* transition_destination, int32_t* transition_pairs, int32_t* transition_raw,
+    int32_t* freed_offsets, int32_t* freed_slots, int32_t* totals, int32_t* status,
+    void* workspace, void* stream) {
+  return akv::drop_compact(n_requests, token_offsets, tile_offsets, n_tiles, range_offsets,
+                           ranges, shared_prefix, req_to_token, row_ids, row_stride, reposition,
+                           page_size, ring, ring_capacity, ring_state, keep_mask, positions,
+                           active_offsets, raw_indices, active_positions, next_position,
+                           transition_offsets, transition_source, transition_destination,
+                           transition_pairs, transition_raw, freed_offsets, freed_slots, totals,
+                           status, workspace, stream);
 }
 
 // ---------------------------------------------------------------------------

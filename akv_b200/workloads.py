@@ -102,9 +102,12 @@ def c2_program(seed=0, tokens=65536, spans=20, frac=0.4):
     return _program([tokens], [place_spans(rng, tokens, lengths)], meta=dict(config="c2"))
 
 
-def c3_program(seed=0, requests=64, min_len=2048, max_len=32768):
+def c3_program(seed=0, requests=64, min_len=2048, max_len=32768, page_align=1):
+    """``page_align``: round the shared prefix down to a whole number of
+    pages of that size (a radix cache over a paged pool shares whole
+    pages); 1 keeps the drawn length."""
     rng = np.random.default_rng(seed)
-    prefix = int(rng.integers(1024, 4097))
+    prefix = int(rng.integers(1024, 4097)) // page_align * page_align
     counts = rng.integers(max(min_len, prefix + 2), max_len + 1, size=requests)
     per_request = []
     for length in counts:
@@ -153,6 +156,35 @@ def slot_rows(rng, program, shared_slots=None, first_slot=1):
         cursor += t - p
         rows.append(row)
     return rows, prefix + private + first_slot
+
+
+def paged_slot_rows(rng, program, page_size, first_page=1):
+    """req_to_token rows over a paged pool (slot = page * page_size +
+    offset): the shared prefix (a whole number of pages) maps every request
+    to the same pages; each request's private tokens fill their own pages,
+    token t at offset t % page_size, the pages drawn from a random
+    permutation and handed to each request in ascending order (as an
+    allocator with a sorted free list does).  Page 0 stays unused (slot 0
+    is SGLang's padding slot).  Returns (rows, number of pages including
+    the unused ones)."""
+    ps = int(page_size)
+    prefix = int(program.shared_prefix.max()) if program.requests else 0
+    if prefix % ps:
+        raise ValueError("the shared prefix must be a whole number of pages")
+    private = [-(-(int(t) - int(p)) // ps) for t, p in
+               zip(program.token_counts, program.shared_prefix)]
+    n_pages = prefix // ps + sum(private)
+    perm = rng.permutation(n_pages).astype(np.int64) + first_page
+    shared = np.sort(perm[: prefix // ps])
+    cursor = prefix // ps
+    rows = []
+    for r in range(program.requests):
+        t, p = int(program.token_counts[r]), int(program.shared_prefix[r])
+        pages = np.concatenate((shared[: p // ps], np.sort(perm[cursor: cursor + private[r]])))
+        cursor += private[r]
+        tok = np.arange(t)
+        rows.append((pages[tok // ps] * ps + tok % ps).astype(np.int32))
+    return rows, n_pages + first_page
 
 
 @dataclass

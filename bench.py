@@ -73,6 +73,7 @@ WORKLOADS = {
     "c4o": (0, 0, 0, None),   # occurrence binding of a c4p forward only (bench_occurrence)
     "c4m": (0, 0, 0, None),   # decode metadata of the c4 batch only (bench_decode_metadata)
     "c3g": (0, 0, 0, None),   # active-slot gather of the c3 batch only (bench_active_slots)
+    "c3": (36, 8, 64, "yarn"),  # batched copy-on-write Drop + Reposition only (bench_c3)
 }
 
 
@@ -93,6 +94,8 @@ def parse_args():
                         "3 tcgen05 warp-specialised, 4 the same with two query tiles per CTA)")
     p.add_argument("--head-dim", type=int, default=64, choices=[64, 128],
                    help="c4p: head_dim of the prefill shape")
+    p.add_argument("--page-size", type=int, default=1, choices=[1, 16],
+                   help="c3: page size of the KV pool")
     return p.parse_args()
 
 
@@ -236,8 +239,10 @@ def dist_setup():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # The path has no exchange: the process group only carries the
+        # barriers around timed regions and the MAX of the timings, on the
+        # host (gloo), so no NCCL communicator is created at all.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     return world, rank, local
 
 
@@ -246,7 +251,7 @@ def dist_max(x, world):
         return x
     import torch.distributed as dist
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -296,7 +301,25 @@ def cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng, th
     oracle.reposition(k, k, idx, idx, pairs, cache_np, bf16=True, threads=threads)
     t_rep = time.perf_counter() - t1
     del slots
-    return t_drop + t_rep * (n / max(1, m)), m, n
+    return t_drop, t_rep * (n / max(1, m)), m, n
+
+
+def cpu_parts(t_drop, t_rep, m, n, layers, heads, tokens):
+    """The two halves of a CPU step, each with its own kind: the event
+    compiler is the reference's own code (oracle/_ref) when it was built
+    here, the reposition is always this package's restatement (the
+    reference has no CPU reposition)."""
+    from oracle import reference
+
+    ref = reference.available()
+    return {
+        "event_compiler": {"kind": "reference" if ref else "port", "ms": round(t_drop * 1e3, 3),
+                           "what": f"{'reference C++ (oracle/_ref)' if ref else 'oracle port'} "
+                                   f"over all {tokens} tokens + numpy decode view, one thread"},
+        "reposition": {"kind": "port", "ms": round(t_rep * 1e3, 3),
+                       "what": f"C restatement of the reference kernel on {m} of {n} moved "
+                               f"tokens x {layers} layers x {heads} heads, scaled to all {n}"},
+    }
 
 
 def run_reference(args):
@@ -316,20 +339,18 @@ def run_reference(args):
     sample = 4000
     for _ in range(args.warmup):
         cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng, threads)
-    times = []
+    times, drops, reps = [], [], []
     for _ in range(args.steps):
-        s, m, n = cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng,
-                                     threads)
-        times.append(s)
+        t_drop, t_rep, m, n = cpu_reference_step(prog, rows, layers, heads, dim, cache_np,
+                                                 sample, rng, threads)
+        times.append(t_drop + t_rep)
+        drops.append(t_drop)
+        reps.append(t_rep)
     sec = sum(times)
     value = (rep_bytes + drop_bytes) * args.steps / sec / 1e9
-    from oracle import reference
-
-    kind = "reference" if reference.available() else "port"
-    desc = (f"{args.workload}: event compiler over all {prog.total_tokens} tokens "
-            f"({'reference C++ from oracle/_ref' if kind == 'reference' else 'oracle port'}) + "
+    desc = (f"{args.workload} per step: event compiler over all {prog.total_tokens} tokens + "
             f"decode view; reposition restatement on {m} of {n} moved tokens x {layers} layers "
-            f"x {heads} heads per step, time scaled to all {n}")
+            f"x {heads} heads, time scaled to all {n} (parts below)")
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * sec / args.steps, 3),
@@ -337,8 +358,10 @@ def run_reference(args):
         "data": "synthetic", "impl": "reference",
         "config": {"workload": args.workload, "layers": layers, "kv_heads": heads, "head_dim": dim,
                    "tokens": prog.total_tokens},
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": desc},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc,
+                         "parts": cpu_parts(sum(drops) / args.steps, sum(reps) / args.steps, m,
+                                            n, layers, heads, prog.total_tokens)},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -501,7 +524,9 @@ def run_ours(args):
     # The other sections have workloads of their own; they run beside the
     # default (c2) line only.
     attention = compiler = prefill = gather = occurrence = metadata = None
+    c3 = {}
     if args.workload == "c2":
+        c3 = bench_c3(dev, world, rank, 3, max(5, min(args.steps, 20)))
         attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                     max(5, min(args.steps // 20, 20)))
         compiler = bench_compiler(dev, world, rank, 3, 20)
@@ -514,17 +539,13 @@ def run_ours(args):
     if rank == 0 and world == 1:
         cache_np = cache.cpu().numpy()
         threads = len(os.sched_getaffinity(0))
-        sec, m, n = cpu_reference_step(prog, rows, layers, heads, dim, cache_np, 4000,
-                                       np.random.default_rng(0), threads)
-        from oracle import reference
-
-        kind = "reference" if reference.available() else "port"
-        cpu = {"value": round((rep_bytes + drop_bytes) / sec / 1e9, 3), "unit": UNIT,
-               "cores": threads, "kind": kind,
-               "sample": f"event compiler ({'reference C++, oracle/_ref' if kind == 'reference' else 'oracle port'}) "
-                         f"over all {total} tokens + numpy decode view; reposition restatement "
-                         f"(the reference has no CPU reposition) on {m} of {n} moved tokens x "
-                         f"{layers} layers x {heads} heads, time scaled to all {n}"}
+        t_drop, t_rep, m, n = cpu_reference_step(prog, rows, layers, heads, dim, cache_np, 4000,
+                                                 np.random.default_rng(0), threads)
+        cpu = {"value": round((rep_bytes + drop_bytes) / (t_drop + t_rep) / 1e9, 3),
+               "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"one c2 step: event compiler over all {total} tokens + reposition "
+                         f"restatement on {m} of {n} moved tokens, scaled (parts below)",
+               "parts": cpu_parts(t_drop, t_rep, m, n, layers, heads, total)}
 
     if rank == 0:
         line = {
@@ -552,14 +573,35 @@ def run_ours(args):
                              "reposition": round(rep_mean, 4)},
             "gpu_launches": 4 * args.steps,
             "cpu_baseline": cpu,
-            "decode_attention": attention,
             "event_compiler": compiler,
             "prefill_attention": prefill,
             "active_slots": gather,
             "occurrence_binding": occurrence,
             "decode_metadata": metadata,
+            "c3_page_size_1": c3.get(1),
+            "c3_page_size_16": c3.get(16),
+            "decode_attention": attention,
             "clocks": clock_info,
         }
+        # Last, so that a reader that keeps only the end of the line still
+        # sees every section's headline: value, unit, kernel fraction of the
+        # HBM (or tensor) peak, e2e and CPU-baseline values.
+        summary = {}
+        for name, sec in (("c2", line), ("c3_ps1", c3.get(1)), ("c3_ps16", c3.get(16)),
+                          ("decode_attention", attention), ("prefill_attention", prefill),
+                          ("event_compiler", compiler), ("decode_metadata", metadata),
+                          ("active_slots", gather), ("occurrence_binding", occurrence)):
+            if not sec:
+                continue
+            item = {"value": sec["value"], "unit": sec["unit"]}
+            if sec.get("roofline"):
+                item["frac"] = sec["roofline"]["frac"]
+            if isinstance(sec.get("e2e"), dict):
+                item["e2e"] = sec["e2e"]["value"]
+            if isinstance(sec.get("cpu_baseline"), dict):
+                item["cpu"] = sec["cpu_baseline"]["value"]
+            summary[name] = item
+        line["summary"] = summary
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -652,6 +694,256 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1)
                      "ms_per_launch": round(full_ms, 4)},
         "gpu_launches_per_step": layers + (layers // 2 if full.split else 0),
     }
+
+
+def c3_counts(prog, page_size):
+    """Closed form of the c3 step on the host (what the kernels produce):
+    kept, moved, copy-on-write transitions, copied units (slots at
+    page_size 1, pages otherwise) and freed units (slots or pages)."""
+    kept = moved = cow = copied = freed = 0
+    ps = int(page_size)
+    for r in range(prog.requests):
+        keep = prog.keep_mask(r)
+        t = np.arange(len(keep))
+        rr = prog.request_ranges(r)
+        first = int(rr[0]) if len(rr) else len(keep)
+        mv = keep & (t > first)
+        p = int(prog.shared_prefix[r])
+        kept += int(keep.sum())
+        if ps == 1:
+            moved += int(mv.sum())
+            cow += int(mv[:p].sum())
+            copied += int(mv[:p].sum())
+            freed += int((~keep[p:]).sum())
+            continue
+        n_pages = -(-len(keep) // ps)
+        pad = np.zeros(n_pages * ps, bool)
+        pad[: len(keep)] = mv
+        page_mv = pad.reshape(n_pages, ps).any(1)
+        kp = np.ones(n_pages * ps, bool)
+        kp[: len(keep)] = keep
+        kp[len(keep):] = False
+        shared_pages = p // ps
+        cow_pages = page_mv[:shared_pages]
+        in_cow = np.repeat(np.concatenate((cow_pages, np.zeros(n_pages - shared_pages, bool))),
+                           ps)[: len(keep)]
+        trans = keep & (mv | in_cow)
+        moved += int(trans.sum())
+        cow += int((trans & in_cow).sum())
+        copied += int(cow_pages.sum())
+        freed += int((~kp.reshape(n_pages, ps)[shared_pages:].any(1)).sum())
+    return kept, moved, cow, copied, freed
+
+
+def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers=36,
+             cpu=True, e2e_steps=5):
+    """c3: batched agent serving -- 64 requests (lengths U{2K..32K}, 1.18M
+    tokens), one radix-shared prefix of 1K..4K tokens (a whole number of
+    16-token pages) whose moved tokens must copy-on-write, per-request drop
+    fraction U[0.1, 0.6], GPT-OSS-120B KV shape (36 layers, 8 KV heads split
+    8/N per rank, head_dim 64), YaRN RoPE; at page_size 1 and 16.
+
+    One step = restore the rows and the ring head that the previous step's
+    copy-on-write changed (one 8 MB device copy of req_to_token and one of
+    the 16-byte ring state; the bytes are not counted) + the Drop (three
+    launches) + one reposition launch over all 36 layers.  Algorithmic
+    bytes: per (transition, layer, local head) 2 * rotary_dim * 2 B in place
+    and 4 * head_dim * 2 B for copy-on-write (K read + write, V read +
+    write); Drop: T + 4 T + 8 A + 4 per freed unit + 12 per transition +
+    4 per rewritten row entry.  The K pools (49 GB) exceed L2."""
+    from akv_b200 import workloads
+    from akv_b200.context_drop import DropCompactor, FreeSlotRing
+    from akv_b200.context_reposition import layer_pointer_table, reposition_kv_layers
+    from akv_b200.rope import yarn_cos_sin_cache
+
+    heads_total, dim = 8, 64
+    heads = heads_total // world
+    prog = workloads.c3_program(seed=seed, page_align=16)
+    total = prog.total_tokens
+    layouts = {}
+    pool_slots = 0
+    for ps in page_sizes:
+        kept, moved, cow, copied, freed = c3_counts(prog, ps)
+        rng = np.random.default_rng(seed)
+        if ps == 1:
+            rows, n_units = workloads.slot_rows(rng, prog)
+            slots = n_units + copied
+        else:
+            rows, n_units = workloads.paged_slot_rows(rng, prog, ps)
+            slots = (n_units + copied) * ps
+        layouts[ps] = (rows, n_units, (kept, moved, cow, copied, freed))
+        pool_slots = max(pool_slots, slots)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    k_pools = [torch.randn(pool_slots, heads, dim, device=dev, generator=g, dtype=torch.bfloat16)
+               for _ in range(layers)]
+    v_pools = [torch.empty(pool_slots, heads, dim, device=dev, dtype=torch.bfloat16)
+               for _ in range(layers)]
+    k_ptrs, v_ptrs = layer_pointer_table(k_pools), layer_pointer_table(v_pools)
+    cache = yarn_cos_sin_cache(32768, dim, 150000.0, 32.0, 4096).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = measured_peak()
+    comp = DropCompactor(total, prog.requests, max(1, len(prog.ranges) // 2), dev)
+    out = {}
+    for ps in page_sizes:
+        rows, n_units, (kept, moved, cow, copied, freed) = layouts[ps]
+        table = np.zeros((prog.requests + 1, int(prog.token_counts.max())), np.int32)
+        for r in range(prog.requests):
+            table[r + 1, : len(rows[r])] = rows[r]
+        rtt0 = torch.from_numpy(table).to(dev)
+        rtt = rtt0.clone()
+        row_ids = np.arange(1, prog.requests + 1)
+        ring = FreeSlotRing(torch.arange(n_units, n_units + copied, dtype=torch.int32),
+                            capacity=copied + freed + 16, device=dev)
+        state0 = ring.state.clone()
+        prepared = comp.prepare(prog.token_counts, prog.range_offsets, prog.ranges, row_ids,
+                                shared_prefix=prog.shared_prefix, page_size=ps)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+
+        def step(i=None):
+            rtt.copy_(rtt0)
+            ring.state.copy_(state0)
+            if i is not None:
+                ev[i][0].record(stream)
+            res = comp.launch(prepared, rtt, ring)
+            if i is not None:
+                ev[i][1].record(stream)
+            reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
+                                 res.transition_destination, res.transition_pairs, cache,
+                                 count_device=res.transition_count)
+            if i is not None:
+                ev[i][2].record(stream)
+            return res
+
+        for _ in range(warmup):
+            res = step()
+        torch.cuda.synchronize()
+        res.check()
+        assert res.totals.cpu().tolist() == [kept, moved, copied, freed], \
+            (res.totals.cpu().tolist(), [kept, moved, copied, freed])
+        n = moved
+        src = res.transition_source[:n]
+        n_cow = int((src != res.transition_destination[:n]).sum().item())
+        assert n_cow == cow
+        rep_bytes = ((n - n_cow) * 2 * dim * 2 + n_cow * 4 * dim * 2) * layers * heads
+        row_writes = copied if ps == 1 else copied * ps
+        drop_bytes = total + 4 * total + 8 * kept + 4 * freed + 12 * n + 4 * row_writes
+        dist_barrier(world)
+        torch.cuda.synchronize()
+        clocks = ClockSampler(dev.index)
+        clocks.start()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        clock_info = clocks.stop()
+        ms = dist_max(t0.elapsed_time(t1) / steps, world)
+        for i in range(steps):
+            step(i)
+        torch.cuda.synchronize()
+        drop_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+        rep_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+        # e2e through the public API from host memory: validate + pack + one
+        # H2D copy + launches, and the decode view read back every step.
+        view = torch.empty(2 * kept, dtype=torch.int32, pin_memory=True)
+        dist_barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            rtt.copy_(rtt0)
+            ring.state.copy_(state0)
+            r2 = comp.run(prog.token_counts, prog.range_offsets, prog.ranges, rtt, row_ids, ring,
+                          shared_prefix=prog.shared_prefix, page_size=ps)
+            reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], r2.transition_source,
+                                 r2.transition_destination, r2.transition_pairs, cache,
+                                 count_device=r2.transition_count)
+            view[:kept].copy_(r2.raw_indices[:kept], non_blocking=True)
+            view[kept:].copy_(r2.active_positions[:kept], non_blocking=True)
+            e1.record(stream)
+            e1.synchronize()
+        e2e_s = dist_max(e0.elapsed_time(e1) / 1e3, world)
+        step_bytes = (rep_bytes + drop_bytes) * world
+        achieved = rep_bytes / (rep_ms / 1e3) / 1e9
+        sec = {
+            "metric": METRIC, "value": round(step_bytes / (ms / 1e3) / 1e9, 2), "unit": UNIT,
+            "ms_per_step": round(ms, 4), "n_gpus": world, "scaling": "strong",
+            "config": {"workload": f"c3 page_size {ps}", "requests": prog.requests,
+                       "tokens": total, "shared_prefix": int(prog.shared_prefix.max()),
+                       "layers": layers, "kv_heads": heads_total, "kv_heads_per_gpu": heads,
+                       "head_dim": dim, "page_size": ps, "rope": "yarn",
+                       "moved_tokens": n, "cow_transitions": n_cow,
+                       "in_place_transitions": n - n_cow,
+                       ("copied_pages" if ps > 1 else "copied_slots"): copied,
+                       ("freed_pages" if ps > 1 else "freed_slots"): freed,
+                       "l2": "K pools 49 GB, larger than L2; no flush",
+                       "restore": "rows + ring head restored on the device each step"},
+            "e2e": {"value": round(step_bytes * e2e_steps / e2e_s / 1e9, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": prepared["h2d_bytes"], "d2h_bytes_per_step": 8 * kept},
+            "breakdown_ms": {"drop_compact": round(drop_ms, 4), "reposition": round(rep_ms, 4)},
+            "roofline": {"bound": "hbm", "kernel": "reposition_kernel",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": rep_bytes,
+                         "ms_per_launch": round(rep_ms, 4),
+                         "traffic": ncu_traffic(f"c3_ps{ps}") if world == 1 else None},
+            "gpu_launches_per_step": 4,
+            "clocks": clock_info,
+        }
+        if cpu and rank == 0 and world == 1:
+            sec["cpu_baseline"] = cpu_reference_c3(prog, rows, layers, heads, dim,
+                                                   cache.cpu().numpy(), rep_bytes + drop_bytes)
+        out[ps] = sec
+    del k_pools, v_pools
+    torch.cuda.empty_cache()
+    return out
+
+
+def cpu_reference_c3(prog, rows, layers, heads, dim, cache_np, step_bytes, sample=2000):
+    """The reference's CPU path for one c3 step, on the host cores: its C++
+    event compiler (oracle/_ref) over every request + the numpy decode view,
+    and the CPU restatement of its reposition kernel (the reference has no
+    CPU reposition; it copies every moved token, so the restatement moves
+    K and V of a sample of the transitions, copy-on-write ones included)
+    scaled to all transitions.  The reference has no paged Reposition, so
+    both page sizes are measured against this page_size 1 path."""
+    from oracle import oracle, reference
+
+    threads = len(os.sched_getaffinity(0))
+    comp = reference.compile_context_layout if reference.available() else oracle.compile_layout
+    t0 = time.perf_counter()
+    trans = []
+    for r in range(prog.requests):
+        t = int(prog.token_counts[r])
+        rr = prog.request_ranges(r)
+        lay = comp(np.zeros(t, np.int32), [t], [0, len(rr) // 2], rr, [t - 1], [t])
+        raw = np.flatnonzero(lay["keep_mask"]).astype(np.int32)
+        _ = lay["positions"][raw]
+        trans.append(np.stack((lay["transition_old_positions"],
+                               lay["transition_new_positions"]), 1))
+    t_drop = time.perf_counter() - t0
+    pairs = np.concatenate(trans).astype(np.int32)
+    n = len(pairs)
+    rng = np.random.default_rng(0)
+    m = min(sample, n)
+    pick = rng.choice(n, size=m, replace=False)
+    k = [np.random.default_rng(l).integers(0, 1 << 16, size=(2 * m, heads, dim),
+                                           dtype=np.uint16) & 0x7F7F for l in range(layers)]
+    v = [np.zeros((2 * m, heads, dim), np.uint16) for _ in range(layers)]
+    src = np.arange(m, dtype=np.int32)
+    t1 = time.perf_counter()
+    oracle.reposition(k, v, src, src + m, pairs[pick], cache_np, bf16=True, threads=threads)
+    t_rep = (time.perf_counter() - t1) * n / m
+    sec = t_drop + t_rep
+    kind = "reference" if reference.available() else "port"
+    return {"value": round(step_bytes / sec / 1e9, 3), "unit": UNIT, "cores": threads,
+            "kind": kind,
+            "sample": f"event compiler ({'reference C++' if kind == 'reference' else 'port'}) "
+                      f"over all {prog.requests} requests ({t_drop * 1e3:.1f} ms) + reposition "
+                      f"restatement (port) moving K and V of {m} of {n} transitions x {layers} "
+                      f"layers x {heads} heads, scaled to all {n} ({t_rep * 1e3:.1f} ms)"}
 
 
 def measured_tensor_peak():
@@ -1266,6 +1558,21 @@ def main():
                               layers=args.layers or 36, shard=args.shard)
         if rank == 0:
             print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return 0
+    if args.workload == "c3" and args.impl == "ours":
+        # The batched copy-on-write step alone (--page-size 1 or 16; --layers
+        # for a smaller cut under a profiler).
+        world, rank, local = dist_setup()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = bench_c3(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)),
+                       page_sizes=(args.page_size,), layers=args.layers or 36, cpu=False)
+        if rank == 0:
+            print(json.dumps(res[args.page_size]), flush=True)
         if world > 1:
             import torch.distributed as dist
 

@@ -33,6 +33,7 @@ extern "C" {
 #define AKV_DROP_RING_OVERFLOW 2  /* freed slots exceed the ring capacity    */
 #define AKV_DROP_BAD_RANGE 4      /* a drop range lies outside its request   */
 #define AKV_DROP_NO_ACTIVE 8      /* Reposition of a request with no token   */
+#define AKV_DROP_BAD_PAGE 16      /* page mode: a row breaks the page layout */
 
 /* Element types. */
 #define AKV_F16 0
@@ -147,6 +148,40 @@ int akv_drop_compact(
     int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
     int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
     int32_t* freed_slots, int32_t* totals, int32_t* status, void* workspace, void* stream);
+
+/*
+ * akv_drop_compact over a paged KV pool: the same computation with
+ * page_size slots per page.  page_size 1 is akv_drop_compact; otherwise a
+ * power of two from 4 to 128.  No counterpart in the reference, whose
+ * Reposition requires page_size 1 (context_reposition.py:153-154,
+ * capabilities.py:11-12); this extends it to SGLang's paged pools.
+ *
+ * Layout rule (checked on the device, AKV_DROP_BAD_PAGE if broken): slot s
+ * is offset s % page_size of page s / page_size, and a request's token t
+ * sits at offset t % page_size, so tokens [g*page_size, (g+1)*page_size)
+ * of a request share one page; shared_prefix[r] is a multiple of
+ * page_size.  The free ring and freed_slots hold PAGE ids, not slots.
+ *   - A private page whose every token is dropped is freed (pushed in the
+ *     order of its tokens; dropped tokens of other pages stay as holes).
+ *   - A shared (radix) page holding a moved token is copied to one fresh
+ *     page popped from the ring: each kept token of the page gets a
+ *     transition to the same offset of the new page (moved tokens rotate;
+ *     tokens before the first drop keep their position and are copied bit
+ *     for bit) and every row entry of the page is rewritten to the new page.
+ *   - Private moved tokens rotate in place.
+ * totals = {active, transitions, copied pages, freed pages}.
+ */
+int akv_drop_compact_paged(
+    int32_t n_requests, const int64_t* token_offsets, const int32_t* tile_offsets,
+    int32_t n_tiles, const int32_t* range_offsets, const int32_t* ranges,
+    const int32_t* shared_prefix, int32_t* req_to_token, const int64_t* row_ids,
+    int64_t row_stride, int32_t reposition, int32_t page_size, int32_t* ring,
+    int64_t ring_capacity, int64_t* ring_state, uint8_t* keep_mask, int32_t* positions,
+    int32_t* active_offsets, int32_t* raw_indices, int32_t* active_positions,
+    int32_t* next_position, int32_t* transition_offsets, int32_t* transition_source,
+    int32_t* transition_destination, int32_t* transition_pairs, int32_t* transition_raw,
+    int32_t* freed_offsets, int32_t* freed_slots, int32_t* totals, int32_t* status,
+    void* workspace, void* stream);
 
 /*
  * akv_drop_compact without a workspace argument: the same computation and

@@ -211,6 +211,73 @@ def drop_compact(token_counts, range_offsets, ranges, slot_rows, shared_prefix=N
     return res
 
 
+def drop_compact_paged(token_counts, range_offsets, ranges, slot_rows, page_size,
+                       shared_prefix=None, reposition=True, free_pages=None, free_head=0,
+                       free_tail=0):
+    """``drop_compact`` over a paged pool (slot = page * page_size + offset,
+    token t of a request at offset t % page_size; the reference has no
+    paged Reposition, so these rules are this package's contract):
+
+    * a private page (tokens at or after ``shared_prefix[r]``, which is a
+      whole number of pages) is freed when every token it holds is
+      dropped; its page id is pushed in token order;
+    * a shared page that holds a moved token is copied to the next free
+      page: every kept token of the page gets a transition to the same
+      offset of the new page (old == new position for the tokens before the
+      first drop) and every row entry of the page points there afterwards;
+    * private moved tokens rotate in place.
+
+    Per request the loop walks pages in token order, exactly as the
+    transitions, copies and frees are emitted."""
+    nreq = len(token_counts)
+    ps = int(page_size)
+    shared_prefix = np.zeros(nreq, np.int64) if shared_prefix is None else np.asarray(shared_prefix)
+    rows = [np.array(r, dtype=np.int32, copy=True) for r in slot_rows]
+    res = dict(raw_indices=[], active_positions=[], next_position=[], src=[], dst=[], pairs=[],
+               raw=[], freed=[], rows=rows, copied_pages=0)
+    head = free_head
+    for r in range(nreq):
+        t_count = int(token_counts[r])
+        rr = np.asarray(ranges[2 * range_offsets[r]: 2 * range_offsets[r + 1]], np.int64)
+        keep = np.ones(t_count, bool)
+        for a, b in rr.reshape(-1, 2):
+            keep[a:b] = False
+        first = int(rr[0]) if len(rr) else t_count
+        rank = np.cumsum(keep) - keep  # kept tokens before t
+        moved = keep & (np.arange(t_count) > first) & bool(reposition)
+        pos = np.where(keep & bool(reposition), rank, np.arange(t_count))
+        res["raw_indices"].append(np.flatnonzero(keep).astype(np.int32))
+        res["active_positions"].append(pos[keep].astype(np.int32))
+        res["next_position"].append(int(keep.sum()) if moved.any() else t_count)
+        p_len = int(shared_prefix[r])
+        row = rows[r]
+        for g0 in range(0, t_count, ps):
+            g1 = min(g0 + ps, t_count)
+            shared = g0 < p_len
+            cow = shared and bool(moved[g0:g1].any())
+            if cow:
+                new_page = int(free_pages[head % len(free_pages)])
+                head += 1
+                res["copied_pages"] += 1
+            for t in range(g0, g1):
+                if keep[t] and (moved[t] or cow):
+                    fresh = new_page * ps + t % ps if cow else int(row[t])
+                    res["src"].append(int(row[t]))
+                    res["dst"].append(fresh)
+                    res["pairs"].append((t, int(pos[t])))
+                    res["raw"].append(t)
+            if cow:
+                row[g0:g1] = new_page * ps + np.arange(g0, g1) % ps
+            if not shared and not keep[g0:g1].any():
+                res["freed"].append(int(row[g0]) // ps)
+    res["free_head"] = head
+    res["free_tail"] = free_tail + len(res["freed"])
+    for k in ("src", "dst", "raw", "freed"):
+        res[k] = np.asarray(res[k], np.int32)
+    res["pairs"] = np.asarray(res["pairs"], np.int32).reshape(-1, 2)
+    return res
+
+
 # --------------------------------------------------------------------------
 # Reposition
 # --------------------------------------------------------------------------
