@@ -263,6 +263,69 @@ def dist_barrier(world):
         dist.barrier()
 
 
+def reference_triton():
+    """The reference's own Triton kernels, loaded unmodified from the
+    reference package installed in baseline/_ref (pip --target of its
+    akv/system project): {"reposition": context_reposition module,
+    "page_table": context_page_table module}; None when not installed or
+    Triton is unusable.  They are the same-box GPU competitor: Triton JITs
+    them for sm_100 on first use."""
+    base = os.path.join(ROOT, "baseline", "_ref", "akv", "system", "sglang", "kernels", "ops",
+                        "attention")
+    paths = {"reposition": os.path.join(base, "context_reposition.py"),
+             "page_table": os.path.join(base, "context_page_table.py")}
+    if not all(os.path.exists(p) for p in paths.values()):
+        return None
+    import importlib.util
+
+    mods = {}
+    try:
+        for name, path in paths.items():
+            spec = importlib.util.spec_from_file_location(f"akv_reference_{name}", path)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            mods[name] = mod
+    except Exception:
+        return None
+    return mods
+
+
+def time_launches(fn, steps, stream, warmup=2):
+    """Mean CUDA-event time of ``fn()`` over ``steps`` back-to-back calls
+    (after ``warmup`` untimed calls), in ms."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        fn()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / steps
+
+
+def triton_versus_ours(ref, k_ptrs, v_ptrs, k0, v0, src, dst, pairs, cache, steps, stream,
+                       our_bytes):
+    """One reposition list through the reference's Triton launch and through
+    ours (same pools, slots and positions): ms of each and the ratio.  The
+    reference always moves the K tail and V as well (its contract is a copy
+    to fresh slots), so on an in-place list it does more work than ours."""
+    from akv_b200.context_reposition import reposition_kv_layers
+
+    def theirs():
+        ref["reposition"].reposition_kv_layers(k_ptrs, v_ptrs, k0, v0, src, dst, pairs, cache)
+
+    def ours():
+        reposition_kv_layers(k_ptrs, v_ptrs, k0, v0, src, dst, pairs, cache)
+
+    t_ref = time_launches(theirs, steps, stream)
+    t_ours = time_launches(ours, steps, stream)
+    return {"transitions": int(src.numel()), "triton_ms": round(t_ref, 4),
+            "ours_ms": round(t_ours, 4), "speedup": round(t_ref / t_ours, 2),
+            "ours_gb_per_s": round(our_bytes / (t_ours / 1e3) / 1e9, 1)}
+
+
 def cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng, threads):
     """One step of the reference's CPU path: its C++ event compiler
     (oracle/_ref) + numpy decode view + the reposition restatement over a
@@ -518,6 +581,17 @@ def run_ours(args):
     achieved = rep_bytes / (rep_mean / 1e3) / 1e9
     traffic = ncu_traffic(args.workload) if world == 1 else None
 
+    # The reference's Triton reposition kernel on the same box, on the same
+    # transitions (in place: destination = source).
+    triton_ref = None
+    ref = reference_triton()
+    if ref is not None and world == 1:
+        n = moved
+        triton_ref = triton_versus_ours(
+            ref, k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source[:n],
+            res.transition_source[:n], res.transition_pairs[:n], cache, 5, stream, rep_bytes)
+        triton_ref["what"] = ("c2 moved tokens in place (destination = source); the Triton "
+                              "kernel also rewrites V, which in place is the same bytes")
     # Second metric: paged GQA decode attention over the compacted cache (c4).
     del k_pools, v_pools
     torch.cuda.empty_cache()
@@ -573,6 +647,7 @@ def run_ours(args):
                              "reposition": round(rep_mean, 4)},
             "gpu_launches": 4 * args.steps,
             "cpu_baseline": cpu,
+            "triton_reference": triton_ref,
             "event_compiler": compiler,
             "prefill_attention": prefill,
             "active_slots": gather,
@@ -783,6 +858,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
     stream = torch.cuda.current_stream(dev)
     peak, peak_kind = measured_peak()
     comp = DropCompactor(total, prog.requests, max(1, len(prog.ranges) // 2), dev)
+    ref = reference_triton()
     out = {}
     for ps in page_sizes:
         rows, n_units, (kept, moved, cow, copied, freed) = layouts[ps]
@@ -845,6 +921,36 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
         torch.cuda.synchronize()
         drop_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
         rep_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+        # The two kinds of transition in separate launches (split once,
+        # outside any timed region): copy-on-write moves K and V to fresh
+        # slots, in-place rotates the rotary part only.
+        split = {}
+        cow_mask = src != res.transition_destination[:n]
+        for kind, sel in (("copy_on_write", cow_mask), ("in_place", ~cow_mask)):
+            s_src = src[sel].contiguous()
+            s_dst = res.transition_destination[:n][sel].contiguous()
+            s_pairs = res.transition_pairs[:n][sel].contiguous()
+            cnt = int(s_src.numel())
+            per = (4 if kind == "copy_on_write" else 2) * dim * 2 * layers * heads
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(steps)]
+            for a0, a1 in [(None, None)] * 2 + evs:
+                if a0 is not None:
+                    a0.record(stream)
+                reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], s_src, s_dst,
+                                     s_pairs, cache)
+                if a1 is not None:
+                    a1.record(stream)
+            torch.cuda.synchronize()
+            k_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+            split[kind] = {"transitions": cnt, "ms": round(k_ms, 4),
+                           "algorithmic_bytes": cnt * per,
+                           "achieved": round(cnt * per / (k_ms / 1e3) / 1e9, 1),
+                           "frac": round(cnt * per / (k_ms / 1e3) / 1e9 / peak, 4)}
+            if ref is not None and world == 1 and cnt:
+                split[kind]["triton_reference"] = triton_versus_ours(
+                    ref, k_ptrs, v_ptrs, k_pools[0], v_pools[0], s_src, s_dst, s_pairs, cache,
+                    3, stream, cnt * per)
         # e2e through the public API from host memory: validate + pack + one
         # H2D copy + launches, and the decode view read back every step.
         view = torch.empty(2 * kept, dtype=torch.int32, pin_memory=True)
@@ -883,6 +989,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
             "e2e": {"value": round(step_bytes * e2e_steps / e2e_s / 1e9, 2), "unit": UNIT,
                     "h2d_bytes_per_step": prepared["h2d_bytes"], "d2h_bytes_per_step": 8 * kept},
             "breakdown_ms": {"drop_compact": round(drop_ms, 4), "reposition": round(rep_ms, 4)},
+            "reposition_by_kind": split,
             "roofline": {"bound": "hbm", "kernel": "reposition_kernel",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
@@ -1384,6 +1491,55 @@ def bench_decode_metadata(dev, world, rank, warmup, steps, seed=0, generated=4):
     del graph
     n_window = int(w_len.sum().item())
     alg = 12 * prefix_keys + 8 * (n_full - prefix_keys) + 12 * n_window
+    # The reference's Triton page-table kernels on the same registry, as its
+    # ContextDecodeRegistry drives them (context_backend.py:754-809): full
+    # indices over the cumulative lengths; window lengths, their cumsum and
+    # starts, then window indices.  Checked equal to ours, then timed the
+    # same way (graph of `steps` steps).
+    triton_ref = None
+    ref = reference_triton()
+    if ref is not None:
+        pt = ref["page_table"]
+        r_indptr = torch.zeros(batch + 1, dtype=torch.int32, device=dev)
+        r_indices = torch.empty_like(kv_indices)
+        r_wlen = torch.empty_like(seq_lens)
+        r_windptr = torch.zeros(batch + 1, dtype=torch.int32, device=dev)
+        r_windices = torch.empty_like(w_indices)
+
+        def ref_step():
+            r_indptr[1:] = seq_lens.cumsum(0)
+            pt.context_decode_indices[(batch,)](
+                registry, table, rows, seq_lens, r_indptr, r_indices, None, None,
+                ROW_STRIDE=table.stride(0), TRANSLATE=False, MULTIPLIER=1, HAS_START=False)
+            pt.context_window_lengths[(batch,)](registry, rows, seq_lens, r_wlen, 128)
+            r_windptr[1:] = r_wlen.cumsum(0)
+            starts = seq_lens - r_wlen
+            pt.context_decode_indices[(batch,)](
+                registry, table, rows, r_wlen, r_windptr, r_windices, starts, None,
+                ROW_STRIDE=table.stride(0), TRANSLATE=False, MULTIPLIER=1, HAS_START=True)
+
+        for _ in range(warmup):
+            ref_step()
+        torch.cuda.synchronize()
+        same = (torch.equal(r_indptr, kv_indptr) and torch.equal(r_indices, kv_indices) and
+                torch.equal(r_wlen, w_len) and torch.equal(r_windptr, w_indptr) and
+                torch.equal(r_windices[:n_window], w_indices[:n_window]))
+        ref_eager = timed(lambda: [ref_step() for _ in range(steps)])
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(steps):
+                ref_step()
+        graph.replay()
+        torch.cuda.synchronize()
+        ref_ms = timed(graph.replay)
+        del graph
+        triton_ref = {"triton_ms_per_step": round(ref_ms, 4),
+                      "triton_eager_ms_per_step": round(ref_eager, 4),
+                      "ours_ms_per_step": round(ms, 4), "speedup": round(ref_ms / ms, 2),
+                      "outputs_equal": bool(same),
+                      "what": "context_decode_indices (full) + context_window_lengths + "
+                              "context_decode_indices (window 128) with the registry's "
+                              "cumsum / starts, graph-captured like ours"}
     peak, peak_kind = measured_peak()
     gbs = alg / (ms / 1e3) / 1e9
     return {
@@ -1397,6 +1553,7 @@ def bench_decode_metadata(dev, world, rank, warmup, steps, seed=0, generated=4):
                      "algorithmic_bytes_per_step": alg},
         "eager_ms_per_step": round(ms_eager, 4),
         "gpu_launches_per_step": 4,
+        "triton_reference": triton_ref,
     }
 
 
