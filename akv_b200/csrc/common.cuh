@@ -4,11 +4,24 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include "akv_b200.h"
 
 namespace akv {
+
+// A named NVTX range over an entry point's host scope (its checks and
+// launches).  Header-only NVTX v3: without a profiler attached each push and
+// pop is a check of an unset function pointer; nsys / ncu show the range
+// and the kernels it enqueued under it.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define AKV_NVTX_RANGE(name) ::akv::NvtxRange akv_nvtx_range_(name)
 
 constexpr int kNumSMs = 148;
 

@@ -426,6 +426,7 @@ extern "C" int akv_decode_attention(
     const int32_t* merge, float* partial_acc,
     float* partial_ml, void* out, int64_t out_stride_batch, int64_t out_stride_head, float* lse,
     int32_t* error_flag, void* stream) {
+  AKV_NVTX_RANGE("akv_decode_attention");
   using namespace akv;
   if (batch < 0 || n_items < 0 || (cta_items != nullptr && n_ctas < 0) || num_kv_heads <= 0 ||
       num_q_heads != num_kv_heads * kGroup ||

@@ -621,6 +621,7 @@ extern "C" int akv_drop_compact(
     int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
     int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
     int32_t* freed_slots, int32_t* totals, int32_t* status, void* workspace, void* stream) {
+  AKV_NVTX_RANGE("akv_drop_compact");
   return akv::drop_compact(n_requests, token_offsets, tile_offsets, n_tiles, range_offsets,
                            ranges, shared_prefix, req_to_token, row_ids, row_stride, reposition,
                            1, ring, ring_capacity, ring_state, keep_mask, positions,
@@ -641,6 +642,7 @@ extern "C" int akv_drop_compact_paged(
     int32_t* transition_destination, int32_t* transition_pairs, int32_t* transition_raw,
     int32_t* freed_offsets, int32_t* freed_slots, int32_t* totals, int32_t* status,
     void* workspace, void* stream) {
+  AKV_NVTX_RANGE("akv_drop_compact_paged");
   return akv::drop_compact(n_requests, token_offsets, tile_offsets, n_tiles, range_offsets,
                            ranges, shared_prefix, req_to_token, row_ids, row_stride, reposition,
                            page_size, ring, ring_capacity, ring_state, keep_mask, positions,
@@ -725,6 +727,7 @@ extern "C" int akv_drop_compact_static(
     int32_t* transition_offsets, int32_t* transition_source, int32_t* transition_destination,
     int32_t* transition_pairs, int32_t* transition_raw, int32_t* freed_offsets,
     int32_t* freed_slots, int32_t* totals, int32_t* status, void* stream) {
+  AKV_NVTX_RANGE("akv_drop_compact_static");
   using namespace akv;
   if (n_requests < 0 || n_tiles < 0 || n_requests > kStaticMaxRequests ||
       n_tiles > kStaticMaxTiles)

@@ -751,6 +751,7 @@ extern "C" int64_t akv_compile_layouts_workspace_bytes(int32_t n_requests, int64
 }
 
 extern "C" int akv_compile_layouts(const akv_layout_batch* batch, void* stream) {
+  AKV_NVTX_RANGE("akv_compile_layouts");
   using namespace akv;
   if (batch == nullptr) return AKV_ERR_INVALID;
   const akv_layout_batch& x = *batch;

@@ -106,6 +106,7 @@ extern "C" int64_t akv_gather_slots_chunk(void) { return akv::kSlotChunk; }
 
 extern "C" int akv_gather_slots(const int64_t* tasks, const int32_t* chunks, int32_t n_chunks,
                                 const int64_t* indices, int32_t* error_flag, void* stream) {
+  AKV_NVTX_RANGE("akv_gather_slots");
   using namespace akv;
   if (n_chunks < 0) return AKV_ERR_INVALID;
   if (n_chunks == 0) return AKV_OK;

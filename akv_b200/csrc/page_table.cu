@@ -427,6 +427,7 @@ extern "C" int akv_context_decode_indices(
     const void* indptr, int32_t indptr_is64, void* output, int32_t output_is64,
     const void* starts, int32_t starts_is64, const void* mapping, int32_t mapping_is64,
     int64_t multiplier, int32_t batch, void* stream) {
+  AKV_NVTX_RANGE("akv_context_decode_indices");
   using namespace akv;
   if (batch < 0 || batch > 65535 || !registry || !req_to_token || !row_ids || !lengths ||
       !indptr || !output)
@@ -443,6 +444,7 @@ extern "C" int akv_context_window_lengths(
     const int64_t* registry, const void* row_ids, int32_t row_ids_is64, const void* lengths,
     int32_t lengths_is64, void* output, int32_t output_is64, int64_t window, int32_t batch,
     void* stream) {
+  AKV_NVTX_RANGE("akv_context_window_lengths");
   using namespace akv;
   if (batch < 0 || !registry || !row_ids || !lengths || !output) return AKV_ERR_INVALID;
   if (batch == 0) return AKV_OK;
@@ -457,6 +459,7 @@ extern "C" int akv_build_decode_metadata(
     const int64_t* row_ids, const int64_t* seq_lens, int64_t window, const int64_t* mapping,
     int64_t multiplier, int32_t batch, int32_t* kv_indptr, int64_t* lengths_out,
     int64_t* starts_out, int32_t* kv_indices, void* stream) {
+  AKV_NVTX_RANGE("akv_build_decode_metadata");
   using namespace akv;
   if (batch < 0 || batch > 65535 || !registry || !req_to_token || !row_ids || !seq_lens ||
       !kv_indptr || !kv_indices)
@@ -480,6 +483,7 @@ extern "C" int akv_build_decode_metadata(
 extern "C" int akv_write_row_slots(const int64_t* pointers, const void* rows, int32_t rows_is64,
                                    const void* columns, int32_t columns_is64, const void* values,
                                    int32_t values_is64, int64_t n, void* stream) {
+  AKV_NVTX_RANGE("akv_write_row_slots");
   using namespace akv;
   if (n < 0 || (n > 0 && (!pointers || !rows || !columns || !values))) return AKV_ERR_INVALID;
   if (n == 0) return AKV_OK;
@@ -494,6 +498,7 @@ extern "C" int akv_active_slots(const int32_t* row, int64_t row_len,
                                 const int32_t* device_indices, int64_t start, int64_t n_indices,
                                 int64_t generated_start, int64_t raw_end, int32_t* out,
                                 int32_t* error_flag, void* stream) {
+  AKV_NVTX_RANGE("akv_active_slots");
   using namespace akv;
   if (row_len < 0 || start < 0 || n_indices < start || generated_start < 0)
     return AKV_ERR_INVALID;
@@ -514,6 +519,7 @@ extern "C" int64_t akv_active_slots_chunk(void) { return akv::kGatherChunk; }
 extern "C" int akv_active_slots_batch(const int64_t* meta, const int64_t* out_offsets,
                                       const int32_t* chunks, int32_t n_chunks, int32_t* out,
                                       int32_t* error_flag, void* stream) {
+  AKV_NVTX_RANGE("akv_active_slots_batch");
   using namespace akv;
   if (n_chunks < 0) return AKV_ERR_INVALID;
   if (n_chunks == 0) return AKV_OK;

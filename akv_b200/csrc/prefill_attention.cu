@@ -1377,6 +1377,7 @@ extern "C" int akv_context_attention(
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, const int32_t* work,
     int32_t n_items, void* out, int64_t out_stride_token, int64_t out_stride_head, float* lse,
     int32_t* error_flag, int32_t variant, void* stream) {
+  AKV_NVTX_RANGE("akv_context_attention");
   using namespace akv;
   if (n_items < 0 || num_kv_heads <= 0 || num_q_heads != num_kv_heads * kGroupP ||
       num_kv_heads > 65535 || num_slots <= 0)

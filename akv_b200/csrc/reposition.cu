@@ -673,6 +673,7 @@ extern "C" int akv_reposition_kv_layers(
     const int32_t* count_device, const void* cos_sin_cache, int32_t cache_dtype,
     int64_t cache_stride, int32_t is_neox_style, int32_t skip_unmapped, int64_t num_slots,
     int64_t max_position, int32_t* error_flag, void* stream) {
+  AKV_NVTX_RANGE("akv_reposition_kv_layers");
   using namespace akv;
   if (count < 0 || n_layers < 0 || n_layers > kMaxLayers || num_heads <= 0 || head_dim <= 0 ||
       rotary_dim <= 0 || rotary_dim > head_dim || (rotary_dim & 1) || position_stride < 2)
@@ -731,6 +732,7 @@ extern "C" int akv_reposition_kv_layers(
 extern "C" int akv_reposition_divide(const float* numerators, const float* denominators,
                                      float* quotients, int64_t count, int32_t method,
                                      void* stream) {
+  AKV_NVTX_RANGE("akv_reposition_divide");
   using namespace akv;
   if (count < 0 || (method != 0 && method != 1) ||
       (count > 0 && (!numerators || !denominators || !quotients)))

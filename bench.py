@@ -96,6 +96,8 @@ def parse_args():
                    help="c4p: head_dim of the prefill shape")
     p.add_argument("--page-size", type=int, default=1, choices=[1, 16],
                    help="c3: page size of the KV pool")
+    p.add_argument("--requests", type=int, default=None,
+                   help="c3 / c5: number of requests (a smaller cut for ncu captures)")
     return p.parse_args()
 
 
@@ -599,7 +601,9 @@ def run_ours(args):
     # default (c2) line only.
     attention = compiler = prefill = gather = occurrence = metadata = None
     c3 = {}
+    c5 = None
     if args.workload == "c2":
+        c5 = bench_c5(dev, world, rank, 2, max(3, min(args.steps, 10)))
         c3 = bench_c3(dev, world, rank, 3, max(5, min(args.steps, 20)))
         attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                     max(5, min(args.steps // 20, 20)))
@@ -653,6 +657,7 @@ def run_ours(args):
             "active_slots": gather,
             "occurrence_binding": occurrence,
             "decode_metadata": metadata,
+            "c5": c5,
             "c3_page_size_1": c3.get(1),
             "c3_page_size_16": c3.get(16),
             "decode_attention": attention,
@@ -662,7 +667,8 @@ def run_ours(args):
         # sees every section's headline: value, unit, kernel fraction of the
         # HBM (or tensor) peak, e2e and CPU-baseline values.
         summary = {}
-        for name, sec in (("c2", line), ("c3_ps1", c3.get(1)), ("c3_ps16", c3.get(16)),
+        for name, sec in (("c2", line), ("c5", c5), ("c3_ps1", c3.get(1)),
+                          ("c3_ps16", c3.get(16)),
                           ("decode_attention", attention), ("prefill_attention", prefill),
                           ("event_compiler", compiler), ("decode_metadata", metadata),
                           ("active_slots", gather), ("occurrence_binding", occurrence)):
@@ -811,7 +817,7 @@ def c3_counts(prog, page_size):
 
 
 def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers=36,
-             cpu=True, e2e_steps=5):
+             cpu=True, e2e_steps=5, requests=64):
     """c3: batched agent serving -- 64 requests (lengths U{2K..32K}, 1.18M
     tokens), one radix-shared prefix of 1K..4K tokens (a whole number of
     16-token pages) whose moved tokens must copy-on-write, per-request drop
@@ -833,7 +839,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
 
     heads_total, dim = 8, 64
     heads = heads_total // world
-    prog = workloads.c3_program(seed=seed, page_align=16)
+    prog = workloads.c3_program(seed=seed, page_align=16, requests=requests)
     total = prog.total_tokens
     layouts = {}
     pool_slots = 0
@@ -1006,6 +1012,118 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
     del k_pools, v_pools
     torch.cuda.empty_cache()
     return out
+
+
+def bench_c5(dev, world, rank, warmup, steps, requests=8, layers=80, budget_gb=96.0, seed=0):
+    """c5, the scaling configuration at its stated size: Llama-3-70B-shaped
+    cache (80 layers, 8 KV heads split 8/N per rank as SGLang TP does,
+    head_dim 128, bf16), 8 requests of 131072 tokens, 30 % dropped in 20
+    seed-placed spans each, plain RoPE theta 500000; every moved token is
+    private and rotates in place.  The full cache (344 GB) does not fit one
+    GPU or two: when this rank's share exceeds ``budget_gb``, as many layers
+    as fit are resident and each step runs the 80 layers as consecutive
+    launches over those resident layers (chunks of the pointer table), the
+    same bytes and the same per-launch shape as 80 resident layers.  At 4
+    and 8 GPUs all 80 layers are resident (one launch).  Every rank computes
+    the same drop metadata (three launches) and no collective runs."""
+    from akv_b200 import workloads
+    from akv_b200.context_drop import DropCompactor, FreeSlotRing
+    from akv_b200.context_reposition import layer_pointer_table, reposition_kv_layers
+    from akv_b200.rope import rope_cos_sin_cache
+
+    heads_total, dim = 8, 128
+    heads = heads_total // world
+    prog = workloads.c5_program(seed=seed, requests=requests)
+    rows, nslots = workloads.slot_rows(np.random.default_rng(seed), prog)
+    total, kept, moved = plan_stats(prog)
+    per_layer = nslots * heads * dim * 2 * 2  # K and V
+    resident = max(1, min(layers, int(budget_gb * 1e9 // per_layer)))
+    chunks = [min(resident, layers - c) for c in range(0, layers, resident)]
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    k_pools = [torch.randn(nslots, heads, dim, device=dev, generator=g, dtype=torch.bfloat16)
+               for _ in range(resident)]
+    v_pools = [torch.empty(nslots, heads, dim, device=dev, dtype=torch.bfloat16)
+               for _ in range(resident)]
+    k_ptrs, v_ptrs = layer_pointer_table(k_pools), layer_pointer_table(v_pools)
+    cache = rope_cos_sin_cache(131072, dim, 500000.0).to(dev)
+    table = np.zeros((prog.requests + 1, int(prog.token_counts.max())), np.int32)
+    for r in range(prog.requests):
+        table[r + 1, : len(rows[r])] = rows[r]
+    rtt = torch.from_numpy(table).to(dev)
+    row_ids = np.arange(1, prog.requests + 1)
+    freed = total - kept
+    ring = FreeSlotRing(torch.zeros(0, dtype=torch.int32),
+                        capacity=freed * (warmup + 2 * steps + 4) + 16, device=dev)
+    comp = DropCompactor(total, prog.requests, max(1, len(prog.ranges) // 2), dev)
+    prepared = comp.prepare(prog.token_counts, prog.range_offsets, prog.ranges, row_ids)
+    stream = torch.cuda.current_stream(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(chunks) + 1)]
+          for _ in range(steps)]
+
+    def step(i=None):
+        res = comp.launch(prepared, rtt, ring)
+        if i is not None:
+            ev[i][0].record(stream)
+        for c, n in enumerate(chunks):
+            reposition_kv_layers(k_ptrs[:n], v_ptrs[:n], k_pools[0], v_pools[0],
+                                 res.transition_source, res.transition_destination,
+                                 res.transition_pairs, cache, count_device=res.transition_count)
+            if i is not None:
+                ev[i][c + 1].record(stream)
+        return res
+
+    for _ in range(warmup):
+        res = step()
+    torch.cuda.synchronize()
+    res.check()
+    assert int(res.totals[1].item()) == moved
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    ms = dist_max(t0.elapsed_time(t1) / steps, world)
+    dist_barrier(world)
+    for i in range(steps):
+        step(i)
+    torch.cuda.synchronize()
+    launch_ms = statistics.mean(e[c].elapsed_time(e[c + 1]) for e in ev
+                                for c in range(len(chunks)))
+    rep_ms = statistics.mean(e[0].elapsed_time(e[-1]) for e in ev)  # all launches of a step
+    rep_bytes = moved * layers * heads * 2 * dim * 2
+    drop_bytes = total + 4 * total + 8 * kept + 4 * (total - kept) + 12 * moved
+    per_launch = moved * chunks[0] * heads * 2 * dim * 2
+    peak, peak_kind = measured_peak()
+    achieved = rep_bytes / (rep_ms / 1e3) / 1e9
+    achieved_max = dist_max(achieved, world)
+    achieved_min = -dist_max(-achieved, world)
+    del k_pools, v_pools
+    torch.cuda.empty_cache()
+    return {
+        "metric": METRIC, "value": round((rep_bytes + drop_bytes) * world / (ms / 1e3) / 1e9, 2),
+        "unit": UNIT, "ms_per_step": round(ms, 4), "n_gpus": world, "scaling": "strong",
+        "config": {"workload": "c5", "requests": prog.requests, "tokens": total,
+                   "moved_tokens": moved, "layers": layers, "kv_heads": heads_total,
+                   "kv_heads_per_gpu": heads, "head_dim": dim, "rope": "rope500000",
+                   "resident_layers": resident, "launches_per_step": len(chunks),
+                   "reposition": "in place", "parallelism": f"kv-head tp{world}",
+                   "l2": f"resident K pools {resident * nslots * heads * dim * 2 / 1e9:.0f} GB "
+                         "per GPU, larger than L2; no flush"},
+        "roofline": {"bound": "hbm", "kernel": "reposition_kernel",
+                     "achieved": round(achieved_min, 1), "achieved_max_rank": round(achieved_max, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved_min / peak, 4),
+                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": per_launch,
+                     "ms_per_launch": round(launch_ms, 4),
+                     "reposition_ms_per_step": round(rep_ms, 4), "per": "GPU (slowest rank)"},
+        "gpu_launches_per_step": 3 + len(chunks),
+        "clocks": clock_info,
+    }
 
 
 def cpu_reference_c3(prog, rows, layers, heads, dim, cache_np, step_bytes, sample=2000):
@@ -1720,6 +1838,21 @@ def main():
 
             dist.destroy_process_group()
         return 0
+    if args.workload == "c5" and args.impl == "ours":
+        # The scaling configuration alone, at its stated size (--requests for
+        # a smaller cut).
+        world, rank, local = dist_setup()
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = bench_c5(dev, world, rank, max(2, args.warmup), max(3, min(args.steps, 30)),
+                       requests=args.requests or 8, layers=args.layers or 80)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return 0
     if args.workload == "c3" and args.impl == "ours":
         # The batched copy-on-write step alone (--page-size 1 or 16; --layers
         # for a smaller cut under a profiler).
@@ -1727,7 +1860,8 @@ def main():
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         res = bench_c3(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)),
-                       page_sizes=(args.page_size,), layers=args.layers or 36, cpu=False)
+                       page_sizes=(args.page_size,), layers=args.layers or 36, cpu=False,
+                       requests=args.requests or 64)
         if rank == 0:
             print(json.dumps(res[args.page_size]), flush=True)
         if world > 1:

@@ -78,7 +78,8 @@ def test_reposition_matches_the_reference_triton_kernel(neox, rotary, in_place):
         torch.cuda.synchronize()
         outs.append((k, v))
     d = torch.from_numpy(dst.astype(np.int64)).to(dev)
-    for (kr, vr), (ko, vo) in zip(*outs):
+    (k_ref, v_ref), (k_ours, v_ours) = outs
+    for kr, vr, ko, vo in zip(k_ref, v_ref, k_ours, v_ours):
         assert torch.equal(kr[d].view(torch.int16), ko[d].view(torch.int16))
         assert torch.equal(vr[d].view(torch.int16), vo[d].view(torch.int16))
         # nothing else in the pools changed differently
