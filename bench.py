@@ -151,14 +151,18 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def ncu_traffic(workload):
+def ncu_traffic(workload, algorithmic=None):
     """Per-launch DRAM bytes of the reposition kernel from the committed ncu
-    summary (profiles/), scaled to this workload; None if not captured."""
+    summary (profiles/reposition_<workload>.md): its measured bytes per
+    launch, or its measured traffic / algorithmic ratio times this launch's
+    algorithmic bytes; None if not captured."""
     path = os.path.join(ROOT, "profiles", f"reposition_{workload}.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
                 return int(line.split(":")[1].strip())
+            if line.startswith("traffic_ratio:") and algorithmic is not None:
+                return int(round(float(line.split(":")[1].strip()) * algorithmic))
     except OSError:
         pass
     return None
@@ -681,6 +685,15 @@ def run_ours(args):
                 item["e2e"] = sec["e2e"]["value"]
             if isinstance(sec.get("cpu_baseline"), dict):
                 item["cpu"] = sec["cpu_baseline"]["value"]
+            tri = sec.get("triton_reference")
+            if isinstance(tri, dict) and "speedup" in tri:
+                item["vs_triton"] = tri["speedup"]
+            kinds = sec.get("reposition_by_kind") or {}
+            if "copy_on_write" in kinds:
+                item["cow_frac"] = kinds["copy_on_write"]["frac"]
+                tri = kinds["copy_on_write"].get("triton_reference")
+                if tri:
+                    item["cow_vs_triton"] = tri["speedup"]
             summary[name] = item
         line["summary"] = summary
         print(json.dumps(line), flush=True)
@@ -1001,7 +1014,9 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": rep_bytes,
                          "ms_per_launch": round(rep_ms, 4),
-                         "traffic": ncu_traffic(f"c3_ps{ps}") if world == 1 else None},
+                         "traffic": ncu_traffic("c3", rep_bytes) if world == 1 else None,
+                         "traffic_source": "profiles/reposition_c3.md (4-request cut, "
+                                           "traffic / algorithmic ratio)"},
             "gpu_launches_per_step": 4,
             "clocks": clock_info,
         }
