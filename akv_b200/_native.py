@@ -15,6 +15,7 @@ import torch
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libakv_b200.so")
 
 AKV_OK, AKV_ERR_INVALID, AKV_ERR_CUDA, AKV_ERR_UNSUPPORTED = 0, 1, 2, 3
+AKV_ERR_OCC_MISSING_SOURCE, AKV_ERR_OCC_MISSING_COPY_SOURCE = 4, 5
 AKV_F16, AKV_BF16, AKV_F32 = 0, 1, 2
 GATHER_OUT64, GATHER_LITERAL, GATHER_SEG64 = 1, 2, 4
 DROP_RING_UNDERFLOW, DROP_RING_OVERFLOW, DROP_BAD_RANGE, DROP_NO_ACTIVE = 1, 2, 4, 8
@@ -67,6 +68,7 @@ SIGNATURES = {
         _I32, _P, _P, _I32, _P, _P, _P, _P, _P, _I64, _I32, _I32, _P, _I64, _P, _P, _P, _P, _P,
         _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
     ],
+    "akv_occurrence_advance_indices": [_P, _P],
     "akv_drop_compact_static_max_requests": [],
     "akv_drop_compact_static_max_tiles": [],
     "akv_drop_compact_static": [

@@ -11,9 +11,11 @@ request -- one concatenation of the state's slots with the new ones, one
 gather per output field, int32 casts -- and the scheduler concatenates the
 per-request results (akv/system/sglang.patch:3133-3180).
 
-This module keeps the CPU decisions (restated from the reference, same
-checks and messages) and does the device part of a whole forward in ONE
-host-to-device copy and ONE launch:
+This module keeps the reference's checks and messages in Python, derives
+every ownership index natively on the host (``akv_occurrence_advance_indices``,
+passes over the arrays described in csrc/occurrence_plan.cu) and does the
+device part of a whole forward in ONE host-to-device copy (int32 indices)
+and ONE launch:
 
 * ``advance`` is a drop-in for ``OccurrenceState.advance`` (:644-755);
 * ``terminal_slots`` for ``OccurrenceState.terminal_slots`` (:757-768);
@@ -34,10 +36,46 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+import ctypes
+
 from . import _native
 
 _MAX_SEGMENTS = 4
 _TASK_WORDS = 12
+_P, _I64 = ctypes.c_void_p, ctypes.c_int64
+
+
+class _AdvanceIn(ctypes.Structure):
+    """struct akv_advance_in of include/akv_b200.h, field for field."""
+
+    _fields_ = [("n", _I64), ("start", _I64), ("end", _I64), ("count", _I64), ("n_old", _I64),
+                ("n_query", _I64), ("n_extra", _I64), ("n_copy", _I64), ("owned", _P),
+                ("canonical_rows", _P), ("terminal_rows", _P), ("canonical_positions", _P),
+                ("swa_resident", _P), ("birth_occurrences", _P), ("terminal_occurrences", _P),
+                ("occurrence_positions", _P), ("source_rows", _P), ("allocated", _P),
+                ("copy_occurrences", _P), ("copy_source_rows", _P), ("plan_terminal", _P),
+                ("visible_until", _P)]
+
+
+class _AdvanceOut(ctypes.Structure):
+    """struct akv_advance_out of include/akv_b200.h, field for field."""
+
+    _fields_ = [("occurrence_rows", _P), ("copy_source_rows", _P),
+                ("copy_destination_rows", _P), ("retained", _P), ("retired", _P),
+                ("unused_swa", _P), ("next_canonical", _P), ("next_terminal", _P),
+                ("next_positions", _P), ("next_owned", _P), ("next_swa", _P),
+                ("retired_swa", _P), ("n_retained", _I64), ("n_retired", _I64),
+                ("n_unused_swa", _I64)]
+
+
+def _host(t, dtype):
+    """A CPU tensor or array as a contiguous numpy array of ``dtype``."""
+    a = t.numpy() if isinstance(t, torch.Tensor) else np.asarray(t)
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _addr(a):
+    return a.ctypes.data if a.size else None
 
 
 class SlotGather:
@@ -63,17 +101,21 @@ class SlotGather:
         """out[i] = concat(segments)[indices[i]] (-1 where the index is
         negative), or indices[i] itself with ``literal``; out is int32 or
         int64 (int64 values are cast to int32 as torch does)."""
-        idx = np.asarray(indices, dtype=np.int64).reshape(-1)
+        idx = np.asarray(indices).reshape(-1)
         if out.dtype not in (torch.int32, torch.int64) or out.get_device() != self._index or \
                 not out.is_contiguous() or out.numel() != len(idx):
             raise ValueError("gather output must be a contiguous int32/int64 vector on the "
                              "device with one element per index")
+        if idx.dtype.kind not in "iu" and len(idx):
+            raise ValueError("gather indices must be integers")
+        if len(idx) and (int(idx.min()) < -2**31 or int(idx.max()) > 2**31 - 1):
+            raise ValueError("gather indices and literals must fit in int32")
         self._add(out, idx, segments, literal)
 
     def _add(self, out, idx, segments=(), literal=False):
         """``add`` for an output this module allocated (contiguous, on the
         device, one element per index): the segments are still checked."""
-        idx = np.asarray(idx, dtype=np.int64).reshape(-1)
+        idx = np.asarray(idx).reshape(-1)
         m = len(idx)
         segments = tuple(segments)
         key = tuple(id(s) for s in segments)
@@ -116,19 +158,21 @@ class SlotGather:
         return chunk, lengths, counts
 
     def words(self):
-        """Length of the packed program in int64 words."""
+        """Length of the packed program in int64 words (indices are int32,
+        two to a word)."""
         _, lengths, counts = self._sizes()
-        return _TASK_WORDS * len(self._tasks) + int(counts.sum()) + int(lengths.sum())
+        return _TASK_WORDS * len(self._tasks) + int(counts.sum()) + (int(lengths.sum()) + 1) // 2
 
     def pack(self, out: np.ndarray | None = None):
         """(words, n_tasks, n_chunks): the int64 task table, the chunk table
         (one word per chunk: the int32 pair {task, first output}) and the
-        indices, in that order; written into ``out`` when given."""
+        int32 indices, in that order; written into ``out`` when given."""
         chunk, lengths, counts = self._sizes()
         n, n_chunks = len(self._tasks), int(counts.sum())
         if n_chunks > 2**31 - 1:
             raise ValueError("too many slot gather chunks for one launch")
-        total = _TASK_WORDS * n + n_chunks + int(lengths.sum())
+        n_idx = int(lengths.sum())
+        total = _TASK_WORDS * n + n_chunks + (n_idx + 1) // 2
         words = np.empty(total, np.int64) if out is None else out[:total]
         if n:
             table = words[:_TASK_WORDS * n].reshape(n, _TASK_WORDS)
@@ -139,10 +183,9 @@ class SlotGather:
         pairs = words[_TASK_WORDS * n:_TASK_WORDS * n + n_chunks].view(np.int32).reshape(-1, 2)
         pairs[:, 0] = task
         pairs[:, 1] = (np.arange(n_chunks) - start) * chunk
-        at = _TASK_WORDS * n + n_chunks
-        for _, idx, _, _ in self._tasks:
-            words[at:at + len(idx)] = idx
-            at += len(idx)
+        if n_idx:
+            idx = words[_TASK_WORDS * n + n_chunks:].view(np.int32)[:n_idx]
+            np.concatenate([t[1] for t in self._tasks], out=idx, casting="unsafe")
         return words, n, n_chunks
 
     def launch(self, error_flag: torch.Tensor | None = None):
@@ -160,7 +203,7 @@ class SlotGather:
         if n_chunks == 0:
             return
         dev = host.to(self.device, non_blocking=True)
-        base = dev.data_ptr()
+        base = dev.data_ptr()  # indices: int32 after the two tables
         status = _native.lib.akv_gather_slots(
             base, base + 8 * _TASK_WORDS * n_tasks, n_chunks,
             base + 8 * (_TASK_WORDS * n_tasks + n_chunks), _native.ptr(error_flag),
@@ -185,11 +228,12 @@ class OccurrenceAdvance:
 
 class _AdvancePlan:
     """The CPU half of ``OccurrenceState.advance`` (occurrence.py:644-755):
-    every ownership decision and index, no device work."""
+    the reference's admission check and messages here, every ownership
+    index from ``akv_occurrence_advance_indices`` (host code), no device
+    work."""
 
     def __init__(self, state, window, plan, query_slots, extra_slots, visible_until):
-        birth_occ = window.birth_occurrences.numpy()
-        n = len(birth_occ)
+        n = len(window.birth_occurrences)
         start, end = len(state.canonical_rows), len(plan.terminal_occurrences)
         slots = state.slots
         if (
@@ -208,73 +252,65 @@ class _AdvancePlan:
             raise ValueError("Context admission does not cover the selected window")
         n_old, n_query, n_extra = len(slots), len(query_slots), len(extra_slots)
         total = n_old + n_query + n_extra
-        owned = np.concatenate((state.owned.numpy(), np.ones(n_query + n_extra, np.bool_)))
-        # Rows of `sources` address the state's canonical owners [0, n) and
-        # its terminal owners [n, 2n); values are indices into all slots.
-        canonical = np.full(n, -1, np.int64)
-        canonical[:start] = state.canonical_rows.numpy()
-        canonical[start:end] = np.arange(n_old, n_old + n_query)
-        terminal = np.full(n, -1, np.int64)
-        terminal[:start] = state.terminal_rows.numpy()
-        sources = np.concatenate((canonical, terminal))
-        rows = plan.source_rows.numpy()
-        occurrences = np.full(len(rows), -1, np.int64)
-        reuse = rows >= 0
-        occurrences[reuse] = sources[rows[reuse]]
-        if np.any(occurrences[reuse] < 0):
+        count = len(plan.source_rows)
+        n_copy = len(plan.copy_occurrences)
+        swa_in = state.swa_resident
+        arrays = dict(
+            owned=_host(state.owned, np.uint8), canonical_rows=_host(state.canonical_rows, np.int64),
+            terminal_rows=_host(state.terminal_rows, np.int64),
+            canonical_positions=_host(state.canonical_positions, np.int32),
+            swa_resident=_host(swa_in, np.uint8) if swa_in is not None else None,
+            birth_occurrences=_host(window.birth_occurrences, np.int64),
+            terminal_occurrences=_host(window.terminal_occurrences, np.int64),
+            occurrence_positions=_host(window.occurrence_positions, np.int32),
+            source_rows=_host(plan.source_rows, np.int64),
+            allocated=_host(plan.allocated_occurrences, np.int64),
+            copy_occurrences=_host(plan.copy_occurrences, np.int64),
+            copy_source_rows=_host(plan.copy_source_rows, np.int64),
+            plan_terminal=_host(plan.terminal_occurrences, np.int64),
+            visible_until=_host(visible_until, np.int32))
+        inp = _AdvanceIn(n, start, end, count, n_old, n_query, n_extra, n_copy,
+                         *[None if a is None else _addr(a) for a in arrays.values()])
+        occ = np.empty(count, np.int64)
+        copy_src, copy_dst = np.empty(n_copy, np.int64), np.empty(n_copy, np.int64)
+        retained, retired = np.empty(total, np.int64), np.empty(total, np.int64)
+        unused_swa = np.empty(n_copy, np.int64)
+        canon_rows, term_rows = np.empty(end, np.int64), np.empty(end, np.int64)
+        positions = np.empty(end, np.int32)
+        owned_next = np.empty(total, np.uint8)
+        swa_next = np.empty(total, np.uint8) if swa_in is not None else None
+        swa_retired = np.empty(total, np.uint8) if swa_in is not None else None
+        out = _AdvanceOut(_addr(occ), _addr(copy_src), _addr(copy_dst), _addr(retained),
+                          _addr(retired), _addr(unused_swa), _addr(canon_rows),
+                          _addr(term_rows), _addr(positions), _addr(owned_next),
+                          None if swa_next is None else _addr(swa_next),
+                          None if swa_retired is None else _addr(swa_retired), 0, 0, 0)
+        status = _native.lib.akv_occurrence_advance_indices(ctypes.byref(inp),
+                                                            ctypes.byref(out))
+        if status == _native.AKV_ERR_OCC_MISSING_SOURCE:
             raise ValueError("Context ownership plan references a missing source")
-        occurrences[plan.allocated_occurrences.numpy()] = np.arange(n_old + n_query, total)
-        copy_src = sources[plan.copy_source_rows.numpy()]
-        if np.any(copy_src < 0):
+        if status == _native.AKV_ERR_OCC_MISSING_COPY_SOURCE:
             raise ValueError("Context copy references a missing canonical source")
-        copy_dst = occurrences[plan.copy_occurrences.numpy()]
-        swa = None
-        unused_swa = np.empty(0, np.int64)
-        if state.swa_resident is not None:
-            swa = np.concatenate((state.swa_resident.numpy(),
-                                  np.ones(n_query + n_extra, np.bool_)))
-            swa[copy_dst] = swa[copy_src]
-            # only fresh private copy destinations without an SWA source
-            unused_swa = copy_dst[~swa[copy_dst]]
-        picked = plan.terminal_occurrences.numpy()
-        kept = picked >= 0
-        next_term = np.full(end, -1, np.int64)
-        next_term[kept] = occurrences[picked[kept]]
-        occ_pos = window.occurrence_positions.numpy()
-        positions = occ_pos[birth_occ[:end]].copy()
-        positions[:start] = state.canonical_positions.numpy()
-        same = positions == occ_pos[window.terminal_occurrences.numpy()[:end]]
-        # a same-position copy is bit-identical: read the terminal owner
-        next_canon = np.where(kept & same, next_term, canonical[:end])
-        # no later prefill query reads a source whose token is invisible by then
-        if end == n:
-            next_canon[:] = -1
-        else:
-            next_canon = np.where(visible_until.numpy()[:end] > end, next_canon, -1)
-        retained = np.unique(np.concatenate((next_canon[next_canon >= 0],
-                                             next_term[next_term >= 0])))
-        live = np.zeros(total, np.bool_)
-        live[retained] = True
-        retired = np.flatnonzero(owned & ~live)
-        remap = np.full(total, -1, np.int64)
-        remap[retained] = np.arange(len(retained))
+        _native.check(status, "occurrence advance")
+        k, r = out.n_retained, out.n_retired
         self.state_type = type(state)
         self.exact_prefix_len = state.exact_prefix_len
         self.segments = tuple(s for s in (slots, query_slots, extra_slots) if len(s)) or \
             (query_slots,)
         self.dtype, self.device = query_slots.dtype, query_slots.device
-        self.occurrences = np.maximum(occurrences, 0)
+        self.occurrences = np.maximum(occ, 0, out=occ)
         self.copy_src, self.copy_dst = copy_src, copy_dst
-        self.pairs = plan.copy_position_pairs.numpy().reshape(-1)
-        self.retained, self.retired, self.unused_swa = retained, retired, unused_swa
-        canon_rows = np.full(end, -1, np.int64)
-        has = next_canon >= 0
-        canon_rows[has] = remap[next_canon[has]]
-        term_rows = np.full(end, -1, np.int64)
-        term_rows[kept] = remap[next_term[kept]]
-        self.successor = (torch.from_numpy(owned[retained]), torch.from_numpy(canon_rows),
-                          torch.from_numpy(term_rows), torch.from_numpy(positions))
-        self.swa = swa
+        self.pairs = _host(plan.copy_position_pairs, np.int64).reshape(-1)
+        self.retained, self.retired = retained[:k], retired[:r]
+        self.unused_swa = unused_swa[: out.n_unused_swa]
+        self.successor = (torch.from_numpy(owned_next[:k].view(np.bool_)),
+                          torch.from_numpy(canon_rows), torch.from_numpy(term_rows),
+                          torch.from_numpy(positions))
+        self.swa = None
+        if swa_in is not None:
+            self.swa_retained = torch.from_numpy(swa_next[:k].view(np.bool_))
+            self.swa_retired = torch.from_numpy(swa_retired[:r].view(np.bool_))
+            self.swa = True
 
     def add_tasks(self, gather: SlotGather, occurrence_out, src_out, dst_out, pairs_out):
         """Queue this request's fields; the batch-level outputs are views the
@@ -296,10 +332,10 @@ class _AdvancePlan:
         owned, canon, term, positions = self.successor
         state = self.state_type(
             succ_slots, owned, canon, term, positions, self.exact_prefix_len,
-            torch.from_numpy(self.swa[self.retained]) if self.swa is not None else None)
+            self.swa_retained if self.swa is not None else None)
         return OccurrenceAdvance(
             state, occurrence_out, src_out, dst_out, pairs_out.view(-1, 2), retired, unused,
-            torch.from_numpy(self.swa[self.retired]) if self.swa is not None else None)
+            self.swa_retired if self.swa is not None else None)
 
 
 def advance(state, window, plan, query_slots, extra_slots, visible_until, *,

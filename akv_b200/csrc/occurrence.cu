@@ -15,7 +15,7 @@
 // outputs are materialised separately.
 //
 // Work: one block per chunk of kSlotChunk outputs of one task (the host cuts
-// each task into chunks).  Each output is one 8-byte index load, at most one
+// each task into chunks).  Each output is one 4-byte index load, at most one
 // 4- or 8-byte slot load and one store; the kernel is bound by launch and
 // latency at the sizes a forward binds (thousands of slots), and by HBM at
 // large ones.
@@ -32,7 +32,7 @@ constexpr int kMaxSegments = 4;
 
 __global__ void __launch_bounds__(kSlotThreads) gather_slots_kernel(
     const int64_t* __restrict__ tasks, const int2* __restrict__ chunks,
-    const int64_t* __restrict__ indices, int32_t* error_flag) {
+    const int32_t* __restrict__ indices, int32_t* error_flag) {
   const int2 c = chunks[blockIdx.x];
   const int64_t* t = tasks + (int64_t)kTaskWords * c.x;
   const int64_t first = __ldg(t), n = __ldg(t + 1);
@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(kSlotThreads) gather_slots_kernel(
   for (int j = 0; j < kPer; ++j) {
     const int64_t k = (int64_t)c.y + j * kSlotThreads + threadIdx.x;
     live[j] = k < n;
-    v[j] = live[j] ? __ldg(indices + first + k) : -1;
+    v[j] = live[j] ? (int64_t)__ldg(indices + first + k) : -1;
   }
   if (!literal) {
 #pragma unroll
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kSlotThreads) gather_slots_kernel(
 extern "C" int64_t akv_gather_slots_chunk(void) { return akv::kSlotChunk; }
 
 extern "C" int akv_gather_slots(const int64_t* tasks, const int32_t* chunks, int32_t n_chunks,
-                                const int64_t* indices, int32_t* error_flag, void* stream) {
+                                const int32_t* indices, int32_t* error_flag, void* stream) {
   AKV_NVTX_RANGE("akv_gather_slots");
   using namespace akv;
   if (n_chunks < 0) return AKV_ERR_INVALID;

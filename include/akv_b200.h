@@ -9,6 +9,8 @@
  *     be captured in a CUDA graph;
  *   - returns an AKV_* status.  A non-zero status means nothing was
  *     enqueued (argument errors) or the launch failed (AKV_ERR_CUDA).
+ * The one host-only entry point, akv_occurrence_advance_indices, reads and
+ * writes host memory and touches no device.
  *
  * Reference interfaces are cited as file:line relative to the reference
  * project root (thu-nics/AKV).
@@ -27,6 +29,8 @@ extern "C" {
 #define AKV_ERR_INVALID 1     /* bad argument (shape, dtype, stride, count) */
 #define AKV_ERR_CUDA 2        /* the CUDA launch failed                      */
 #define AKV_ERR_UNSUPPORTED 3 /* valid but not supported by this build       */
+#define AKV_ERR_OCC_MISSING_SOURCE 4      /* an ownership plan row has no owner */
+#define AKV_ERR_OCC_MISSING_COPY_SOURCE 5 /* a copy's source version is absent  */
 
 /* Device-side status bits written by akv_drop_compact into `status`. */
 #define AKV_DROP_RING_UNDERFLOW 1 /* not enough free slots for copy-on-write */
@@ -526,21 +530,80 @@ int akv_active_slots_batch(const int64_t* meta, const int64_t* out_offsets, cons
  *       | n_segments << 8 (0..4)
  *   [4..7] segment addresses                   [8..11] cumulative segment
  *                                                      lengths
- * For i < n: v = indices[first + i]; with AKV_GATHER_LITERAL, out[i] = v;
+ * For i < n: v = indices[first + i] (int32: a row below 2^31, or a literal
+ * of that range); with AKV_GATHER_LITERAL, out[i] = v;
  * else out[i] = -1 if v < 0, else element v of the concatenation of the
  * segments (an index at or past its end writes -1 and sets *error_flag).
  * Segments are int64 with AKV_GATHER_SEG64, else int32; out is int64 with
  * AKV_GATHER_OUT64, else int32 (the low 32 bits, as a torch int32 cast).
  * chunks: DEVICE int32 [n_chunks][2] = {task, first output of the task},
  * every task cut into pieces of akv_gather_slots_chunk() outputs (one block
- * each).  indices: DEVICE int64.  No reference counterpart as one call.
+ * each).  indices: DEVICE int32.  No reference counterpart as one call.
  */
+/*
+ * Host half of OccurrenceState.advance
+ * (akv/system/sglang/srt/context_system/occurrence.py:644-755): every
+ * ownership index of one prefill forward of one request, computed on the
+ * CPU (no device memory is touched).  All pointers are HOST memory.
+ *
+ * Rows index all = state slots ++ query slots ++ extra slots.  Outputs:
+ * occurrence_rows[count] (-1 = unbound), copy_source_rows /
+ * copy_destination_rows [n_copy], retained / retired (ascending rows; room
+ * for n_old + n_query + n_extra each) with their counts, unused_swa (room
+ * for n_copy), the successor's canonical / terminal rows and positions
+ * [end], owned flags of the retained rows and, with swa_resident, the
+ * residency of retained and retired rows (next_swa / retired_swa may be
+ * NULL without it).  Returns AKV_OK, AKV_ERR_OCC_MISSING_SOURCE (a reused
+ * occurrence's version has no owner: "Context ownership plan references a
+ * missing source"), AKV_ERR_OCC_MISSING_COPY_SOURCE ("Context copy
+ * references a missing canonical source") or AKV_ERR_INVALID (indices out
+ * of range).  The passes are described in akv_b200/csrc/occurrence_plan.cu.
+ */
+typedef struct {
+  int64_t n;          /* tokens of the occurrence window */
+  int64_t start, end; /* the state covers [0, start); this forward's queries [start, end) */
+  int64_t count;      /* occurrences of the window */
+  int64_t n_old, n_query, n_extra, n_copy;
+  const uint8_t* owned;               /* [n_old] */
+  const int64_t* canonical_rows;      /* [start] */
+  const int64_t* terminal_rows;       /* [start] */
+  const int32_t* canonical_positions; /* [start] */
+  const uint8_t* swa_resident;        /* [n_old] or NULL */
+  const int64_t* birth_occurrences;   /* [n] */
+  const int64_t* terminal_occurrences; /* [n] */
+  const int32_t* occurrence_positions; /* [count] */
+  const int64_t* source_rows;         /* [count] */
+  const int64_t* allocated;           /* [n_extra] */
+  const int64_t* copy_occurrences;    /* [n_copy] */
+  const int64_t* copy_source_rows;    /* [n_copy] */
+  const int64_t* plan_terminal;       /* [end] */
+  const int32_t* visible_until;       /* [n] */
+} akv_advance_in;
+
+typedef struct {
+  int64_t* occurrence_rows;
+  int64_t* copy_source_rows;
+  int64_t* copy_destination_rows;
+  int64_t* retained;
+  int64_t* retired;
+  int64_t* unused_swa;
+  int64_t* next_canonical;
+  int64_t* next_terminal;
+  int32_t* next_positions;
+  uint8_t* next_owned;
+  uint8_t* next_swa;
+  uint8_t* retired_swa;
+  int64_t n_retained, n_retired, n_unused_swa;
+} akv_advance_out;
+
+int akv_occurrence_advance_indices(const akv_advance_in* in, akv_advance_out* out);
+
 #define AKV_GATHER_OUT64 1
 #define AKV_GATHER_LITERAL 2
 #define AKV_GATHER_SEG64 4
 int64_t akv_gather_slots_chunk(void);
 int akv_gather_slots(const int64_t* tasks, const int32_t* chunks, int32_t n_chunks,
-                     const int64_t* indices, int32_t* error_flag, void* stream);
+                     const int32_t* indices, int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

@@ -561,7 +561,7 @@ def gather_slots(words, n_tasks, n_chunks, memory, chunk):
     words = np.asarray(words, np.int64)
     table = words[: 12 * n_tasks].reshape(n_tasks, 12)
     chunks = words[12 * n_tasks: 12 * n_tasks + n_chunks].view(np.int32).reshape(-1, 2)
-    indices = words[12 * n_tasks + n_chunks:]
+    indices = words[12 * n_tasks + n_chunks:].view(np.int32)
     writes = {t: np.zeros(int(table[t, 1]), np.int64) for t in range(n_tasks)}
     for task, first in chunks:
         first_idx, n, out_addr, flags = (int(x) for x in table[task, :4])

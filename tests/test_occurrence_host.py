@@ -211,9 +211,11 @@ def test_gather_program_chunks_and_literals():
     g.add(a, idx, segs)
     b = torch.empty(0, dtype=torch.int32)
     g.add(b, [], segs)
-    lit = rng.integers(-2**40, 2**40, size=2100)
+    lit = rng.integers(-2**31, 2**31, size=2100)
     c = torch.empty(2100, dtype=torch.int32)
     g.add(c, lit, literal=True)
+    with pytest.raises(ValueError, match="fit in int32"):
+        g.add(torch.empty(1, dtype=torch.int64), [2**31], literal=True)
     run_on_host(g)
     flat = torch.cat(segs).numpy().astype(np.int64)
     np.testing.assert_array_equal(a.numpy(), np.where(idx < 0, -1, flat[np.maximum(idx, 0)]))
