@@ -56,8 +56,14 @@ def reposition_kv_layers(
     validates positions/slots on the CPU before they reach the device, and
     keeps the KV pools and metadata alive until the stream finishes.  No
     device-to-host read, no synchronisation, no allocation.
+
+    ``page_size``: the reference accepts 1 only (context_reposition.py:
+    153-154).  Slots here are token slots (page * page_size + offset) in
+    every case, so the paged pools of ``DropCompactor(page_size=...)``
+    (powers of two from 4 to 128) are accepted as well; any other value
+    raises the reference's error.
     """
-    if page_size != 1:
+    if page_size != 1 and (page_size < 4 or page_size > 128 or page_size & (page_size - 1)):
         raise ValueError("Context Reposition requires page_size=1")
     tensors = (
         k_data_ptrs,

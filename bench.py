@@ -96,6 +96,8 @@ def parse_args():
                    help="c4p: head_dim of the prefill shape")
     p.add_argument("--page-size", type=int, default=1, choices=[1, 16],
                    help="c3: page size of the KV pool")
+    p.add_argument("--slot-layout", default="random", choices=["random", "paged16"],
+                   help="c4: where a request's keys sit in the pool")
     p.add_argument("--requests", type=int, default=None,
                    help="c3 / c5: number of requests (a smaller cut for ncu captures)")
     return p.parse_args()
@@ -603,7 +605,7 @@ def run_ours(args):
     torch.cuda.empty_cache()
     # The other sections have workloads of their own; they run beside the
     # default (c2) line only.
-    attention = compiler = prefill = gather = occurrence = metadata = None
+    attention = attention_paged = compiler = prefill = gather = occurrence = metadata = None
     c3 = {}
     c5 = None
     if args.workload == "c2":
@@ -611,6 +613,8 @@ def run_ours(args):
         c3 = bench_c3(dev, world, rank, 3, max(5, min(args.steps, 20)))
         attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                     max(5, min(args.steps // 20, 20)))
+        attention_paged = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
+                                          max(5, min(args.steps // 20, 20)), layout="paged16")
         compiler = bench_compiler(dev, world, rank, 3, 20)
         prefill = bench_prefill(dev, world, rank, 3, 5)
         gather = bench_active_slots(dev, world, rank, 3, 20)
@@ -665,6 +669,7 @@ def run_ours(args):
             "c3_page_size_1": c3.get(1),
             "c3_page_size_16": c3.get(16),
             "decode_attention": attention,
+            "decode_attention_paged16": attention_paged,
             "clocks": clock_info,
         }
         # Last, so that a reader that keeps only the end of the line still
@@ -673,7 +678,9 @@ def run_ours(args):
         summary = {}
         for name, sec in (("c2", line), ("c5", c5), ("c3_ps1", c3.get(1)),
                           ("c3_ps16", c3.get(16)),
-                          ("decode_attention", attention), ("prefill_attention", prefill),
+                          ("decode_attention", attention),
+                          ("decode_attention_paged16", attention_paged),
+                          ("prefill_attention", prefill),
                           ("event_compiler", compiler), ("decode_metadata", metadata),
                           ("active_slots", gather), ("occurrence_binding", occurrence)):
             if not sec:
@@ -704,13 +711,20 @@ def run_ours(args):
     return 0
 
 
-def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1):
+def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1,
+                    layout="random"):
     """c4: batch 128, 64 query / 8 KV heads (split 8/N per rank), head_dim 64,
     bf16, lognormal KV lengths (median 8192, sigma 1.0, max 65536), 36 layers
     alternating sliding window 128 and full attention, per-head sinks.  One
     step = one decode token for the whole batch = 36 layer launches (18
     full over all keys, 18 over the 129 visible keys of each request), each
-    layer with its own K/V pool.  tokens/s = batch / step time."""
+    layer with its own K/V pool.  tokens/s = batch / step time.
+
+    ``layout``: where a request's keys sit in the pool.  "random": every key
+    at a random slot (a page_size 1 pool after much churn; the worst case
+    for DRAM locality).  "paged16": a page_size 16 pool (the layout the
+    paged Drop keeps): a request's keys fill its own 16-slot pages in order,
+    the pages at random places in the pool."""
     from akv_b200 import workloads
     from akv_b200.context_attention import DecodeAttention
 
@@ -724,12 +738,26 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1)
     full_indptr = np.concatenate(([0], np.cumsum(lengths)))
     swa_len = np.minimum(lengths, window + 1)
     swa_indptr = np.concatenate(([0], np.cumsum(swa_len)))
-    # Keys of a request sit at random slots of its layer's pool.
-    full_idx = torch.from_numpy(rng.permutation(total).astype(np.int32)).to(dev)
-    swa_idx = torch.from_numpy(rng.permutation(int(swa_len.sum())).astype(np.int32)).to(dev)
+    def slots_for(lens):
+        if layout == "random":
+            return rng.permutation(int(lens.sum())).astype(np.int32), int(lens.sum())
+        pages_per = -(-lens // 16)
+        pages = rng.permutation(int(pages_per.sum())).astype(np.int64)
+        firsts = np.concatenate(([0], np.cumsum(pages_per)))
+        out = []
+        for b, n in enumerate(lens.tolist()):
+            i = np.arange(n)
+            out.append(pages[firsts[b] + i // 16] * 16 + i % 16)
+        return np.concatenate(out).astype(np.int32), int(pages_per.sum()) * 16
+
+    # Keys of a request sit in its layer's pool at the layout's slots.
+    full_np, full_slots = slots_for(lengths)
+    swa_np, swa_slots = slots_for(swa_len)
+    full_idx = torch.from_numpy(full_np).to(dev)
+    swa_idx = torch.from_numpy(swa_np).to(dev)
     pools = []
     for layer in range(layers):
-        slots = total if layer % 2 else int(swa_len.sum())
+        slots = full_slots if layer % 2 else swa_slots
         pools.append((torch.randn(slots, hkv, d, device=dev, generator=g, dtype=torch.bfloat16),
                       torch.randn(slots, hkv, d, device=dev, generator=g, dtype=torch.bfloat16)))
     q = torch.randn(bs, hq, d, device=dev, generator=g, dtype=torch.bfloat16)
@@ -777,7 +805,8 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1)
         "metric": "paged GQA decode attn tokens/s", "value": round(bs / (ms / 1e3), 1),
         "unit": "tokens/s", "ms_per_step": round(ms, 4), "n_gpus": world,
         "gb_per_s": round(step_bytes / (ms / 1e3) / 1e9, 1),
-        "config": {"workload": "c4", "batch": bs, "q_heads": hq_total, "kv_heads": hkv_total,
+        "config": {"workload": "c4", "slot_layout": layout, "kv_heads_per_gpu": hkv,
+                   "batch": bs, "q_heads": hq_total, "kv_heads": hkv_total,
                    "head_dim": d, "layers": layers, "sliding_window": window,
                    "kv_tokens": total, "lengths": "lognormal median 8192 sigma 1.0",
                    "sinks": True, "work_items_full": full.n_items, "chunk": full.chunk},
@@ -904,7 +933,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                 ev[i][1].record(stream)
             reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
                                  res.transition_destination, res.transition_pairs, cache,
-                                 count_device=res.transition_count)
+                                 count_device=res.transition_count, page_size=ps)
             if i is not None:
                 ev[i][2].record(stream)
             return res
@@ -1847,7 +1876,8 @@ def main():
         dev = torch.device("cuda", local)
         torch.cuda.set_device(dev)
         res = bench_attention(dev, world, rank, max(3, args.warmup), max(3, args.steps // 20),
-                              layers=args.layers or 36, shard=args.shard)
+                              layers=args.layers or 36, shard=args.shard,
+                              layout=args.slot_layout)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:

@@ -213,7 +213,7 @@ def test_paged_and_unpaged_runs_leave_the_same_logical_kv(page_size):
         reposition_kv_layers(layer_pointer_table(k_pools), layer_pointer_table(v_pools),
                              k_pools[0], v_pools[0], res.transition_source,
                              res.transition_destination, res.transition_pairs, cache,
-                             count_device=res.transition_count)
+                             count_device=res.transition_count, page_size=ps)
         torch.cuda.synchronize()
         ao = res.active_offsets.cpu().numpy()
         raw = res.raw_indices[: ao[-1]].cpu().numpy()

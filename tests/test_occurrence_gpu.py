@@ -156,7 +156,7 @@ def test_gather_kernel_at_scale(seg_dtype, out_dtype):
         expect = np.where(idx < 0, -1, flat[np.clip(idx, 0, max(total - 1, 0))] if total
                           else -1)
         checks.append((out, expect))
-    lit = rng.integers(-2**40, 2**40, size=300_000)
+    lit = rng.integers(-2**31, 2**31, size=300_000)  # literals are int32 values
     lit_out = torch.empty(len(lit), dtype=out_dtype, device=DEV)
     g.add(lit_out, lit, literal=True)
     checks.append((lit_out, lit))

@@ -235,8 +235,10 @@ def test_reposition_validation_errors():
     s = torch.zeros(1, dtype=torch.int32, device=dev)
     pairs = torch.zeros(1, 2, dtype=torch.int32, device=dev)
     cache = torch.zeros(4, 64, device=dev)
-    with pytest.raises(ValueError, match="page_size=1"):
-        reposition_kv_layers(ptrs, ptrs, k, k, s, s, pairs, cache, page_size=16)
+    for bad in (2, 12, 256):  # the paged Drop's page sizes are powers of two in [4, 128]
+        with pytest.raises(ValueError, match="page_size=1"):
+            reposition_kv_layers(ptrs, ptrs, k, k, s, s, pairs, cache, page_size=bad)
+    reposition_kv_layers(ptrs, ptrs, k, k, s, s, pairs, cache, page_size=16)  # token slots
     with pytest.raises(ValueError, match="int32 slot vectors"):
         reposition_kv_layers(ptrs, ptrs, k, k, s.long(), s, pairs, cache)
     with pytest.raises(ValueError, match="cos/sin cache"):
