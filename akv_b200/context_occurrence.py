@@ -115,12 +115,13 @@ class SlotGather:
     def _add(self, out, idx, segments=(), literal=False):
         """``add`` for an output this module allocated (contiguous, on the
         device, one element per index): the segments are still checked."""
-        idx = np.asarray(idx).reshape(-1)
-        m = len(idx)
-        segments = tuple(segments)
-        key = tuple(id(s) for s in segments)
+        if type(idx) is not np.ndarray or idx.ndim != 1:
+            idx = np.asarray(idx).reshape(-1)
+        m = idx.shape[0]
+        key = tuple(map(id, segments))
         info = self._segments.get(key)
         if info is None:
+            segments = tuple(segments)
             if len(segments) > _MAX_SEGMENTS or (not literal and not segments and m):
                 raise ValueError("a slot gather reads one to four segments")
             for s in segments:
@@ -271,10 +272,10 @@ class _AdvancePlan:
             visible_until=_host(visible_until, np.int32))
         inp = _AdvanceIn(n, start, end, count, n_old, n_query, n_extra, n_copy,
                          *[None if a is None else _addr(a) for a in arrays.values()])
-        occ = np.empty(count, np.int64)
-        copy_src, copy_dst = np.empty(n_copy, np.int64), np.empty(n_copy, np.int64)
-        retained, retired = np.empty(total, np.int64), np.empty(total, np.int64)
-        unused_swa = np.empty(n_copy, np.int64)
+        occ = np.empty(count, np.int32)
+        copy_src, copy_dst = np.empty(n_copy, np.int32), np.empty(n_copy, np.int32)
+        retained, retired = np.empty(total, np.int32), np.empty(total, np.int32)
+        unused_swa = np.empty(n_copy, np.int32)
         canon_rows, term_rows = np.empty(end, np.int64), np.empty(end, np.int64)
         positions = np.empty(end, np.int32)
         owned_next = np.empty(total, np.uint8)
@@ -300,7 +301,7 @@ class _AdvancePlan:
         self.dtype, self.device = query_slots.dtype, query_slots.device
         self.occurrences = np.maximum(occ, 0, out=occ)
         self.copy_src, self.copy_dst = copy_src, copy_dst
-        self.pairs = _host(plan.copy_position_pairs, np.int64).reshape(-1)
+        self.pairs = _host(plan.copy_position_pairs, np.int32).reshape(-1)
         self.retained, self.retired = retained[:k], retired[:r]
         self.unused_swa = unused_swa[: out.n_unused_swa]
         self.successor = (torch.from_numpy(owned_next[:k].view(np.bool_)),

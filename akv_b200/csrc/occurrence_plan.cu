@@ -71,7 +71,7 @@ extern "C" int akv_occurrence_advance_indices(const akv_advance_in* in, akv_adva
   const int64_t n_old = in->n_old, n_query = in->n_query, n_extra = in->n_extra;
   const int64_t total = n_old + n_query + n_extra;
   if (n < 0 || start < 0 || start > end || end > n || count < 0 || n_old < 0 ||
-      n_query != end - start || n_extra < 0 || in->n_copy < 0)
+      n_query != end - start || n_extra < 0 || in->n_copy < 0 || total > INT32_MAX)
     return AKV_ERR_INVALID;
   const Owner owner{in, n};
   const int64_t row_limit = total;
@@ -84,12 +84,12 @@ extern "C" int akv_occurrence_advance_indices(const akv_advance_in* in, akv_adva
       row = owner(r);
       if (row < 0 || row >= row_limit) return AKV_ERR_OCC_MISSING_SOURCE;
     }
-    out->occurrence_rows[o] = row;
+    out->occurrence_rows[o] = (int32_t)row;
   }
   for (int64_t i = 0; i < n_extra; ++i) {
     const int64_t o = in->allocated[i];
     if (o < 0 || o >= count) return AKV_ERR_INVALID;
-    out->occurrence_rows[o] = n_old + n_query + i;
+    out->occurrence_rows[o] = (int32_t)(n_old + n_query + i);
   }
   // 2. copies
   for (int64_t j = 0; j < in->n_copy; ++j) {
@@ -97,7 +97,7 @@ extern "C" int akv_occurrence_advance_indices(const akv_advance_in* in, akv_adva
     if (src < 0 || src >= row_limit) return AKV_ERR_OCC_MISSING_COPY_SOURCE;
     const int64_t o = in->copy_occurrences[j];
     if (o < 0 || o >= count) return AKV_ERR_INVALID;
-    out->copy_source_rows[j] = src;
+    out->copy_source_rows[j] = (int32_t)src;
     out->copy_destination_rows[j] = out->occurrence_rows[o];
   }
   // 3. SWA residency
@@ -115,7 +115,7 @@ extern "C" int akv_occurrence_advance_indices(const akv_advance_in* in, akv_adva
     }
     for (int64_t j = 0; j < in->n_copy; ++j) {
       const int64_t d = out->copy_destination_rows[j];
-      if (!swa[d]) out->unused_swa[out->n_unused_swa++] = d;
+      if (!swa[d]) out->unused_swa[out->n_unused_swa++] = (int32_t)d;
     }
   }
   // 4. tokens of the successor
@@ -154,12 +154,12 @@ extern "C" int akv_occurrence_advance_indices(const akv_advance_in* in, akv_adva
     const bool owned = row < n_old ? in->owned[row] != 0 : true;
     if (rank[row] == 0) {
       rank[row] = kept;
-      out->retained[kept] = row;
+      out->retained[kept] = (int32_t)row;
       out->next_owned[kept] = owned;
       if (out->next_swa && in->swa_resident) out->next_swa[kept] = swa[row];
       ++kept;
     } else if (owned) {
-      out->retired[retired] = row;
+      out->retired[retired] = (int32_t)row;
       if (out->retired_swa && in->swa_resident) out->retired_swa[retired] = swa[row];
       ++retired;
     }

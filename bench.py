@@ -1473,8 +1473,10 @@ def bench_occurrence(dev, world, rank, warmup, steps, seed=0, requests=16, prefi
         keep = np.sort(rng.choice(total, total - copies, replace=False))
         release = np.setdiff1d(np.arange(total), keep)
         pairs = rng.integers(0, 10**5, 2 * copies)
-        reqs.append(dict(seg=(old, q, e), occ=occ, src=src, dst=dst, keep=keep,
-                         release=release, pairs=pairs))
+        # int32 row vectors, as the host derivation of advance returns them
+        reqs.append(dict(seg=(old, q, e), occ=occ.astype(np.int32), src=src.astype(np.int32),
+                         dst=dst.astype(np.int32), keep=keep.astype(np.int32),
+                         release=release.astype(np.int32), pairs=pairs.astype(np.int32)))
     n_slots = sum(len(r["occ"]) for r in reqs)
     n_copy = requests * copies
     out_slots = torch.empty(n_slots, dtype=torch.int64, device=dev)

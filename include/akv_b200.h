@@ -546,8 +546,9 @@ int akv_active_slots_batch(const int64_t* meta, const int64_t* out_offsets, cons
  * ownership index of one prefill forward of one request, computed on the
  * CPU (no device memory is touched).  All pointers are HOST memory.
  *
- * Rows index all = state slots ++ query slots ++ extra slots.  Outputs:
- * occurrence_rows[count] (-1 = unbound), copy_source_rows /
+ * Rows index all = state slots ++ query slots ++ extra slots (fewer than
+ * 2^31 rows, else AKV_ERR_INVALID).  Outputs (int32 row vectors, ready to be
+ * akv_gather_slots indices): occurrence_rows[count] (-1 = unbound), copy_source_rows /
  * copy_destination_rows [n_copy], retained / retired (ascending rows; room
  * for n_old + n_query + n_extra each) with their counts, unused_swa (room
  * for n_copy), the successor's canonical / terminal rows and positions
@@ -581,12 +582,12 @@ typedef struct {
 } akv_advance_in;
 
 typedef struct {
-  int64_t* occurrence_rows;
-  int64_t* copy_source_rows;
-  int64_t* copy_destination_rows;
-  int64_t* retained;
-  int64_t* retired;
-  int64_t* unused_swa;
+  int32_t* occurrence_rows; /* rows are below 2^31: n_old + n_query + n_extra must be */
+  int32_t* copy_source_rows;
+  int32_t* copy_destination_rows;
+  int32_t* retained;
+  int32_t* retired;
+  int32_t* unused_swa;
   int64_t* next_canonical;
   int64_t* next_terminal;
   int32_t* next_positions;
