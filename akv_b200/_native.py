@@ -20,6 +20,7 @@ AKV_F16, AKV_BF16, AKV_F32 = 0, 1, 2
 GATHER_OUT64, GATHER_LITERAL, GATHER_SEG64 = 1, 2, 4
 DROP_RING_UNDERFLOW, DROP_RING_OVERFLOW, DROP_BAD_RANGE, DROP_NO_ACTIVE = 1, 2, 4, 8
 DROP_BAD_PAGE = 16
+REPOSITION_BULK_V = 1
 
 DTYPE_CODE = {torch.float16: AKV_F16, torch.bfloat16: AKV_BF16, torch.float32: AKV_F32}
 
@@ -56,6 +57,10 @@ SIGNATURES = {
     "akv_reposition_kv_layers": [
         _P, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64,
         _P, _P, _I32, _I64, _I32, _I32, _I64, _I64, _P, _P,
+    ],
+    "akv_reposition_kv_layers_ex": [
+        _P, _P, _I32, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _I64, _I64,
+        _P, _P, _I32, _I64, _I32, _I32, _I64, _I64, _P, _I32, _P,
     ],
     "akv_reposition_divide": [_P, _P, _P, _I64, _I32, _P],
     "akv_drop_compact_tile_tokens": [],

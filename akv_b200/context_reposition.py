@@ -16,7 +16,7 @@ the capacity.  Callers that do not pass it get the reference's behaviour.
 Slots are bounded by the exemplar pool's slot count and positions by the
 cos/sin table's length: a transition outside them is skipped instead of
 touching memory outside the pools, and ``error_flag`` (optional int32 CUDA
-tensor) is set to 1.
+tensor) gets bit 1 (bit 2: a bulk-copy wait of ``bulk_copy_v`` ran out).
 
 A transition whose source equals its destination is rotated in place; the
 reference's contract (fresh destinations disjoint from every source) is
@@ -46,6 +46,7 @@ def reposition_kv_layers(
     rotary_dim: int | None = None,
     count_device: torch.Tensor | None = None,
     error_flag: torch.Tensor | None = None,
+    bulk_copy_v: bool = False,
 ) -> None:
     """Rotate K and copy V across native per-layer pools in one GPU launch.
 
@@ -62,6 +63,12 @@ def reposition_kv_layers(
     every case, so the paged pools of ``DropCompactor(page_size=...)``
     (powers of two from 4 to 128) are accepted as well; any other value
     raises the reference's error.
+
+    ``bulk_copy_v``: move the V rows of copy transitions with TMA bulk
+    copies in a second kernel (``AKV_REPOSITION_BULK_V``).  Faster when
+    copies are a minority of the list, as in a Drop's mixed list of in-place
+    rotations and copy-on-write; slower when every transition is a copy.
+    Results are identical either way.
     """
     if page_size != 1 and (page_size < 4 or page_size > 128 or page_size & (page_size - 1)):
         raise ValueError("Context Reposition requires page_size=1")
@@ -135,7 +142,7 @@ def reposition_kv_layers(
         raise ValueError("count_device must be an int32 tensor on the KV device")
     if count == 0 or len(k_data_ptrs) == 0:
         return
-    status = _native.lib.akv_reposition_kv_layers(
+    status = _native.lib.akv_reposition_kv_layers_ex(
         _native.ptr(k_data_ptrs),
         _native.ptr(v_data_ptrs),
         len(k_data_ptrs),
@@ -161,6 +168,7 @@ def reposition_kv_layers(
         k_layout.shape[0],
         cos_sin_cache.shape[0],
         _native.ptr(error_flag),
+        _native.REPOSITION_BULK_V if bulk_copy_v else 0,
         _native.stream_of(k_layout.device),
     )
     _native.check(status, "reposition_kv_layers")

@@ -65,6 +65,7 @@ struct RepositionParams {
   long long max_position;  // 0 = unchecked
   int* error_flag;
   float one;  // 1.0f, passed at run time (see the packed sums in rotate)
+  int v_moved;  // copy-on-write V rows are moved by reposition_v_move_kernel
 };
 
 // V consecutive elements of T, moved with one 16-byte access when
@@ -567,7 +568,7 @@ reposition_kernel(const RepositionParams p) {
     const long long pn = __ldg(p.pairs + tok * p.pstride + 1);
     if ((p.num_slots > 0 && (src < 0 || dst < 0 || src >= p.num_slots || dst >= p.num_slots)) ||
         (p.max_position > 0 && (po < 0 || pn < 0 || po >= p.max_position || pn >= p.max_position))) {
-      if (p.error_flag != nullptr) *p.error_flag = 1;
+      if (p.error_flag != nullptr) atomicOr(p.error_flag, 1);
       continue;
     }
     g.same = po == pn;
@@ -583,7 +584,9 @@ reposition_kernel(const RepositionParams p) {
     g.vd = dst * p.v_ss + head * p.v_sh;
 
     if constexpr (kVector) {
-      if (all_vec && g.in_place) {
+      // In place, or a copy whose V rows the move kernel carries: only the
+      // K pair of the unit moves (rotated into the destination row).
+      if (all_vec && (g.in_place || (p.v_moved && g.tail_vecs == 0))) {
         unit_pipelined<T, C, NEOX, V, 8, 2>(p, s_k, s_v, stage, g, po, pn, j, l0, l1);
         continue;
       }
@@ -596,6 +599,156 @@ reposition_kernel(const RepositionParams p) {
     load_trig<C, V>(p, po, pn, j, tr);
     unit_direct<T, NEOX, V>(p, s_k, s_v, s_vec, g, tr, l0, l1);
   }
+}
+
+// ---------------------------------------------------------------------------
+// V rows of copy-on-write transitions, moved by the TMA engine.
+//
+// For a copy (source != destination) the whole V row of a token over the
+// local heads -- num_heads * head_dim contiguous elements when heads are
+// contiguous in the [slot, head, dim] pool -- moves unchanged.  Here one
+// thread per warp (a "mover") streams such rows through a ring of
+// kMoveSlots row buffers in its own shared memory: a 1-D bulk copy global ->
+// shared completes on the slot's mbarrier (bounded wait), then a 1-D bulk
+// copy shared -> global writes the destination row, and a slot is refilled
+// only after the store that read it has finished reading
+// (cp.async.bulk.wait_group.read).  No register or thread touches the data.
+// All addresses are this GPU's own pools; no cluster multicast.
+// Work: mover m takes transitions m, m + M, m + 2M, ... (M movers in the
+// grid), each with all its layers, so that copies clustered in the list
+// (a request's shared prefix) spread over every mover; in-place, skipped
+// and out-of-range transitions are passed over whole (the main kernel
+// reports the latter).
+constexpr int kMoveWarps = 8;
+constexpr int kMoveSlots = 8;
+constexpr int kMoveAhead = kMoveSlots - 2;  // loads in flight; the store two rows back is read
+constexpr int kMaxMoveRow = 2048;           // bytes: 8 heads x 128 dims x 2 B
+constexpr unsigned long long kMoveWaitNs = 100000000ull;  // 100 ms per row
+
+__device__ __forceinline__ bool move_bar_wait(uint32_t bar, uint32_t parity) {
+  auto done = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (done()) return true;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    if (done()) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > kMoveWaitNs) return false;
+  }
+}
+
+__global__ void __launch_bounds__(kMoveWarps * 32) reposition_v_move_kernel(
+    const RepositionParams p, int row_bytes) {
+  extern __shared__ __align__(128) unsigned char move_smem[];
+  __shared__ __align__(8) unsigned long long move_bars[kMoveWarps][kMoveSlots];
+  pdl_wait();  // transitions and their count may come from the kernel before
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) != 0) return;  // one thread per mover
+  long long count = p.count;
+  if (p.count_dev != nullptr) {
+    const long long c = *p.count_dev;
+    count = c < count ? c : count;
+  }
+  const long long movers = (long long)gridDim.x * kMoveWarps;
+  long long tr = (long long)blockIdx.x * kMoveWarps + warp;  // this mover's current transition
+  int layer = 0;                                             // its next layer
+  long long tr_src = 0, tr_dst = 0;
+
+  const uint32_t slots = (uint32_t)__cvta_generic_to_shared(move_smem) +
+                         (uint32_t)(warp * kMoveSlots * row_bytes);
+  const uint32_t bars = (uint32_t)__cvta_generic_to_shared(&move_bars[warp][0]);
+  for (int s = 0; s < kMoveSlots; ++s)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bars + 8 * s));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+  unsigned long long dst_of[kMoveSlots];
+  uint32_t parity = 0;  // bit s: parity of slot s's next completion
+  long long issued = 0, done = 0;
+  // The next row of this mover: source and destination addresses.
+  auto next_row = [&](unsigned long long& src, unsigned long long& dst) -> bool {
+    while (tr < count) {
+      if (layer == 0) {  // a new transition: is it a copy to move?
+        tr_src = __ldg(p.src + tr);
+        tr_dst = __ldg(p.dst + tr);
+        const bool skip =
+            tr_src == tr_dst || (p.skip_unmapped && (tr_src <= 0 || tr_dst <= 0)) ||
+            (p.num_slots > 0 &&
+             (tr_src < 0 || tr_dst < 0 || tr_src >= p.num_slots || tr_dst >= p.num_slots));
+        if (skip) {
+          tr += movers;
+          continue;
+        }
+      }
+      const unsigned long long vb = __ldg(p.v_ptrs + layer);
+      src = vb + (unsigned long long)(tr_src * p.v_ss) * 2ull;
+      dst = vb + (unsigned long long)(tr_dst * p.v_ss) * 2ull;
+      if (++layer == p.n_layers) {
+        layer = 0;
+        tr += movers;
+      }
+      if (((src | dst) & 15ull) == 0) return true;  // misaligned layer: the main kernel moves it
+    }
+    return false;
+  };
+  auto load = [&](unsigned long long src, unsigned long long dst) {
+    const int s = (int)(issued % kMoveSlots);
+    const uint32_t bar = bars + 8 * s, buf = slots + (uint32_t)(s * row_bytes);
+    dst_of[s] = dst;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                 "r"(row_bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+        "[%3];" ::"r"(buf),
+        "l"(src), "r"(row_bytes), "r"(bar)
+        : "memory");
+    ++issued;
+  };
+  unsigned long long src, dst;
+  while (issued < kMoveAhead && next_row(src, dst)) load(src, dst);
+  bool failed = false;
+  while (done < issued) {
+    const int s = (int)(done % kMoveSlots);
+    if (!move_bar_wait(bars + 8 * s, (parity >> s) & 1u)) {
+      failed = true;
+      break;
+    }
+    parity ^= 1u << s;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_of[s]),
+                 "r"(slots + (uint32_t)(s * row_bytes)), "r"(row_bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    ++done;
+    if (next_row(src, dst)) {
+      // The slot to fill last held row issued - kMoveSlots, whose store is
+      // older than the newest kMoveSlots - kMoveAhead stores.
+      asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kMoveSlots - kMoveAhead) : "memory");
+      load(src, dst);
+    }
+  }
+  if (failed) {
+    if (p.error_flag != nullptr) atomicOr(p.error_flag, 2);
+    // The loads still in flight land in this CTA's shared memory: wait for
+    // each (bounded) before the CTA leaves.
+    for (long long k = done; k < issued; ++k) {
+      const int s = (int)(k % kMoveSlots);
+      if (move_bar_wait(bars + 8 * s, (parity >> s) & 1u)) parity ^= 1u << s;
+    }
+  }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 template <typename T, typename C, bool NEOX, int V>
@@ -618,6 +771,24 @@ int launch(const RepositionParams& p, cudaStream_t stream) {
   const long long spans = ((units + 31) / 32 * p.n_layers + kMinSpan - 1) / kMinSpan;
   const long long blocks = (spans + kThreads / 32 - 1) / (kThreads / 32);
   const int grid = persistent_grid(per_sm, blocks);
+  if (p.v_moved) {
+    // Copy-on-write V rows by bulk copies, then the K rotation; both are
+    // programmatic dependent launches (each waits for its predecessor).
+    const int row_bytes = p.num_heads * p.head_dim * (int)sizeof(T);
+    const int move_smem = kMoveWarps * kMoveSlots * row_bytes;
+    if (cudaFuncSetAttribute(reposition_v_move_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, move_smem) != cudaSuccess)
+      return AKV_ERR_CUDA;
+    int move_per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&move_per_sm, reposition_v_move_kernel,
+                                                      kMoveWarps * 32, move_smem) != cudaSuccess ||
+        move_per_sm < 1)
+      move_per_sm = 1;
+    const int move_grid = persistent_grid(move_per_sm, (p.count + kMoveWarps - 1) / kMoveWarps);
+    if (launch_pdl(reposition_v_move_kernel, move_grid, kMoveWarps * 32, move_smem, stream, p,
+                   row_bytes) != cudaSuccess)
+      return AKV_ERR_CUDA;
+  }
   if (launch_pdl(kernel, grid, kThreads, smem, stream, p) != cudaSuccess) return AKV_ERR_CUDA;
   return launch_status();
 }
@@ -664,7 +835,7 @@ __global__ void divide_kernel(const float* n, const float* s, float* q, int64_t 
 }  // namespace
 }  // namespace akv
 
-extern "C" int akv_reposition_kv_layers(
+extern "C" int akv_reposition_kv_layers_ex(
     const void* k_data_ptrs, const void* v_data_ptrs, int32_t n_layers, int32_t kv_dtype,
     int32_t num_heads, int32_t head_dim, int32_t rotary_dim, int64_t k_stride_slot,
     int64_t k_stride_head, int64_t v_stride_slot, int64_t v_stride_head,
@@ -672,9 +843,10 @@ extern "C" int akv_reposition_kv_layers(
     const int32_t* position_pairs, int64_t position_stride, int64_t count,
     const int32_t* count_device, const void* cos_sin_cache, int32_t cache_dtype,
     int64_t cache_stride, int32_t is_neox_style, int32_t skip_unmapped, int64_t num_slots,
-    int64_t max_position, int32_t* error_flag, void* stream) {
+    int64_t max_position, int32_t* error_flag, int32_t options, void* stream) {
   AKV_NVTX_RANGE("akv_reposition_kv_layers");
   using namespace akv;
+  if (options & ~AKV_REPOSITION_BULK_V) return AKV_ERR_INVALID;
   if (count < 0 || n_layers < 0 || n_layers > kMaxLayers || num_heads <= 0 || head_dim <= 0 ||
       rotary_dim <= 0 || rotary_dim > head_dim || (rotary_dim & 1) || position_stride < 2)
     return AKV_ERR_INVALID;
@@ -707,6 +879,7 @@ extern "C" int akv_reposition_kv_layers(
   p.max_position = max_position;
   p.error_flag = error_flag;
   p.one = 1.0f;
+  p.v_moved = 0;
   const bool cache_rows = cache_dtype == AKV_F32 &&
                           (reinterpret_cast<uintptr_t>(cos_sin_cache) & 15) == 0 &&
                           cache_stride % 4 == 0 && p.half % 4 == 0;
@@ -721,12 +894,37 @@ extern "C" int akv_reposition_kv_layers(
                    (v_stride_slot % V == 0) && (v_stride_head % V == 0);
   const bool neox = is_neox_style != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // With AKV_REPOSITION_BULK_V, copy-on-write V rows go through the
+  // bulk-copy move kernel when a token's V row over the local heads is one
+  // contiguous run of 16-byte multiples and K has no tail to copy
+  // (rotary_dim == head_dim); otherwise the main kernel moves them.
+  const long long v_row = (long long)num_heads * head_dim * esize;
+  p.v_moved = (options & AKV_REPOSITION_BULK_V) && vec && esize == 2 &&
+              rotary_dim == head_dim && v_stride_head == head_dim && v_row % 16 == 0 &&
+              v_row <= kMaxMoveRow && v_stride_slot % 8 == 0;
   switch (kv_dtype) {
     case AKV_F32: return dispatch_cache<float>(p, cache_dtype, cache_rows, neox, vec, s);
     case AKV_BF16: return dispatch_cache<__nv_bfloat16>(p, cache_dtype, cache_rows, neox, vec, s);
     case AKV_F16: return dispatch_cache<__half>(p, cache_dtype, cache_rows, neox, vec, s);
   }
   return AKV_ERR_INVALID;
+}
+
+extern "C" int akv_reposition_kv_layers(
+    const void* k_data_ptrs, const void* v_data_ptrs, int32_t n_layers, int32_t kv_dtype,
+    int32_t num_heads, int32_t head_dim, int32_t rotary_dim, int64_t k_stride_slot,
+    int64_t k_stride_head, int64_t v_stride_slot, int64_t v_stride_head,
+    const int32_t* source_slots, const int32_t* destination_slots,
+    const int32_t* position_pairs, int64_t position_stride, int64_t count,
+    const int32_t* count_device, const void* cos_sin_cache, int32_t cache_dtype,
+    int64_t cache_stride, int32_t is_neox_style, int32_t skip_unmapped, int64_t num_slots,
+    int64_t max_position, int32_t* error_flag, void* stream) {
+  return akv_reposition_kv_layers_ex(
+      k_data_ptrs, v_data_ptrs, n_layers, kv_dtype, num_heads, head_dim, rotary_dim,
+      k_stride_slot, k_stride_head, v_stride_slot, v_stride_head, source_slots,
+      destination_slots, position_pairs, position_stride, count, count_device, cos_sin_cache,
+      cache_dtype, cache_stride, is_neox_style, skip_unmapped, num_slots, max_position,
+      error_flag, 0, stream);
 }
 
 extern "C" int akv_reposition_divide(const float* numerators, const float* denominators,

@@ -869,7 +869,8 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
     One step = restore the rows and the ring head that the previous step's
     copy-on-write changed (one 8 MB device copy of req_to_token and one of
     the 16-byte ring state; the bytes are not counted) + the Drop (three
-    launches) + one reposition launch over all 36 layers.  Algorithmic
+    launches) + the reposition over all 36 layers (``bulk_copy_v``: the V
+    rows of the copies by TMA bulk copies in one launch, K in another).  Algorithmic
     bytes: per (transition, layer, local head) 2 * rotary_dim * 2 B in place
     and 4 * head_dim * 2 B for copy-on-write (K read + write, V read +
     write); Drop: T + 4 T + 8 A + 4 per freed unit + 12 per transition +
@@ -933,7 +934,8 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                 ev[i][1].record(stream)
             reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
                                  res.transition_destination, res.transition_pairs, cache,
-                                 count_device=res.transition_count, page_size=ps)
+                                 count_device=res.transition_count, page_size=ps,
+                                 bulk_copy_v=True)
             if i is not None:
                 ev[i][2].record(stream)
             return res
@@ -974,19 +976,20 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
         # slots, in-place rotates the rotary part only.
         split = {}
         cow_mask = src != res.transition_destination[:n]
-        for kind, sel in (("copy_on_write", cow_mask), ("in_place", ~cow_mask)):
+        for kind, sel, bulk in (("copy_on_write", cow_mask, True), ("in_place", ~cow_mask, True),
+                                ("copy_on_write_one_pass", cow_mask, False)):
             s_src = src[sel].contiguous()
             s_dst = res.transition_destination[:n][sel].contiguous()
             s_pairs = res.transition_pairs[:n][sel].contiguous()
             cnt = int(s_src.numel())
-            per = (4 if kind == "copy_on_write" else 2) * dim * 2 * layers * heads
+            per = (2 if kind == "in_place" else 4) * dim * 2 * layers * heads
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(steps)]
             for a0, a1 in [(None, None)] * 2 + evs:
                 if a0 is not None:
                     a0.record(stream)
                 reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], s_src, s_dst,
-                                     s_pairs, cache)
+                                     s_pairs, cache, bulk_copy_v=bulk)
                 if a1 is not None:
                     a1.record(stream)
             torch.cuda.synchronize()
@@ -995,7 +998,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                            "algorithmic_bytes": cnt * per,
                            "achieved": round(cnt * per / (k_ms / 1e3) / 1e9, 1),
                            "frac": round(cnt * per / (k_ms / 1e3) / 1e9 / peak, 4)}
-            if ref is not None and world == 1 and cnt:
+            if ref is not None and world == 1 and cnt and kind != "copy_on_write_one_pass":
                 split[kind]["triton_reference"] = triton_versus_ours(
                     ref, k_ptrs, v_ptrs, k_pools[0], v_pools[0], s_src, s_dst, s_pairs, cache,
                     3, stream, cnt * per)
@@ -1013,7 +1016,8 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                           shared_prefix=prog.shared_prefix, page_size=ps)
             reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], r2.transition_source,
                                  r2.transition_destination, r2.transition_pairs, cache,
-                                 count_device=r2.transition_count)
+                                 count_device=r2.transition_count, page_size=ps,
+                                 bulk_copy_v=True)
             view[:kept].copy_(r2.raw_indices[:kept], non_blocking=True)
             view[kept:].copy_(r2.active_positions[:kept], non_blocking=True)
             e1.record(stream)
@@ -1046,7 +1050,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                          "traffic": ncu_traffic("c3", rep_bytes) if world == 1 else None,
                          "traffic_source": "profiles/reposition_c3.md (4-request cut, "
                                            "traffic / algorithmic ratio)"},
-            "gpu_launches_per_step": 4,
+            "gpu_launches_per_step": 5,
             "clocks": clock_info,
         }
         if cpu and rank == 0 and world == 1:

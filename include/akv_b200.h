@@ -89,6 +89,34 @@ int akv_reposition_kv_layers(
     int64_t max_position, int32_t* error_flag, void* stream);
 
 /*
+ * akv_reposition_kv_layers with options; akv_reposition_kv_layers is this
+ * with options 0.  No reference counterpart.
+ *
+ * AKV_REPOSITION_BULK_V: the V rows of copy transitions (source !=
+ * destination) are moved by a second kernel that streams whole token rows
+ * through shared memory with TMA bulk copies (cp.async.bulk global ->
+ * shared on an mbarrier, then shared -> global), and the reposition kernel
+ * moves only their K rows.  Used when the token's V row over the local
+ * heads is contiguous (v_stride_head == head_dim), 16-byte aligned, at most
+ * 2 KiB, and rotary_dim == head_dim; otherwise the option is ignored.  It
+ * pays when copies are a minority of the list (a Drop's mixed list of
+ * in-place rotations and copy-on-write: c3 step 6 % faster) and costs when
+ * every transition is a copy (two passes instead of one: about 11 % slower),
+ * so the caller chooses.  A bulk-copy wait that runs out (100 ms) sets bit 2
+ * of *error_flag.
+ */
+#define AKV_REPOSITION_BULK_V 1
+int akv_reposition_kv_layers_ex(
+    const void* k_data_ptrs, const void* v_data_ptrs, int32_t n_layers, int32_t kv_dtype,
+    int32_t num_heads, int32_t head_dim, int32_t rotary_dim, int64_t k_stride_slot,
+    int64_t k_stride_head, int64_t v_stride_slot, int64_t v_stride_head,
+    const int32_t* source_slots, const int32_t* destination_slots,
+    const int32_t* position_pairs, int64_t position_stride, int64_t count,
+    const int32_t* count_device, const void* cos_sin_cache, int32_t cache_dtype,
+    int64_t cache_stride, int32_t is_neox_style, int32_t skip_unmapped, int64_t num_slots,
+    int64_t max_position, int32_t* error_flag, int32_t options, void* stream);
+
+/*
  * The correctly rounded fp32 division the reposition kernel uses, exported
  * so a caller can check it against IEEE division on its own GPU: method 0
  * is IEEE division (__fdiv_rn, the reference's tl.div_rn), method 1 the

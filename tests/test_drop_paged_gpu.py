@@ -186,8 +186,9 @@ def _logical_pools(rng_seed, program, rows, n_slots, layers, heads, dim, dev):
     return k_pools, v_pools
 
 
+@pytest.mark.parametrize("bulk", [False, True])
 @pytest.mark.parametrize("page_size", [16])
-def test_paged_and_unpaged_runs_leave_the_same_logical_kv(page_size):
+def test_paged_and_unpaged_runs_leave_the_same_logical_kv(page_size, bulk):
     from akv_b200 import workloads
     from akv_b200.context_reposition import layer_pointer_table, reposition_kv_layers
     from akv_b200.rope import yarn_cos_sin_cache
@@ -213,7 +214,8 @@ def test_paged_and_unpaged_runs_leave_the_same_logical_kv(page_size):
         reposition_kv_layers(layer_pointer_table(k_pools), layer_pointer_table(v_pools),
                              k_pools[0], v_pools[0], res.transition_source,
                              res.transition_destination, res.transition_pairs, cache,
-                             count_device=res.transition_count, page_size=ps)
+                             count_device=res.transition_count, page_size=ps,
+                             bulk_copy_v=bulk)
         torch.cuda.synchronize()
         ao = res.active_offsets.cpu().numpy()
         raw = res.raw_indices[: ao[-1]].cpu().numpy()

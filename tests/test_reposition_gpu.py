@@ -93,7 +93,9 @@ def test_reposition_matches_reference_golden(case, storage):
 
 
 def _random_case(rng, *, dtype, layers, heads, dim, rot, neox, n, slots, in_place, pad=0,
-                 cache_dtype=torch.float32, max_pos=4096, yarn=False):
+                 cache_dtype=torch.float32, max_pos=4096, yarn=False, bulk=False):
+    """``in_place``: True (every transition in place), False (every one a
+    copy) or "mixed" (every third in place, the rest copies)."""
     from oracle import oracle
     from akv_b200.rope import rope_cos_sin_cache, yarn_cos_sin_cache
 
@@ -103,7 +105,9 @@ def _random_case(rng, *, dtype, layers, heads, dim, rot, neox, n, slots, in_plac
     v_full = [torch.randn(slots, heads, width).to(dtype) for _ in range(layers)]
     perm = rng.permutation(np.arange(1, slots))
     src = perm[:n].astype(np.int32)
-    dst = src.copy() if in_place else perm[n: 2 * n].astype(np.int32)
+    dst = src.copy() if in_place is True else perm[n: 2 * n].astype(np.int32)
+    if in_place == "mixed":
+        dst[::3] = src[::3]
     old = rng.integers(0, max_pos, size=n)
     new = rng.integers(0, max_pos, size=n)
     new[::9] = old[::9]
@@ -134,7 +138,7 @@ def _random_case(rng, *, dtype, layers, heads, dim, rot, neox, n, slots, in_plac
     vs = [v[..., :dim] for v in dv]
     reposition_kv_layers(table(ks), table(vs), ks[0], vs[0], torch.from_numpy(src).to(dev),
                          torch.from_numpy(dst).to(dev), torch.from_numpy(pairs).to(dev),
-                         cache.to(dev), is_neox_style=neox, rotary_dim=rot)
+                         cache.to(dev), is_neox_style=neox, rotary_dim=rot, bulk_copy_v=bulk)
     torch.cuda.synchronize()
     for layer in range(layers):
         np.testing.assert_array_equal(host(dk[layer].cpu()), hk[layer])
@@ -167,6 +171,63 @@ def test_reposition_shapes_match_oracle(heads, dim, rot, pad, cache_dtype, layer
                      cache_dtype=cache_dtype)
 
 
+@pytest.mark.parametrize(
+    "dtype,heads,dim,rot,pad,neox,in_place",
+    [(torch.bfloat16, 8, 64, 64, 0, True, "mixed"), (torch.bfloat16, 8, 64, 64, 0, False, False),
+     (torch.float16, 4, 128, 128, 0, True, "mixed"), (torch.bfloat16, 1, 64, 64, 0, True, False),
+     (torch.bfloat16, 2, 128, 128, 0, True, "mixed"), (torch.bfloat16, 8, 128, 128, 0, True, True),
+     # the option does not apply (the main kernel moves V): padded heads,
+     # partial rotary, fp32 storage
+     (torch.bfloat16, 8, 64, 64, 8, True, "mixed"), (torch.bfloat16, 4, 128, 64, 0, True, False),
+     (torch.float32, 4, 64, 64, 0, True, "mixed")],
+)
+def test_reposition_bulk_v_move_matches_oracle(dtype, heads, dim, rot, pad, neox, in_place):
+    """AKV_REPOSITION_BULK_V (copy V rows moved by TMA bulk copies in a
+    second kernel): bit for bit the oracle's result, as without it."""
+    rng = np.random.default_rng(heads * 100 + dim + pad)
+    _random_case(rng, dtype=dtype, layers=7, heads=heads, dim=dim, rot=rot, neox=neox, n=700,
+                 slots=2000, in_place=in_place, pad=pad, yarn=True, bulk=True)
+
+
+def test_reposition_bulk_v_move_with_device_count_and_skips():
+    """Bulk V move over a device-counted prefix of the list, with
+    skip_unmapped rows and an out-of-range destination."""
+    from oracle import oracle
+    from akv_b200.rope import rope_cos_sin_cache
+
+    reposition_kv_layers, table = _rp()
+    rng = np.random.default_rng(21)
+    dev = torch.device("cuda")
+    slots, heads, dim, layers, n = 1500, 8, 64, 4, 600
+    ks = [torch.randn(slots, heads, dim).to(torch.bfloat16) for _ in range(layers)]
+    vs = [torch.randn(slots, heads, dim).to(torch.bfloat16) for _ in range(layers)]
+    perm = rng.permutation(np.arange(1, slots))
+    src, dst = perm[:n].astype(np.int32), perm[n: 2 * n].astype(np.int32)
+    dst[1::4] = src[1::4]
+    src[5] = 0  # skip_unmapped: slot 0 is not mapped
+    dst[9] = slots + 7  # outside the pool: skipped and flagged
+    pairs = rng.integers(0, 3000, size=(n, 2)).astype(np.int32)
+    cache = rope_cos_sin_cache(3000, dim, 10000.0)
+    used = 450
+    keep = np.arange(used)
+    keep = keep[(keep != 5) & (keep != 9)]
+    host = lambda t: t.view(torch.int16).numpy().view(np.uint16).copy()  # noqa: E731
+    hk, hv = [host(k) for k in ks], [host(v) for v in vs]
+    oracle.reposition(hk, hv, src[keep], dst[keep], pairs[keep], cache.numpy(), bf16=True)
+    dk, dv = [k.to(dev) for k in ks], [v.to(dev) for v in vs]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    cnt = torch.tensor([used], dtype=torch.int32, device=dev)
+    reposition_kv_layers(table(dk), table(dv), dk[0], dv[0], torch.from_numpy(src).to(dev),
+                         torch.from_numpy(dst).to(dev), torch.from_numpy(pairs).to(dev),
+                         cache.to(dev), skip_unmapped=True, count_device=cnt, error_flag=err,
+                         bulk_copy_v=True)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+    for layer in range(layers):
+        np.testing.assert_array_equal(host(dk[layer].cpu()), hk[layer])
+        np.testing.assert_array_equal(host(dv[layer].cpu()), hv[layer])
+
+
 def test_reposition_misaligned_layer_matches_oracle():
     """A layer whose base address is not 16-byte aligned takes the element path."""
     from oracle import oracle
@@ -188,15 +249,17 @@ def test_reposition_misaligned_layer_matches_oracle():
     cache = rope_cos_sin_cache(1000, dim, 10000.0)
     host = [t.view(torch.int16).numpy().view(np.uint16).copy() for t in (k0, k1, v0, v1)]
     oracle.reposition(host[:2], host[2:], src, dst, pairs, cache.numpy(), bf16=True)
-    dbase = base.to(dev)
-    dk0 = dbase[4: 4 + slots * heads * dim].view(slots, heads, dim)
-    dk1, dv0, dv1 = k1.to(dev), v0.to(dev), v1.to(dev)
-    reposition_kv_layers(table([dk0, dk1]), table([dv0, dv1]), dk1, dv1,
-                         torch.from_numpy(src).to(dev), torch.from_numpy(dst).to(dev),
-                         torch.from_numpy(pairs).to(dev), cache.to(dev))
-    torch.cuda.synchronize()
-    for got, want in zip((dk0, dk1, dv0, dv1), host):
-        np.testing.assert_array_equal(got.cpu().view(torch.int16).numpy().view(np.uint16), want)
+    for bulk in (False, True):
+        dbase = base.to(dev)
+        dk0 = dbase[4: 4 + slots * heads * dim].view(slots, heads, dim)
+        dk1, dv0, dv1 = k1.to(dev), v0.to(dev), v1.to(dev)
+        reposition_kv_layers(table([dk0, dk1]), table([dv0, dv1]), dk1, dv1,
+                             torch.from_numpy(src).to(dev), torch.from_numpy(dst).to(dev),
+                             torch.from_numpy(pairs).to(dev), cache.to(dev), bulk_copy_v=bulk)
+        torch.cuda.synchronize()
+        for got, want in zip((dk0, dk1, dv0, dv1), host):
+            np.testing.assert_array_equal(got.cpu().view(torch.int16).numpy().view(np.uint16),
+                                          want)
 
 
 def test_reposition_count_device_and_bounds():
