@@ -198,37 +198,65 @@ __global__ void __launch_bounds__(kThreads) decode_indices_flat_kernel(const Ind
   }
 }
 
-__device__ __forceinline__ int64_t window_length(const Entry& e, int64_t length, int64_t window) {
-  if (e.raw_ids == nullptr) return length < window ? length : window;
-  const int64_t generated = length - e.active;
-  // The window is the inclusive distance q_pos - k_pos (context_page_table.py:19-20).
-  const int64_t lower = (int64_t)e.next_pos + generated - 1 - window;
-  int32_t lo = 0, hi = e.active;
-  while (lo < hi) {
-    const int32_t mid = (lo + hi) >> 1;
-    if ((int64_t)__ldg(e.positions + mid) < lower) lo = mid + 1;
-    else hi = mid;
+// Window length of one request computed by the eight lanes of a lane group
+// (lanes 8g .. 8g + 7 of a warp; every lane of the warp calls this, `has`
+// false for lanes without a request): each round the eight lanes probe
+// eight evenly spaced positions of the request's active range and keep the
+// ninth part that holds the first position at or above the window's lower
+// edge, so a 64K range takes six dependent loads instead of sixteen.  Every
+// lane of the group returns the length.
+__device__ __forceinline__ long long group_window_length(bool has, const Entry& e, long long seq,
+                                                         int64_t window) {
+  const int lane = threadIdx.x & 31, sub = threadIdx.x & 7, first_lane = lane & 24;
+  const unsigned group = 0xffu << first_lane;
+  long long lower = 0, generated = 0;
+  int32_t lo = 0, hi = 0;
+  if (has && e.raw_ids != nullptr) {
+    generated = seq - e.active;
+    // the window is the inclusive distance q_pos - k_pos (context_page_table.py:19-20)
+    lower = (long long)e.next_pos + generated - 1 - window;
+    hi = e.active;
   }
-  const int64_t skipped = lower - e.next_pos > 0 ? lower - e.next_pos : 0;
-  return (int64_t)e.active - lo + generated - skipped;
+  while (__any_sync(0xffffffffu, hi > lo)) {
+    int32_t probe = lo;
+    bool below = false;
+    if (hi > lo) {
+      probe = lo + (int32_t)(((long long)(hi - lo) * (sub + 1)) / 9);
+      below = (long long)__ldg(e.positions + probe) < lower;
+    }
+    const int c = __popc(__ballot_sync(0xffffffffu, below) & group);
+    const int32_t p_below = __shfl_sync(0xffffffffu, probe, first_lane + (c > 0 ? c - 1 : 0));
+    const int32_t p_above = __shfl_sync(0xffffffffu, probe, first_lane + (c < 8 ? c : 7));
+    if (hi > lo) {
+      if (c > 0) lo = p_below + 1;
+      if (c < 8) hi = p_above;
+    }
+  }
+  if (e.raw_ids == nullptr) return seq < window ? seq : window;
+  const long long skipped = lower - e.next_pos > 0 ? lower - e.next_pos : 0;
+  return (long long)e.active - lo + generated - skipped;
 }
 
+// The drop-in context_window_lengths: eight lanes per request.
 __global__ void __launch_bounds__(kThreads) window_lengths_kernel(
     const int64_t* registry, const void* row_ids, int row_ids_is64, const void* lengths,
     int lengths_is64, void* output, int output_is64, int64_t window, int batch) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= batch) return;
-  const Entry e = load_entry(registry, ld_index(row_ids, b, row_ids_is64));
-  st_index(output, b, output_is64, window_length(e, ld_index(lengths, b, lengths_is64), window));
+  const int b = (int)(((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3);
+  const bool has = b < batch;
+  Entry e{};
+  long long seq = 0;
+  if (has) {
+    seq = ld_index(lengths, b, lengths_is64);
+    e = load_entry(registry, ld_index(row_ids, b, row_ids_is64));
+  }
+  const long long len = group_window_length(has, e, seq, window);
+  if (has && (threadIdx.x & 7) == 0) st_index(output, b, output_is64, len);
 }
 
 // One block: lengths (windowed or not), their exclusive scan into kv_indptr,
 // and starts = seq_len - length.  Windowed lengths are found first, eight
-// lanes per request: each round the eight lanes probe eight evenly spaced
-// positions of the request's active range and keep the ninth part that
-// holds the first position at or above the window's lower edge, so a 64K
-// range takes six dependent loads instead of sixteen.  They go to
-// lengths_out, which the scan then reads.
+// lanes per request (group_window_length), into lengths_out, which the scan
+// then reads.
 __global__ void __launch_bounds__(1024) decode_lengths_scan_kernel(
     const int64_t* registry, const int64_t* row_ids, const int64_t* seq_lens, int64_t window,
     int batch, int32_t* kv_indptr, int64_t* lengths_out, int64_t* starts_out) {
@@ -237,49 +265,17 @@ __global__ void __launch_bounds__(1024) decode_lengths_scan_kernel(
   if (threadIdx.x == 0) carry = 0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (window >= 0) {
-    const int sub = threadIdx.x & 7, first_lane = lane & 24;
-    const unsigned group = 0xffu << first_lane;
     for (int b0 = 0; b0 < batch; b0 += blockDim.x >> 3) {
       const int b = b0 + (threadIdx.x >> 3);
       const bool has = b < batch;
       Entry e{};
-      long long seq = 0, lower = 0, generated = 0;
-      int32_t lo = 0, hi = 0;
+      long long seq = 0;
       if (has) {
         seq = seq_lens[b];
         e = load_entry(registry, row_ids[b]);
-        if (e.raw_ids != nullptr) {
-          generated = seq - e.active;
-          // the window is the inclusive distance q_pos - k_pos
-          lower = (long long)e.next_pos + generated - 1 - window;
-          hi = e.active;
-        }
       }
-      while (__any_sync(0xffffffffu, hi > lo)) {
-        int32_t probe = lo;
-        bool below = false;
-        if (hi > lo) {
-          probe = lo + (int32_t)(((long long)(hi - lo) * (sub + 1)) / 9);
-          below = (long long)__ldg(e.positions + probe) < lower;
-        }
-        const int c = __popc(__ballot_sync(0xffffffffu, below) & group);
-        const int32_t p_below = __shfl_sync(0xffffffffu, probe, first_lane + (c > 0 ? c - 1 : 0));
-        const int32_t p_above = __shfl_sync(0xffffffffu, probe, first_lane + (c < 8 ? c : 7));
-        if (hi > lo) {
-          if (c > 0) lo = p_below + 1;
-          if (c < 8) hi = p_above;
-        }
-      }
-      if (has && sub == 0) {
-        long long len;
-        if (e.raw_ids == nullptr) {
-          len = seq < window ? seq : window;
-        } else {
-          const long long skipped = lower - e.next_pos > 0 ? lower - e.next_pos : 0;
-          len = (long long)e.active - lo + generated - skipped;
-        }
-        lengths_out[b] = len;
-      }
+      const long long len = group_window_length(has, e, seq, window);
+      if (has && (threadIdx.x & 7) == 0) lengths_out[b] = len;
     }
   }
   __syncthreads();
@@ -448,7 +444,7 @@ extern "C" int akv_context_window_lengths(
   using namespace akv;
   if (batch < 0 || !registry || !row_ids || !lengths || !output) return AKV_ERR_INVALID;
   if (batch == 0) return AKV_OK;
-  window_lengths_kernel<<<(batch + kThreads - 1) / kThreads, kThreads, 0,
+  window_lengths_kernel<<<(int)(((long long)batch * 8 + kThreads - 1) / kThreads), kThreads, 0,
                           static_cast<cudaStream_t>(stream)>>>(
       registry, row_ids, row_ids_is64, lengths, lengths_is64, output, output_is64, window, batch);
   return launch_status();

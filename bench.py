@@ -1703,13 +1703,55 @@ def bench_decode_metadata(dev, world, rank, warmup, steps, seed=0, generated=4):
         torch.cuda.synchronize()
         ref_ms = timed(graph.replay)
         del graph
+        # Kernel by kernel: the reference's Triton launch and this package's
+        # drop-in launcher of the same name, same arguments, graph-captured.
+        from akv_b200 import context_page_table as ours_pt
+
+        w_starts = (seq_lens - r_wlen).contiguous()
+        o_wlen = torch.empty_like(seq_lens)
+        o_idx = torch.empty_like(kv_indices)
+        per_kernel = {}
+        for name, theirs, mine in (
+            ("context_window_lengths",
+             lambda: pt.context_window_lengths[(batch,)](registry, rows, seq_lens, r_wlen, 128),
+             lambda: ours_pt.context_window_lengths[(batch,)](registry, rows, seq_lens, o_wlen,
+                                                              128)),
+            ("context_decode_indices",
+             lambda: pt.context_decode_indices[(batch,)](
+                 registry, table, rows, seq_lens, r_indptr, r_indices, None, None,
+                 ROW_STRIDE=table.stride(0), TRANSLATE=False, MULTIPLIER=1, HAS_START=False),
+             lambda: ours_pt.context_decode_indices[(batch,)](
+                 registry, table, rows, seq_lens, r_indptr, o_idx, None, None,
+                 ROW_STRIDE=table.stride(0), TRANSLATE=False, MULTIPLIER=1, HAS_START=False)),
+        ):
+            times = []
+            for fn in (theirs, mine):
+                fn()
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for _ in range(steps):
+                        fn()
+                g.replay()
+                torch.cuda.synchronize()
+                times.append(timed(g.replay))
+                del g
+            torch.cuda.synchronize()
+            equal = torch.equal(o_wlen, r_wlen) if name == "context_window_lengths" else \
+                torch.equal(o_idx, r_indices)
+            per_kernel[name] = {"triton_us": round(1e3 * times[0], 2),
+                                "ours_us": round(1e3 * times[1], 2),
+                                "speedup": round(times[0] / times[1], 2),
+                                "outputs_equal": bool(equal)}
+        del w_starts
         triton_ref = {"triton_ms_per_step": round(ref_ms, 4),
                       "triton_eager_ms_per_step": round(ref_eager, 4),
                       "ours_ms_per_step": round(ms, 4), "speedup": round(ref_ms / ms, 2),
                       "outputs_equal": bool(same),
                       "what": "context_decode_indices (full) + context_window_lengths + "
                               "context_decode_indices (window 128) with the registry's "
-                              "cumsum / starts, graph-captured like ours"}
+                              "cumsum / starts, graph-captured like ours",
+                      "per_kernel": per_kernel}
     peak, peak_kind = measured_peak()
     gbs = alg / (ms / 1e3) / 1e9
     return {
