@@ -66,6 +66,18 @@ def test_argument_errors_are_reported_before_any_launch():
         None, None, 0, None, 0, None, 0, None, 0, None, 0, None, 0, None, 0, 1, 4,
         None) == _native.AKV_ERR_INVALID
     assert lib.akv_write_row_slots(None, None, 0, None, 0, None, 0, 0, None) == _native.AKV_OK
+    # reposition options: unknown bits are refused; the bulk V move is a known bit
+    assert lib.akv_reposition_kv_layers_ex(
+        None, None, 1, 1, 8, 64, 64, 512, 64, 512, 64, None, None, None, 2, 0, None, None,
+        2, 64, 1, 0, 0, 0, None, 2, None) == _native.AKV_ERR_INVALID
+    assert lib.akv_reposition_kv_layers_ex(
+        None, None, 1, 1, 8, 64, 64, 512, 64, 512, 64, None, None, None, 2, 0, None, None,
+        2, 64, 1, 0, 0, 0, None, _native.REPOSITION_BULK_V, None) == _native.AKV_OK
+    # paged Drop: page sizes other than 1 and powers of two in [4, 128]
+    for bad in (2, 12, 256, 0, -16):
+        args = [0, None, None, 0, None, None, None, None, None, 0, 1, bad, None, 1]
+        assert lib.akv_drop_compact_paged(*args, *([None] * 18)) == _native.AKV_ERR_INVALID
+    assert lib.akv_occurrence_advance_indices(None, None) == _native.AKV_ERR_INVALID
 
 
 def test_layout_batch_struct_matches_the_header():
@@ -84,3 +96,27 @@ def test_layout_batch_struct_matches_the_header():
     assert _native.lib.akv_compile_layouts_max_repositions() >= 1024
     assert _native.lib.akv_compile_layouts_workspace_bytes(3, 5000, 10, 300) > 0
     assert _native.lib.akv_compile_layouts(None, None) == _native.AKV_ERR_INVALID
+
+
+def _header_fields(text, typedef_end):
+    """Field names of the plain C struct ending at ``} <typedef_end>;``."""
+    end = text.index("} " + typedef_end + ";")
+    body = text[text.rindex("typedef struct", 0, end): end]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    names = []
+    for decl in body.split("{", 1)[1].split(";"):
+        decl = decl.strip()
+        if decl:
+            names += [n.strip().lstrip("*") for n in decl.split(" ", 1)[1].split(",")] \
+                if " " in decl else []
+    return [n.split()[-1].lstrip("*") for n in names]
+
+
+def test_occurrence_structs_match_the_header():
+    """The ctypes mirrors of akv_advance_in / akv_advance_out have the
+    header's fields, in order."""
+    from akv_b200 import context_occurrence as co
+
+    text = open(os.path.join(ROOT, "include", "akv_b200.h")).read()
+    assert _header_fields(text, "akv_advance_in") == [f[0] for f in co._AdvanceIn._fields_]
+    assert _header_fields(text, "akv_advance_out") == [f[0] for f in co._AdvanceOut._fields_]
