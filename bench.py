@@ -859,7 +859,7 @@ def c3_counts(prog, page_size):
 
 
 def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers=36,
-             cpu=True, e2e_steps=5, requests=64):
+             cpu=True, e2e_steps=8, requests=64):
     """c3: batched agent serving -- 64 requests (lengths U{2K..32K}, 1.18M
     tokens), one radix-shared prefix of 1K..4K tokens (a whole number of
     16-token pages) whose moved tokens must copy-on-write, per-request drop
@@ -1003,13 +1003,16 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                     ref, k_ptrs, v_ptrs, k_pools[0], v_pools[0], s_src, s_dst, s_pairs, cache,
                     3, stream, cnt * per)
         # e2e through the public API from host memory: validate + pack + one
-        # H2D copy + launches, and the decode view read back every step.
-        view = torch.empty(2 * kept, dtype=torch.int32, pin_memory=True)
+        # H2D copy + launches, and the decode view read back every step.  As
+        # in a serving loop (and the c2 e2e), the host issues step i + 1
+        # before it waits for the read-back of step i (two pinned buffers).
+        views = [torch.empty(2 * kept + 1, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        read = [torch.cuda.Event() for _ in range(2)]
         dist_barrier(world)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(e2e_steps):
+        for i in range(e2e_steps):
             rtt.copy_(rtt0)
             ring.state.copy_(state0)
             r2 = comp.run(prog.token_counts, prog.range_offsets, prog.ranges, rtt, row_ids, ring,
@@ -1018,10 +1021,19 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                                  r2.transition_destination, r2.transition_pairs, cache,
                                  count_device=r2.transition_count, page_size=ps,
                                  bulk_copy_v=True)
+            view = views[i % 2]
             view[:kept].copy_(r2.raw_indices[:kept], non_blocking=True)
-            view[kept:].copy_(r2.active_positions[:kept], non_blocking=True)
-            e1.record(stream)
-            e1.synchronize()
+            view[kept: 2 * kept].copy_(r2.active_positions[:kept], non_blocking=True)
+            view[2 * kept:].copy_(r2.status, non_blocking=True)
+            read[i % 2].record(stream)
+            if i > 0:
+                read[(i - 1) % 2].synchronize()
+                if int(views[(i - 1) % 2][-1]) != 0:
+                    raise RuntimeError("drop_compact status in the c3 e2e loop")
+        e1.record(stream)
+        e1.synchronize()
+        if int(views[(e2e_steps - 1) % 2][-1]) != 0:
+            raise RuntimeError("drop_compact status in the c3 e2e loop")
         e2e_s = dist_max(e0.elapsed_time(e1) / 1e3, world)
         step_bytes = (rep_bytes + drop_bytes) * world
         achieved = rep_bytes / (rep_ms / 1e3) / 1e9
@@ -1039,7 +1051,8 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                        "l2": "K pools 49 GB, larger than L2; no flush",
                        "restore": "rows + ring head restored on the device each step"},
             "e2e": {"value": round(step_bytes * e2e_steps / e2e_s / 1e9, 2), "unit": UNIT,
-                    "h2d_bytes_per_step": prepared["h2d_bytes"], "d2h_bytes_per_step": 8 * kept},
+                    "h2d_bytes_per_step": prepared["h2d_bytes"],
+                    "d2h_bytes_per_step": 8 * kept + 4},
             "breakdown_ms": {"drop_compact": round(drop_ms, 4), "reposition": round(rep_ms, 4)},
             "reposition_by_kind": split,
             "roofline": {"bound": "hbm", "kernel": "reposition_kernel",
