@@ -35,7 +35,7 @@ namespace {
 constexpr int kTile = 512;
 constexpr int kThreads = 128;
 constexpr int kPerThread = kTile / kThreads;  // 4 contiguous tokens per thread
-constexpr int kPlanThreads = 1024;
+constexpr int kPlanThreads = 256;
 constexpr int kFields = 4;  // kept, moved, cow, freed
 
 // Field packing for the block scan: 16 bits per counter (a tile holds at
@@ -300,47 +300,76 @@ __global__ void __launch_bounds__(kThreads) drop_count_kernel(const DropArgs a) 
   }
 }
 
+// Pairs of 32-bit counters in one 64-bit word: {kept, moved} and {cow,
+// freed}.  Every prefix is a count of tokens or pages of the call, below
+// 2^31, so the low field never carries into the high one.
+__device__ __forceinline__ unsigned long long pair32(int lo, int hi) {
+  return (unsigned long long)(unsigned)lo | ((unsigned long long)(unsigned)hi << 32);
+}
+
 __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs a) {
-  __shared__ int s_bad;
-  __shared__ long long s_carry[kFields];
+  __shared__ int s_bad, s_no_active;
+  // The ring state is written by no kernel of this call (last by the plan
+  // of the previous call, which completed before this call's count kernel
+  // started), so it is read before waiting for the tile counters.
+  // So are the staged program's offsets of this thread's first request.
+  long long ring_head = 0, ring_tail = 0;
+  if (threadIdx.x == 0) {
+    ring_head = a.ring_state[0];
+    ring_tail = a.ring_state[1];
+    s_bad = 0;
+    s_no_active = 0;
+  }
+  int first_tb = 0, first_te = 0, first_T = 0;
+  if ((int)threadIdx.x < a.n_requests) {
+    first_tb = a.tile_offsets[threadIdx.x];
+    first_te = a.tile_offsets[threadIdx.x + 1];
+    first_T = (int)(a.token_offsets[threadIdx.x + 1] - a.token_offsets[threadIdx.x]);
+  }
   pdl_wait();
   pdl_launch_dependents();
-  if (threadIdx.x == 0) {
-    s_bad = 0;
-    for (int f = 0; f < kFields; ++f) s_carry[f] = 0;
+  // Exclusive scan of the per-tile counters: thread i sums a contiguous run
+  // of tiles, one block scan gives each run its base, and the run is walked
+  // again to write the tiles' bases.
+  const int per = (a.n_tiles + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int t_begin = min((int)threadIdx.x * per, a.n_tiles);
+  const int t_end = min(t_begin + per, a.n_tiles);
+  unsigned long long km = 0, cf = 0;
+  int bad = 0;
+#pragma unroll 4
+  for (int t = t_begin; t < t_end; ++t) {
+    const int* ts = a.ws.tile_sums + 5 * (size_t)t;
+    km += pair32(ts[0], ts[1]);
+    cf += pair32(ts[2], ts[3]);
+    bad |= ts[4];
   }
-  __syncthreads();
-  // Exclusive scan of the per-tile counters, 1024 tiles per round.
-  for (int t0 = 0; t0 < a.n_tiles; t0 += blockDim.x) {
-    const int t = t0 + threadIdx.x;
-    int v[kFields] = {0, 0, 0, 0};
-    if (t < a.n_tiles) {
-      const int* ts = a.ws.tile_sums + 5 * (size_t)t;
-      for (int f = 0; f < kFields; ++f) v[f] = ts[f];
-      if (ts[4]) atomicOr(&s_bad, ts[4]);
-    }
-    for (int f = 0; f < kFields; ++f) {
-      int tot;
-      const int ex = block_exclusive_scan<int>(v[f], &tot);
-      if (t < a.n_tiles) a.ws.tile_base[4 * (size_t)t + f] = (int)(s_carry[f] + ex);
-      __syncthreads();
-      if (threadIdx.x == 0) s_carry[f] += tot;
-      __syncthreads();
-    }
+  unsigned long long km_total, cf_total;
+  unsigned long long km_base = block_exclusive_scan<unsigned long long>(km, &km_total);
+  if (bad) atomicOr(&s_bad, bad);  // s_bad was set before the scan's barriers
+  unsigned long long cf_base = block_exclusive_scan<unsigned long long>(cf, &cf_total);
+  for (int t = t_begin; t < t_end; ++t) {
+    *reinterpret_cast<int4*>(a.ws.tile_base + 4 * (size_t)t) =
+        make_int4((int)(unsigned)km_base, (int)(km_base >> 32), (int)(unsigned)cf_base,
+                  (int)(cf_base >> 32));
+    const int* ts = a.ws.tile_sums + 5 * (size_t)t;
+    km_base += pair32(ts[0], ts[1]);
+    cf_base += pair32(ts[2], ts[3]);
   }
-  const long long total_kept = s_carry[0], total_moved = s_carry[1], total_cow = s_carry[2],
-                  total_freed = s_carry[3];
-  __shared__ int s_no_active;
-  if (threadIdx.x == 0) s_no_active = 0;
-  __syncthreads();
+  __syncthreads();  // the bases are read back below by other threads
+  const long long carry[kFields] = {(long long)(unsigned)km_total, (long long)(km_total >> 32),
+                                    (long long)(unsigned)cf_total, (long long)(cf_total >> 32)};
+  const long long total_kept = carry[0], total_moved = carry[1], total_cow = carry[2],
+                  total_freed = carry[3];
   auto base_at = [&](int tile, int f) -> int {
-    return tile < a.n_tiles ? a.ws.tile_base[4 * (size_t)tile + f] : (int)s_carry[f];
+    return tile < a.n_tiles ? a.ws.tile_base[4 * (size_t)tile + f] : (int)carry[f];
   };
   for (int r = threadIdx.x; r < a.n_requests; r += blockDim.x) {
-    const int tb = a.tile_offsets[r], te = a.tile_offsets[r + 1];
+    const bool first = r == (int)threadIdx.x;
+    const int tb = first ? first_tb : a.tile_offsets[r];
+    const int te = first ? first_te : a.tile_offsets[r + 1];
+    const int T = first ? first_T : (int)(a.token_offsets[r + 1] - a.token_offsets[r]);
     const int kb = base_at(tb, 0), ke = base_at(te, 0);
     const int mb = base_at(tb, 1), me = base_at(te, 1);
-    const int T = (int)(a.token_offsets[r + 1] - a.token_offsets[r]);
     a.active_offsets[r] = kb;
     a.transition_offsets[r] = mb;
     a.freed_offsets[r] = base_at(tb, 3);
@@ -362,7 +391,7 @@ __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs 
     if (s_bad & 1) st |= AKV_DROP_BAD_RANGE;
     if (s_bad & 2) st |= AKV_DROP_BAD_PAGE;
     if (s_no_active) st |= AKV_DROP_NO_ACTIVE;
-    const long long head = a.ring_state[0], tail = a.ring_state[1];
+    const long long head = ring_head, tail = ring_tail;
     if (total_cow > tail - head) st |= AKV_DROP_RING_UNDERFLOW;
     else if (tail - head - total_cow + total_freed > a.ring_capacity) st |= AKV_DROP_RING_OVERFLOW;
     a.ws.plan[0] = head;
@@ -383,8 +412,9 @@ __global__ void __launch_bounds__(kPlanThreads) drop_plan_kernel(const DropArgs 
 }
 
 // Scatter of one tile in page mode (the rules above drop_count_kernel).
-__device__ void scatter_pages(const DropArgs& a, const TileCtx& c, int tile, int first_drop,
-                              int base) {
+__device__ void scatter_pages(const DropArgs& a, const TileCtx& c, int first_drop, int base,
+                              const int (&slots)[kPerThread], int4 tb, int req_kept_base,
+                              long long head, long long tail) {
   const int shift = a.page_shift, mask = (1 << shift) - 1;
   const int lanes = (1 << shift) / kPerThread;
   const PageFlags f = page_flags(a, c, first_drop, base);
@@ -398,19 +428,13 @@ __device__ void scatter_pages(const DropArgs& a, const TileCtx& c, int tile, int
   unsigned long long tot;
   const unsigned long long ex = block_exclusive_scan<unsigned long long>(
       pack4(kept, moved, f.lead && f.cow, f.lead && f.freed), &tot);
-  const int* tb = a.ws.tile_base + 4 * (size_t)tile;
-  int gk = tb[0] + field(ex, 0);
-  int gm = tb[1] + field(ex, 1);
-  const int gc = tb[2] + field(ex, 2);  // ring index of this page's copy (lead lane)
-  const int gf = tb[3] + field(ex, 3);
+  int gk = tb.x + field(ex, 0);
+  int gm = tb.y + field(ex, 1);
+  const int gc = tb.z + field(ex, 2);  // ring index of this page's copy (lead lane)
+  const int gf = tb.w + field(ex, 3);
   const int lead_lane = (threadIdx.x & 31) & ~(lanes - 1);
   const int page_gc = __shfl_sync(0xffffffffu, gc, lead_lane);
-  const int req_kept_base = a.active_offsets[c.r];
   int32_t* row = a.req_to_token + a.row_ids[c.r] * a.row_stride;
-  const long long head = a.ws.plan[0], tail = a.ws.plan[1];
-  int slots[kPerThread];
-#pragma unroll
-  for (int k = 0; k < kPerThread; ++k) slots[k] = base + k < c.n ? row[c.t0 + base + k] : 0;
   const int new_page = f.cow ? a.ring[(head + page_gc) % a.ring_capacity] : 0;
 #pragma unroll
   for (int k = 0; k < kPerThread; ++k) {
@@ -446,23 +470,40 @@ __device__ void scatter_pages(const DropArgs& a, const TileCtx& c, int tile, int
 }
 
 __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();  // lets a following reposition launch be scheduled
-  if (a.ws.plan[2] != 0) return;
+  // This kernel always follows the plan kernel of the same call, which
+  // follows count; count is an ordinary launch, so all earlier work of the
+  // stream has completed.  The staged program and the request's row are
+  // written by no kernel of this call before this one, so the tile's request
+  // and the slots of its tokens are read before waiting for the plan.
   const int tile = blockIdx.x;
   const TileCtx c = tile_context(a, tile);
-  const int first_drop = a.ws.first_drop[c.r];
   const int base = threadIdx.x * kPerThread;
+  int32_t* row = a.req_to_token + a.row_ids[c.r] * a.row_stride;
+  // All of this thread's slot loads go out before any store: the stores
+  // below may alias the row (copy-on-write rewrites it) so the compiler
+  // would otherwise serialise load, store, load, ...
+  int slots[kPerThread];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) slots[k] = base + k < c.n ? row[c.t0 + base + k] : 0;
+  pdl_wait();
+  pdl_launch_dependents();  // lets a following reposition launch be scheduled
+  // What count and plan wrote for this tile, loaded together.
+  const long long status = a.ws.plan[2], head = a.ws.plan[0], tail = a.ws.plan[1];
+  const int first_drop = a.ws.first_drop[c.r];
+  const int4 tb = *reinterpret_cast<const int4*>(a.ws.tile_base + 4 * (size_t)tile);
+  const int req_kept_base = a.active_offsets[c.r];
+  bool keep[kPerThread];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) keep[k] = base + k < c.n && a.keep_mask[c.flat0 + base + k] != 0;
+  if (status != 0) return;
   if (a.page_shift != 0) {
-    scatter_pages(a, c, tile, first_drop, base);
+    scatter_pages(a, c, first_drop, base, slots, tb, req_kept_base, head, tail);
     return;
   }
-  bool keep[kPerThread];
   int kept = 0, moved = 0, cow = 0, freed = 0;
 #pragma unroll
   for (int k = 0; k < kPerThread; ++k) {
     const int i = base + k;
-    keep[k] = i < c.n && a.keep_mask[c.flat0 + i] != 0;
     if (i < c.n) {
       const int t = c.t0 + i;
       const bool mv = a.reposition && keep[k] && t > first_drop;
@@ -475,20 +516,10 @@ __global__ void __launch_bounds__(kThreads) drop_scatter_kernel(const DropArgs a
   unsigned long long tot;
   const unsigned long long ex =
       block_exclusive_scan<unsigned long long>(pack4(kept, moved, cow, freed), &tot);
-  const int* tb = a.ws.tile_base + 4 * (size_t)tile;
-  int gk = tb[0] + field(ex, 0);
-  int gm = tb[1] + field(ex, 1);
-  int gc = tb[2] + field(ex, 2);
-  int gf = tb[3] + field(ex, 3);
-  const int req_kept_base = a.active_offsets[c.r];
-  int32_t* row = a.req_to_token + a.row_ids[c.r] * a.row_stride;
-  const long long head = a.ws.plan[0], tail = a.ws.plan[1];
-  // All of this thread's slot loads go out before any store: the stores
-  // below may alias the row (copy-on-write rewrites it) so the compiler
-  // would otherwise serialise load, store, load, ...
-  int slots[kPerThread];
-#pragma unroll
-  for (int k = 0; k < kPerThread; ++k) slots[k] = base + k < c.n ? row[c.t0 + base + k] : 0;
+  int gk = tb.x + field(ex, 0);
+  int gm = tb.y + field(ex, 1);
+  int gc = tb.z + field(ex, 2);
+  int gf = tb.w + field(ex, 3);
 #pragma unroll
   for (int k = 0; k < kPerThread; ++k) {
     const int i = base + k;
