@@ -458,26 +458,34 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (global_ns() - t0 > kWaitNs) return false;
   return true;
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+// TMEM access: each tcgen05.ld / tcgen05.st shares one asm statement with its
+// tcgen05.wait, so the compiler never sees a destination (or source)
+// register as settled while the asynchronous access is still in flight --
+// a register spilled or reused in between would otherwise be written (or
+// read) late.
+__device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, float* v) {
   uint32_t r[32];
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      "%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31},"
+      " [%32];\n\ttcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-        "=r"(r[31])
-      : "r"(taddr));
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+__device__ __forceinline__ void tmem_st32_sync(uint32_t taddr, const uint32_t* r) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
-      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
-          taddr),
+      "%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      "\n\ttcgen05.wait::st.sync.aligned;" ::"r"(taddr),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
@@ -485,31 +493,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+// Two stores of 16 columns (P's hi and lo words) and their wait.
+__device__ __forceinline__ void tmem_st16x2_sync(uint32_t ta, const uint32_t* a, uint32_t tb,
+                                                 const uint32_t* b) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
-      "%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15])
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%2,%3,%4,%5,%6,%7,%8,"
+      "%9,%10,%11,%12,%13,%14,%15,%16,%17};"
+      "\n\ttcgen05.st.sync.aligned.32x32b.x16.b32 [%1], {%18,%19,%20,%21,%22,%23,%24,%25,%26,"
+      "%27,%28,%29,%30,%31,%32,%33};"
+      "\n\ttcgen05.wait::st.sync.aligned;" ::"r"(ta), "r"(tb),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]),
+      "r"(a[8]), "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]),
+      "r"(a[15]), "r"(b[0]), "r"(b[1]), "r"(b[2]), "r"(b[3]), "r"(b[4]), "r"(b[5]), "r"(b[6]),
+      "r"(b[7]), "r"(b[8]), "r"(b[9]), "r"(b[10]), "r"(b[11]), "r"(b[12]), "r"(b[13]),
+      "r"(b[14]), "r"(b[15])
       : "memory");
-}
-// tcgen05.wait::ld that also takes the 32 loaded values as operands, so the
-// compiler cannot move their uses above the wait when other work sits
-// between the load and the wait.
-__device__ __forceinline__ void tmem_wait_ld32(float* v) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]),
-                 "+f"(v[6]), "+f"(v[7]), "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]),
-                 "+f"(v[12]), "+f"(v[13]), "+f"(v[14]), "+f"(v[15]), "+f"(v[16]), "+f"(v[17]),
-                 "+f"(v[18]), "+f"(v[19]), "+f"(v[20]), "+f"(v[21]), "+f"(v[22]), "+f"(v[23]),
-                 "+f"(v[24]), "+f"(v[25]), "+f"(v[26]), "+f"(v[27]), "+f"(v[28]), "+f"(v[29]),
-                 "+f"(v[30]), "+f"(v[31])
-               :
-               : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(const PrefillParams p) {
@@ -639,8 +637,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
     uint32_t z[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) z[i] = 0u;
-    tmem_st32(trow + kColO + 32 * half, z);
-    tmem_wait_st();
+    tmem_st32_sync(trow + kColO + 32 * half, z);
   }
   // S(0) as soon as Q and tile 0 have landed.
   cp_async_wait<kTcStages - 2>();
@@ -666,8 +663,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
     timed_out |= !mbar_wait(bar_s0 + 8 * (tile & 1), (uint32_t)(tile >> 1) & 1u);
     tc_fence_after();
     float s[kHalf];
-    tmem_ld32(trow + kColS + (tile & 1) * kTcKeys + half * kHalf, s);
-    tmem_wait_ld32(s);
+    tmem_ld32_sync(trow + kColS + (tile & 1) * kTcKeys + half * kHalf, s);
 
     // 2. Mask; half-row maximum of the raw scores (the scale is positive, so
     //    it is applied to the maximum only) to shared memory.  Rows past the
@@ -757,16 +753,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
     //    are warp-wide: a warp rescales when any of its rows must).
     if (__any_sync(0xffffffffu, rescale)) {
       float o[32];
-      tmem_ld32(trow + kColO + 32 * half, o);
-      tmem_wait_ld32(o);
+      tmem_ld32_sync(trow + kColO + 32 * half, o);
       uint32_t r[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
-      tmem_st32(trow + kColO + 32 * half, r);
+      tmem_st32_sync(trow + kColO + 32 * half, r);
     }
-    tmem_st16(trow + kColPHi + half * (kHalf / 2), hi);
-    tmem_st16(trow + kColPLo + half * (kHalf / 2), lo);
-    tmem_wait_st();
+    tmem_st16x2_sync(trow + kColPHi + half * (kHalf / 2), hi, trow + kColPLo + half * (kHalf / 2),
+                     lo);
     tc_fence_before();
     if (__syncthreads_or(timed_out)) {
       if (tid == 0) s_abort = 1;
@@ -802,8 +796,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) prefill_attention_tc_kernel(con
   }
   if (!failed) {
     float o[32];
-    tmem_ld32(trow + kColO + 32 * half, o);  // every thread: the load is warp-wide
-    tmem_wait_ld32(o);
+    tmem_ld32_sync(trow + kColO + 32 * half, o);  // every thread: the load is warp-wide
     float den = s_sum[row] + s_sum[128 + row];
     const float mb = m_used == -INFINITY ? 0.f : m_used;
     if (p.sinks) den += fast_exp2(p.sinks[head] * kLog2e - mb);
@@ -1158,8 +1151,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) z[i] = 0u;
 #pragma unroll
-      for (int c = 0; c < kOCols; c += 32) tmem_st32(trow + kColO + kOCols * half + c, z);
-      tmem_wait_st();
+      for (int c = 0; c < kOCols; c += 32) tmem_st32_sync(trow + kColO + kOCols * half + c, z);
     }
     if (n_tiles > 0) {  // Q and tile 0 landed
       cp_async_wait<kWsAhead - 1>();
@@ -1185,12 +1177,8 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
       // 1. S(t) -> this thread's 32 values of its row.
       ws_wait(bar_s(qt, tile & 1), (uint32_t)(tile >> 1) & 1u, abort);
       tc_fence_after();
-      const uint32_t sbuf = trow + kColS + (tile & 1) * kTcKeys;
-      float s[kHalf];
-      tmem_ld32(sbuf + half * kHalf, s);
-      // While the TMEM load is in flight: tile t + kWsAhead into the stage of
-      // tile t-2 (S(t) completed after P(t-2).V(t-2), so that stage is no
-      // longer read).
+      // Tile t + kWsAhead into the stage of tile t-2 (S(t) completed after
+      // P(t-2).V(t-2), so that stage is no longer read).
       {
         const int nt = tile + kWsAhead;
         if (nt < n_tiles) {
@@ -1199,7 +1187,9 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
         }
         cp_async_commit();
       }
-      tmem_wait_ld32(s);
+      const uint32_t sbuf = trow + kColS + (tile & 1) * kTcKeys;
+      float s[kHalf];
+      tmem_ld32_sync(sbuf + half * kHalf, s);
 
       // 2. Mask (key positions of tile t: acquired through its kv barrier);
       //    half-row maximum of the raw scores, four independent chains.
@@ -1272,17 +1262,14 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
 #pragma unroll
         for (int c = 0; c < kOCols; c += 32) {
           float o[32];
-          tmem_ld32(trow + kColO + kOCols * half + c, o);
-          tmem_wait_ld32(o);
+          tmem_ld32_sync(trow + kColO + kOCols * half + c, o);
           uint32_t r[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i] * alpha);
-          tmem_st32(trow + kColO + kOCols * half + c, r);
+          tmem_st32_sync(trow + kColO + kOCols * half + c, r);
         }
       }
-      tmem_st16(sbuf + half * (kHalf / 2), hi);
-      tmem_st16(sbuf + 32 + half * (kHalf / 2), lo);
-      tmem_wait_st();
+      tmem_st16x2_sync(sbuf + half * (kHalf / 2), hi, sbuf + 32 + half * (kHalf / 2), lo);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p(qt, tile & 1));
@@ -1306,8 +1293,7 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
 #pragma unroll
       for (int cb = 0; cb < kOCols; cb += 32) {
         float o[32];
-        tmem_ld32(trow + kColO + kOCols * half + cb, o);  // every lane: warp-wide load
-        tmem_wait_ld32(o);
+        tmem_ld32_sync(trow + kColO + kOCols * half + cb, o);  // every lane: warp-wide load
 #pragma unroll
         for (int c = 0; c < 4 && row_valid; ++c) {
           uint4 v;
