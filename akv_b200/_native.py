@@ -147,7 +147,18 @@ def ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device) -> ctypes.c_void_p:
+    """The current torch stream of ``device`` as a cudaStream_t."""
+    if _raw_stream is not None:
+        if isinstance(device, int):
+            return ctypes.c_void_p(_raw_stream(device))
+        d = device if isinstance(device, torch.device) else torch.device(device)
+        if d.type == "cuda":
+            index = d.index if d.index is not None else torch.cuda.current_device()
+            return ctypes.c_void_p(_raw_stream(index))
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 

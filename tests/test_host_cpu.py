@@ -23,6 +23,60 @@ def test_validate_program_follows_reference_rules():
         validate_program([4], [0, 1], [0, 4])
 
 
+def _validate_request_by_request(token_counts, range_offsets, ranges, reposition):
+    """The rules checked one request at a time, in order, as the reference
+    compiler meets them (context_plan.py:362-411); returns the message of
+    the first violation or None."""
+    ranges = np.asarray(ranges, np.int64).reshape(-1, 2)
+    for r, t in enumerate(token_counts):
+        rr = ranges[range_offsets[r]: range_offsets[r + 1]]
+        if not len(rr):
+            continue
+        s, e = rr[:, 0], rr[:, 1]
+        if np.any(s < 0) or np.any(s >= e) or np.any(e > t) or np.any(s[1:] <= e[:-1]):
+            return "Drop ranges must be ordered, disjoint, and already materialized"
+        if reposition and t > 0 and int((e - s).sum()) == t:
+            return f"Reposition at raw boundary {int(t) - 1} has no active tokens."
+    return None
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_validate_program_reports_the_first_failing_request(seed):
+    """The vectorised check raises what a request-by-request walk raises
+    first, on random batches with overlapping, empty, out-of-range and
+    all-covering ranges sprinkled in."""
+    from akv_b200.context_drop import validate_program
+
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(1, 12))
+    counts = rng.integers(0, 40, n)
+    offsets, ranges = [0], []
+    for t in counts:
+        k = int(rng.integers(0, 4))
+        cuts = np.sort(rng.choice(np.arange(t + 1), size=min(2 * k, t + 1), replace=False))
+        cuts = cuts if len(cuts) % 2 == 0 else cuts[:-1]
+        pairs = cuts.reshape(-1, 2).tolist()
+        kind = rng.integers(0, 30)
+        if kind == 0 and pairs:
+            pairs[0] = [pairs[0][1], pairs[0][0]]  # reversed
+        elif kind == 1 and len(pairs) > 1:
+            pairs[1][0] = pairs[0][0]  # overlap
+        elif kind == 2:
+            pairs.append([int(t), int(t) + 3])  # past the prompt
+        elif kind == 3 and t > 0:
+            pairs = [[0, int(t)]]  # everything dropped
+        ranges += [x for pr in pairs for x in pr]
+        offsets.append(offsets[-1] + len(pairs))
+    for reposition in (True, False):
+        want = _validate_request_by_request(counts, offsets, ranges, reposition)
+        if want is None:
+            validate_program(counts, offsets, ranges, reposition)
+        else:
+            with pytest.raises(ValueError) as err:
+                validate_program(counts, offsets, ranges, reposition)
+            assert str(err.value) == want
+
+
 @pytest.mark.parametrize("seed", range(6))
 def test_single_stage_closed_form_matches_compiler(seed):
     """The formulas the drop kernels evaluate (keep = not covered, rank =
