@@ -228,7 +228,9 @@ class DropCompactor:
                 reposition=True, validate=True, page_size=1) -> dict:
         """Host half: validation, packing and the host-to-device copy.  The
         returned handle can be launched any number of times while the
-        staged program stays resident on the device.
+        staged program stays resident on the device, i.e. until the next
+        ``prepare`` or ``run`` of this compactor (which restages; a program
+        of the same shape gets the same handle back).
 
         ``page_size`` > 1 (a power of two from 4 to 128) runs the paged form
         (``akv_drop_compact_paged``): the ring holds page ids, a private

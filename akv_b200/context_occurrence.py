@@ -37,11 +37,13 @@ import numpy as np
 import torch
 
 import ctypes
+import itertools
 
 from . import _native
 
 _MAX_SEGMENTS = 4
-_TASK_WORDS = 12
+_TASK_WORDS = 12  # first index, outputs, output address, flags, 4 segment addresses, 4 ends
+_CHUNK = int(_native.lib.akv_gather_slots_chunk())  # outputs per block of the gather kernel
 _P, _I64 = ctypes.c_void_p, ctypes.c_int64
 
 
@@ -93,9 +95,59 @@ class SlotGather:
             self.device = torch.device("cuda", torch.cuda.current_device())
         # what Tensor.get_device() returns for a tensor on this device
         self._index = self.device.index if self.device.type == "cuda" else -1
-        self._tasks = []
-        self._rows = []
-        self._segments = {}
+        self._reset()
+
+    def _reset(self):
+        self._tasks = []      # (out, indices, segments, literal): kept alive until the launch
+        self._idx = []        # index vector of each task
+        self._meta = []       # (outputs, output address, flags, segment set) of recent tasks
+        self._blocks = []     # earlier tasks' rows of the same four columns, in order
+        self._sized = None    # the three arrays of _sizes, until the next task
+        self._seg_ids = {}    # segment-set key -> row of _seg_table
+        self._seg_objs = []   # the segment tuples, by id
+        self._seg_table = []  # per segment set: 4 base addresses, 4 cumulative ends
+        self._seg_flags = []
+
+    def segment_set(self, segments, literal=False, m=0):
+        """Id of a tuple of segments (checked and registered on first use)."""
+        # A tuple is keyed by its identity (registered here, so it stays
+        # alive and its id unique); anything else by its tensors' identities.
+        key = id(segments) if type(segments) is tuple else tuple(map(id, segments))
+        sid = self._seg_ids.get(key)
+        if sid is not None:
+            if m and not literal and not self._seg_flags[sid] >> 8:
+                raise ValueError("a slot gather reads one to four segments")
+            return sid
+        segments = tuple(segments)
+        if len(segments) > _MAX_SEGMENTS or (not literal and not segments and m):
+            raise ValueError("a slot gather reads one to four segments")
+        for s in segments:
+            if s.ndim != 1 or s.dtype != segments[0].dtype or s.dtype not in (
+                    torch.int32, torch.int64) or s.get_device() != self._index or \
+                    not s.is_contiguous():
+                raise ValueError("gather segments must be contiguous int32/int64 vectors "
+                                 "of one dtype on the device")
+        ptrs, ends, end = [0] * _MAX_SEGMENTS, [0] * _MAX_SEGMENTS, 0
+        for i, seg in enumerate(segments):
+            size = seg.numel()
+            end += size
+            ptrs[i] = seg.data_ptr() if size else 0
+            ends[i] = end
+        flags = len(segments) << 8
+        if segments and segments[0].dtype == torch.int64:
+            flags |= _native.GATHER_SEG64
+        sid = len(self._seg_table)
+        self._seg_table.append(ptrs + ends)
+        self._seg_flags.append(flags)
+        self._seg_objs.append(segments)
+        self._seg_ids[key] = sid
+        return sid
+
+    def _flush(self):
+        if self._meta:
+            self._blocks.append(np.fromiter(itertools.chain.from_iterable(self._meta), np.int64,
+                                            4 * len(self._meta)).reshape(-1, 4))
+            self._meta = []
 
     def add(self, out: torch.Tensor, indices, segments=(), *, literal: bool = False):
         """out[i] = concat(segments)[indices[i]] (-1 where the index is
@@ -118,45 +170,26 @@ class SlotGather:
         if type(idx) is not np.ndarray or idx.ndim != 1:
             idx = np.asarray(idx).reshape(-1)
         m = idx.shape[0]
-        key = tuple(map(id, segments))
-        info = self._segments.get(key)
-        if info is None:
-            segments = tuple(segments)
-            if len(segments) > _MAX_SEGMENTS or (not literal and not segments and m):
-                raise ValueError("a slot gather reads one to four segments")
-            for s in segments:
-                if s.ndim != 1 or s.dtype != segments[0].dtype or s.dtype not in (
-                        torch.int32, torch.int64) or s.get_device() != self._index or \
-                        not s.is_contiguous():
-                    raise ValueError("gather segments must be contiguous int32/int64 vectors "
-                                     "of one dtype on the device")
-            ptrs, ends, end = [0] * _MAX_SEGMENTS, [0] * _MAX_SEGMENTS, 0
-            for i, seg in enumerate(segments):
-                size = seg.numel()
-                end += size
-                ptrs[i] = seg.data_ptr() if size else 0
-                ends[i] = end
-            flags = len(segments) << 8
-            if segments and segments[0].dtype == torch.int64:
-                flags |= _native.GATHER_SEG64
-            info = (flags, ptrs + ends)
-            # the task list holds the segments, so their ids stay unique
-            self._segments[key] = info
+        sid = self.segment_set(segments, literal, m)
         if m > 2**31 - 1:
             raise ValueError("a slot gather task holds at most 2^31 - 1 outputs")
-        flags = info[0] | (_native.GATHER_OUT64 if out.dtype == torch.int64 else 0) | \
-            (_native.GATHER_LITERAL if literal else 0)
-        self._rows.append([0, m, out.data_ptr() if m else 0, flags, *info[1]])
-        self._tasks.append((out, idx, segments, literal))
+        flags = self._seg_flags[sid] | (_native.GATHER_OUT64 if out.dtype == torch.int64 else 0) \
+            | (_native.GATHER_LITERAL if literal else 0)
+        self._meta.append((m, out.data_ptr() if m else 0, flags, sid))
+        self._idx.append(idx)
+        self._tasks.append((out, idx, self._seg_objs[sid], literal))
+        self._sized = None
 
     def __len__(self):
         return len(self._tasks)
 
     def _sizes(self):
-        chunk = int(_native.lib.akv_gather_slots_chunk())
-        lengths = np.fromiter((len(t[1]) for t in self._tasks), np.int64, len(self._tasks))
-        counts = (lengths + chunk - 1) // chunk
-        return chunk, lengths, counts
+        if self._sized is None:
+            self._flush()
+            meta = np.concatenate(self._blocks) if self._blocks else np.zeros((0, 4), np.int64)
+            lengths = meta[:, 0]
+            self._sized = (meta, lengths, (lengths + _CHUNK - 1) // _CHUNK)
+        return self._sized
 
     def words(self):
         """Length of the packed program in int64 words (indices are int32,
@@ -168,7 +201,7 @@ class SlotGather:
         """(words, n_tasks, n_chunks): the int64 task table, the chunk table
         (one word per chunk: the int32 pair {task, first output}) and the
         int32 indices, in that order; written into ``out`` when given."""
-        chunk, lengths, counts = self._sizes()
+        meta, lengths, counts = self._sizes()
         n, n_chunks = len(self._tasks), int(counts.sum())
         if n_chunks > 2**31 - 1:
             raise ValueError("too many slot gather chunks for one launch")
@@ -176,17 +209,19 @@ class SlotGather:
         total = _TASK_WORDS * n + n_chunks + (n_idx + 1) // 2
         words = np.empty(total, np.int64) if out is None else out[:total]
         if n:
+            # row: first index, outputs, output address, flags, segment addresses, ends
             table = words[:_TASK_WORDS * n].reshape(n, _TASK_WORDS)
-            table[:] = np.asarray(self._rows, np.int64)
             table[:, 0] = np.cumsum(lengths) - lengths
+            table[:, 1:4] = meta[:, :3]
+            table[:, 4:] = np.array(self._seg_table, np.int64)[meta[:, 3]]
         task = np.repeat(np.arange(n, dtype=np.int32), counts)
         start = np.repeat(np.cumsum(counts) - counts, counts)
         pairs = words[_TASK_WORDS * n:_TASK_WORDS * n + n_chunks].view(np.int32).reshape(-1, 2)
         pairs[:, 0] = task
-        pairs[:, 1] = (np.arange(n_chunks) - start) * chunk
+        pairs[:, 1] = (np.arange(n_chunks) - start) * _CHUNK
         if n_idx:
             idx = words[_TASK_WORDS * n + n_chunks:].view(np.int32)[:n_idx]
-            np.concatenate([t[1] for t in self._tasks], out=idx, casting="unsafe")
+            np.concatenate(self._idx, out=idx, casting="unsafe")
         return words, n, n_chunks
 
     def launch(self, error_flag: torch.Tensor | None = None):
@@ -200,7 +235,7 @@ class SlotGather:
         # copy that reads it has run
         host = torch.empty(self.words(), dtype=torch.int64, pin_memory=True)
         _, n_tasks, n_chunks = self.pack(out=host.numpy())
-        self._tasks, self._rows, self._segments = [], [], {}
+        self._reset()
         if n_chunks == 0:
             return
         dev = host.to(self.device, non_blocking=True)
@@ -313,29 +348,39 @@ class _AdvancePlan:
             self.swa_retired = torch.from_numpy(swa_retired[:r].view(np.bool_))
             self.swa = True
 
-    def add_tasks(self, gather: SlotGather, occurrence_out, src_out, dst_out, pairs_out):
-        """Queue this request's fields; the batch-level outputs are views the
-        caller provides.  Returns the per-request device tensors."""
-        dev, dt = self.device, self.dtype
-        succ_slots = torch.empty(len(self.retained), dtype=dt, device=dev)
-        retired = torch.empty(len(self.retired), dtype=dt, device=dev)
-        seg = self.segments
+    def sizes(self):
+        """Outputs per field: occurrences, copies, pair words, retained,
+        retired, unused SWA slots."""
+        return (len(self.occurrences), len(self.copy_src), len(self.pairs), len(self.retained),
+                len(self.retired), len(self.unused_swa) if self.swa is not None else 0)
+
+    def add_tasks(self, gather: SlotGather, occurrence_out, src_out, dst_out, pairs_out,
+                  succ_slots=None, retired=None, unused=None):
+        """Queue this request's fields into the views the caller provides
+        (the successor's slots and the retired and unused SWA slots are
+        allocated here when not given).  Returns the per-request result."""
+        dev, dt, seg = self.device, self.dtype, self.segments
+        if succ_slots is None:
+            succ_slots = torch.empty(len(self.retained), dtype=dt, device=dev)
+        if retired is None:
+            retired = torch.empty(len(self.retired), dtype=dt, device=dev)
         gather._add(occurrence_out, self.occurrences, seg)
         gather._add(src_out, self.copy_src, seg)
         gather._add(dst_out, self.copy_dst, seg)
         gather._add(pairs_out, self.pairs, literal=True)
         gather._add(succ_slots, self.retained, seg)
         gather._add(retired, self.retired, seg)
-        unused = None
         if self.swa is not None:
-            unused = torch.empty(len(self.unused_swa), dtype=dt, device=dev)
+            if unused is None:
+                unused = torch.empty(len(self.unused_swa), dtype=dt, device=dev)
             gather._add(unused, self.unused_swa, seg)
         owned, canon, term, positions = self.successor
         state = self.state_type(
             succ_slots, owned, canon, term, positions, self.exact_prefix_len,
             self.swa_retained if self.swa is not None else None)
         return OccurrenceAdvance(
-            state, occurrence_out, src_out, dst_out, pairs_out.view(-1, 2), retired, unused,
+            state, occurrence_out, src_out, dst_out, pairs_out.view(-1, 2), retired,
+            unused if self.swa is not None else None,
             self.swa_retired if self.swa is not None else None)
 
 
@@ -453,33 +498,35 @@ class OccurrenceBatch:
         if len(dtypes) != 1:
             raise ValueError("all requests of a forward bind slots of one dtype")
         dtype = dtypes.pop()
-        n_slots = n_copy = n_pairs = 0
-        for kind, p in self._items:
-            if kind == "context":
-                n_slots += len(p.occurrences)
-                n_copy += len(p.copy_src)
-                n_pairs += len(p.pairs)
-            else:
-                n_slots += len(p[0]) + len(p[1])
-        slots = torch.empty(n_slots, dtype=dtype, device=self.device)
+        # Per item: slots (occurrences, or prefix + birth), copies, pair
+        # words, retained, retired, unused SWA slots; every field of the
+        # batch is one buffer split into per-item views.
+        sizes = np.array([p.sizes() if kind == "context" else
+                          (len(p[0]) + len(p[1]), 0, 0, 0, 0, 0) for kind, p in self._items],
+                         np.int64).reshape(-1, 6)
+        totals = sizes.sum(axis=0)
+        slots = torch.empty(int(totals[0]), dtype=dtype, device=self.device)
+        n_copy, n_pairs = int(totals[1]), int(totals[2])
         i32 = torch.empty(2 * n_copy + n_pairs, dtype=torch.int32, device=self.device)
         sources, destinations = i32[:n_copy], i32[n_copy:2 * n_copy]
         positions = i32[2 * n_copy:]
+        kept = torch.empty(int(totals[3] + totals[4] + totals[5]), dtype=dtype, device=self.device)
+        split = lambda t, col: t.split_with_sizes(sizes[:, col].tolist())  # noqa: E731
+        v_slots, v_src, v_dst = split(slots, 0), split(sources, 1), split(destinations, 1)
+        v_pairs = split(positions, 2)
+        v_succ, v_retired, v_unused = kept.split_with_sizes(
+            [int(totals[3]), int(totals[4]), int(totals[5])])
+        v_succ, v_retired, v_unused = split(v_succ, 3), split(v_retired, 4), split(v_unused, 5)
         gather = SlotGather(self.device)
         advances = []
-        s = c = q = 0
-        for kind, p in self._items:
+        for i, (kind, p) in enumerate(self._items):
             if kind == "context":
-                k, m, r = len(p.occurrences), len(p.copy_src), len(p.pairs)
-                advances.append(p.add_tasks(gather, slots[s:s + k], sources[c:c + m],
-                                            destinations[c:c + m], positions[q:q + r]))
-                s, c, q = s + k, c + m, q + r
+                advances.append(p.add_tasks(gather, v_slots[i], v_src[i], v_dst[i], v_pairs[i],
+                                            v_succ[i], v_retired[i], v_unused[i]))
             else:
                 prefix, birth = p
-                k = len(prefix) + len(birth)
                 seg = tuple(x for x in (prefix, birth) if len(x)) or (birth,)
-                gather._add(slots[s:s + k], np.arange(k), seg)
+                gather._add(v_slots[i], np.arange(int(sizes[i, 0])), seg)
                 advances.append(None)
-                s += k
         self._items = []
         return gather, (advances, slots, sources, destinations, positions.view(-1, 2))

@@ -1501,21 +1501,24 @@ def bench_occurrence(dev, world, rank, warmup, steps, seed=0, requests=16, prefi
     succ = [torch.empty(len(r["keep"]), dtype=torch.int64, device=dev) for r in reqs]
     retired = [torch.empty(len(r["release"]), dtype=torch.int64, device=dev) for r in reqs]
 
+    occ_sizes = [len(r["occ"]) for r in reqs]
+
     def queue():
         # the tasks OccurrenceBatch queues per request (its internal _add:
-        # outputs it allocated, indices that fit int32 by construction)
+        # per-request views of batch buffers it allocated, indices that fit
+        # int32 by construction)
         g = SlotGather(dev)
-        s = c = 0
+        v_slots = out_slots.split_with_sizes(occ_sizes)
+        v_src, v_dst, v_pairs = (i32[:n_copy].split(copies), i32[n_copy:2 * n_copy].split(copies),
+                                 i32[2 * n_copy:].split(2 * copies))
         for j, r in enumerate(reqs):
-            k = len(r["occ"])
-            g._add(out_slots[s:s + k], r["occ"], r["seg"])
-            g._add(i32[c:c + copies], r["src"], r["seg"])
-            g._add(i32[n_copy + c:n_copy + c + copies], r["dst"], r["seg"])
-            g._add(i32[2 * n_copy + 2 * c:2 * n_copy + 2 * c + 2 * copies], r["pairs"],
-                   literal=True)
-            g._add(succ[j], r["keep"], r["seg"])
-            g._add(retired[j], r["release"], r["seg"])
-            s, c = s + k, c + copies
+            seg = r["seg"]
+            g._add(v_slots[j], r["occ"], seg)
+            g._add(v_src[j], r["src"], seg)
+            g._add(v_dst[j], r["dst"], seg)
+            g._add(v_pairs[j], r["pairs"], literal=True)
+            g._add(succ[j], r["keep"], seg)
+            g._add(retired[j], r["release"], seg)
         return g
 
     def ours():
