@@ -470,7 +470,10 @@ class OccurrenceBatch:
     positions)``: one ``OccurrenceAdvance`` per context request (None for
     ordinary ones) and the concatenations the scheduler builds with
     ``torch.cat`` (akv/system/sglang.patch:3133-3180).  Per-request outputs
-    are views of the concatenated tensors."""
+    are views of the concatenated tensors, and the successors' slots and
+    the retired and unused SWA slots are views of one more batch buffer
+    (each view is its request's own elements; the buffer lives as long as
+    any of them)."""
 
     def __init__(self, device):
         self.device = torch.device(device)
