@@ -100,15 +100,14 @@ class SlotGather:
     def _reset(self):
         self._tasks = []      # (out, indices, segments, literal): kept alive until the launch
         self._idx = []        # index vector of each task
-        self._meta = []       # (outputs, output address, flags, segment set) of recent tasks
-        self._blocks = []     # earlier tasks' rows of the same four columns, in order
+        self._meta = []       # (outputs, output address, flags, segment set) per task
         self._sized = None    # the three arrays of _sizes, until the next task
         self._seg_ids = {}    # segment-set key -> row of _seg_table
         self._seg_objs = []   # the segment tuples, by id
         self._seg_table = []  # per segment set: 4 base addresses, 4 cumulative ends
         self._seg_flags = []
 
-    def segment_set(self, segments, literal=False, m=0):
+    def _segment_set(self, segments, literal=False, m=0):
         """Id of a tuple of segments (checked and registered on first use)."""
         # A tuple is keyed by its identity (registered here, so it stays
         # alive and its id unique); anything else by its tensors' identities.
@@ -143,12 +142,6 @@ class SlotGather:
         self._seg_ids[key] = sid
         return sid
 
-    def _flush(self):
-        if self._meta:
-            self._blocks.append(np.fromiter(itertools.chain.from_iterable(self._meta), np.int64,
-                                            4 * len(self._meta)).reshape(-1, 4))
-            self._meta = []
-
     def add(self, out: torch.Tensor, indices, segments=(), *, literal: bool = False):
         """out[i] = concat(segments)[indices[i]] (-1 where the index is
         negative), or indices[i] itself with ``literal``; out is int32 or
@@ -170,7 +163,7 @@ class SlotGather:
         if type(idx) is not np.ndarray or idx.ndim != 1:
             idx = np.asarray(idx).reshape(-1)
         m = idx.shape[0]
-        sid = self.segment_set(segments, literal, m)
+        sid = self._segment_set(segments, literal, m)
         if m > 2**31 - 1:
             raise ValueError("a slot gather task holds at most 2^31 - 1 outputs")
         flags = self._seg_flags[sid] | (_native.GATHER_OUT64 if out.dtype == torch.int64 else 0) \
@@ -185,8 +178,8 @@ class SlotGather:
 
     def _sizes(self):
         if self._sized is None:
-            self._flush()
-            meta = np.concatenate(self._blocks) if self._blocks else np.zeros((0, 4), np.int64)
+            meta = np.fromiter(itertools.chain.from_iterable(self._meta), np.int64,
+                               4 * len(self._meta)).reshape(-1, 4)
             lengths = meta[:, 0]
             self._sized = (meta, lengths, (lengths + _CHUNK - 1) // _CHUNK)
         return self._sized
