@@ -87,8 +87,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=None,
                    help="override the workload's layer count (a smaller cut for ncu captures)")
     p.add_argument("--shard", type=int, default=1, choices=[1, 2, 4, 8],
-                   help="c4: run one rank's share of an N-way KV-head split on this GPU "
-                        "(8/N KV heads; a profiling aid, not a multi-GPU run)")
+                   help="c4 / c3: run one rank's share of an N-way KV-head split on this "
+                        "GPU (8/N KV heads; a profiling aid, not a multi-GPU run)")
     p.add_argument("--variant", type=int, default=0,
                    help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05, "
                         "3 tcgen05 warp-specialised, 4 the same with two query tiles per CTA)")
@@ -859,7 +859,7 @@ def c3_counts(prog, page_size):
 
 
 def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers=36,
-             cpu=True, e2e_steps=8, requests=64):
+             cpu=True, e2e_steps=8, requests=64, shard=1, bulk_v=True):
     """c3: batched agent serving -- 64 requests (lengths U{2K..32K}, 1.18M
     tokens), one radix-shared prefix of 1K..4K tokens (a whole number of
     16-token pages) whose moved tokens must copy-on-write, per-request drop
@@ -881,7 +881,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
     from akv_b200.rope import yarn_cos_sin_cache
 
     heads_total, dim = 8, 64
-    heads = heads_total // world
+    heads = heads_total // (world * shard)
     prog = workloads.c3_program(seed=seed, page_align=16, requests=requests)
     total = prog.total_tokens
     layouts = {}
@@ -935,7 +935,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
             reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
                                  res.transition_destination, res.transition_pairs, cache,
                                  count_device=res.transition_count, page_size=ps,
-                                 bulk_copy_v=True)
+                                 bulk_copy_v=bulk_v)
             if i is not None:
                 ev[i][2].record(stream)
             return res
@@ -1020,7 +1020,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
             reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], r2.transition_source,
                                  r2.transition_destination, r2.transition_pairs, cache,
                                  count_device=r2.transition_count, page_size=ps,
-                                 bulk_copy_v=True)
+                                 bulk_copy_v=bulk_v)
             view = views[i % 2]
             view[:kept].copy_(r2.raw_indices[:kept], non_blocking=True)
             view[kept: 2 * kept].copy_(r2.active_positions[:kept], non_blocking=True)
@@ -1972,7 +1972,7 @@ def main():
         torch.cuda.set_device(dev)
         res = bench_c3(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)),
                        page_sizes=(args.page_size,), layers=args.layers or 36, cpu=False,
-                       requests=args.requests or 64)
+                       requests=args.requests or 64, shard=args.shard)
         if rank == 0:
             print(json.dumps(res[args.page_size]), flush=True)
         if world > 1:
