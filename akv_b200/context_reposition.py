@@ -67,8 +67,10 @@ def reposition_kv_layers(
     ``bulk_copy_v``: move the V rows of copy transitions with TMA bulk
     copies in a second kernel (``AKV_REPOSITION_BULK_V``).  Faster when
     copies are a minority of the list, as in a Drop's mixed list of in-place
-    rotations and copy-on-write; slower when every transition is a copy.
-    Results are identical either way.
+    rotations and copy-on-write, and a token's V row (local heads x head_dim
+    x element size) is 512 bytes or more; slower when every transition is a
+    copy, and at 128-byte rows (one KV head of head_dim 64).  Results are
+    identical either way.
     """
     if page_size != 1 and (page_size < 4 or page_size > 128 or page_size & (page_size - 1)):
         raise ValueError("Context Reposition requires page_size=1")

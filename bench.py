@@ -859,7 +859,7 @@ def c3_counts(prog, page_size):
 
 
 def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers=36,
-             cpu=True, e2e_steps=8, requests=64, shard=1, bulk_v=True):
+             cpu=True, e2e_steps=8, requests=64, shard=1, bulk_v=None):
     """c3: batched agent serving -- 64 requests (lengths U{2K..32K}, 1.18M
     tokens), one radix-shared prefix of 1K..4K tokens (a whole number of
     16-token pages) whose moved tokens must copy-on-write, per-request drop
@@ -882,6 +882,10 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
 
     heads_total, dim = 8, 64
     heads = heads_total // (world * shard)
+    if bulk_v is None:
+        # The TMA bulk move of the copies' V rows pays from 512-byte rows on
+        # (4+ local heads); at one head (128 B) it loses to one-pass staging.
+        bulk_v = heads * dim * 2 >= 512
     prog = workloads.c3_program(seed=seed, page_align=16, requests=requests)
     total = prog.total_tokens
     layouts = {}
@@ -1044,6 +1048,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                        "tokens": total, "shared_prefix": int(prog.shared_prefix.max()),
                        "layers": layers, "kv_heads": heads_total, "kv_heads_per_gpu": heads,
                        "head_dim": dim, "page_size": ps, "rope": "yarn",
+                       "bulk_copy_v": bool(bulk_v),
                        "moved_tokens": n, "cow_transitions": n_cow,
                        "in_place_transitions": n - n_cow,
                        ("copied_pages" if ps > 1 else "copied_slots"): copied,
