@@ -274,3 +274,41 @@ def test_drop_then_reposition_replayed_from_a_cuda_graph():
         np.testing.assert_array_equal(dv[layer].cpu().view(torch.int16).numpy().view(np.uint16),
                                       hv[layer])
     del graph
+
+
+def test_same_shape_programs_restage_through_one_compactor():
+    """A compactor hands the same staging handle back for programs of the
+    same shape; each call must still stage its own program (A, B, A again
+    through one compactor, each against the oracle)."""
+    from akv_b200.context_drop import DropCompactor, FreeSlotRing
+    from akv_b200.workloads import DropProgram
+    from oracle import oracle
+
+    dev = torch.device("cuda")
+    counts = np.array([3000, 2000])
+    programs = [DropProgram(counts, np.array([0, 2, 3], np.int32),
+                            np.asarray(r, np.int32), np.zeros(2, np.int64))
+                for r in ([10, 200, 700, 900, 5, 1500], [1000, 1100, 2500, 2990, 400, 401])]
+    rng = np.random.default_rng(5)
+    rows = [rng.permutation(int(c)).astype(np.int32) + 1 + 5000 * r for r, c in enumerate(counts)]
+    table = np.zeros((3, 3000), np.int32)
+    table[1, :3000], table[2, :2000] = rows
+    req_to_token = torch.from_numpy(table).to(dev)
+    comp = DropCompactor(5000, 2, 3, dev)
+    handles = []
+    for p in (programs[0], programs[1], programs[0]):
+        ring = FreeSlotRing(torch.zeros(0, dtype=torch.int32), capacity=6000, device=dev)
+        handles.append(comp.prepare(p.token_counts, p.range_offsets, p.ranges, [1, 2]))
+        res = comp.launch(handles[-1], req_to_token, ring)
+        want = oracle.drop_compact(p.token_counts, p.range_offsets, p.ranges, rows,
+                                   shared_prefix=p.shared_prefix, reposition=True,
+                                   free_ring=np.zeros(0, np.int32), free_head=0, free_tail=0)
+        torch.cuda.synchronize()
+        res.check()
+        keep = np.concatenate([lay["keep_mask"] for lay in want["layouts"]])
+        pos = np.concatenate([lay["positions"] for lay in want["layouts"]])
+        np.testing.assert_array_equal(res.keep_mask.cpu().numpy().astype(bool), keep)
+        np.testing.assert_array_equal(res.positions.cpu().numpy(), pos)
+        n = int(res.totals[1].item())
+        np.testing.assert_array_equal(res.transition_source[:n].cpu().numpy(), want["src"])
+    assert handles[0] is handles[1] is handles[2]
