@@ -410,3 +410,18 @@ def test_reposition_division_matches_ieee():
         assert int(bad.sum().item()) == 0, (
             f"{int(bad.sum())} quotients differ, e.g. "
             f"{a[bad][:4].tolist()} / {b[bad][:4].tolist()}")
+
+
+def test_launches_follow_the_current_torch_stream():
+    """Every entry point takes the stream torch has current for the device:
+    the fast lookup agrees with torch.cuda.current_stream inside and
+    outside a stream context, for every way a device is named."""
+    from akv_b200 import _native
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    forms = (dev, dev.index, f"cuda:{dev.index}", torch.device("cuda"))
+    for s in (torch.cuda.current_stream(dev), torch.cuda.Stream(dev)):
+        with torch.cuda.stream(s):
+            for form in forms:
+                assert _native.stream_of(form).value == s.cuda_stream or \
+                    (_native.stream_of(form).value is None and s.cuda_stream == 0)
