@@ -125,17 +125,28 @@ def validate_program(token_counts, range_offsets, ranges, reposition=True):
     token_counts = np.asarray(token_counts, np.int64)
     range_offsets = np.asarray(range_offsets, np.int64)
     ranges = np.asarray(ranges, np.int64).reshape(-1, 2)
-    per_request = np.diff(range_offsets)
-    if len(range_offsets) != len(token_counts) + 1 or range_offsets[0] != 0 or \
-            range_offsets[-1] != len(ranges) or np.any(per_request < 0):
+    n = len(token_counts)
+    if len(range_offsets) != n + 1 or range_offsets[0] != 0 or \
+            range_offsets[-1] != len(ranges):
         raise ValueError("drop_range_offsets does not cover drop_ranges")
-    if np.any(token_counts < 0) or np.any(token_counts > np.iinfo(np.int32).max):
+    per_request = range_offsets[1:] - range_offsets[:-1]
+    if (per_request < 0).any():
+        raise ValueError("drop_range_offsets does not cover drop_ranges")
+    if n and (token_counts.min() < 0 or token_counts.max() > np.iinfo(np.int32).max):
         raise ValueError("token_count exceeds the int32 Reposition limit")
     if not len(ranges):
         return
-    n = len(token_counts)
-    owner = np.repeat(np.arange(n), per_request)  # request of each range
     starts, ends = ranges[:, 0], ranges[:, 1]
+    if n == 1 and len(ranges) <= 256:  # one request, few ranges: a plain walk is cheapest
+        t, previous_end, dropped = int(token_counts[0]), -1, 0
+        for start, end in ranges.tolist():
+            if start < 0 or start >= end or end > t or start <= previous_end:
+                raise ValueError("Drop ranges must be ordered, disjoint, and already materialized")
+            previous_end, dropped = end, dropped + end - start
+        if reposition and t > 0 and dropped == t:
+            raise ValueError(f"Reposition at raw boundary {t - 1} has no active tokens.")
+        return
+    owner = np.repeat(np.arange(n), per_request)  # request of each range
     bad = (starts < 0) | (starts >= ends) | (ends > token_counts[owner])
     # a range that is not its request's first starts after the previous end
     bad[1:] |= (owner[1:] == owner[:-1]) & (starts[1:] <= ends[:-1])
@@ -271,27 +282,26 @@ class DropCompactor:
             views, used = self._layout(nreq, nranges)
             dev = {name: self._dev[off: off + count * (8 if dt == torch.int64 else 4)].view(dt)
                    for name, (off, count, dt) in views.items()}
+            host_views = {name: self._host_np[off: off + count * (8 if dt == torch.int64 else 4)]
+                          .view(np.int64 if dt == torch.int64 else np.int32)
+                          for name, (off, count, dt) in views.items()}
             prepared = dict(dev=dev, nreq=nreq, n_tiles=n_tiles, total=total, shared=shared,
                             reposition=bool(reposition), page_size=page_size, h2d_bytes=used,
-                            _views=views, _src=self._host[:used], _dst=self._dev[:used])
+                            _host_views=host_views, _src=self._host[:used],
+                            _dst=self._dev[:used])
             if len(self._prepared) > 64:
                 self._prepared.clear()
             self._prepared[key] = prepared
-        host = self._host_np
         self._copied.synchronize()
-        fields = {
-            "token_offsets": np.concatenate(([0], np.cumsum(token_counts))),
-            "row_ids": row_ids,
-            "tile_offsets": tile_offsets,
-            "range_offsets": range_offsets,
-            "shared_prefix": 0 if shared_prefix is None else shared_prefix,
-            "ranges": ranges,
-        }
-        for name, (off, count, dtype) in prepared["_views"].items():
-            if dtype == torch.int64:
-                host[off: off + 8 * count].view(np.int64)[:] = fields[name]
-            else:
-                host[off: off + 4 * count].view(np.int32)[:] = fields[name]
+        hv = prepared["_host_views"]
+        offsets = hv["token_offsets"]
+        offsets[0] = 0
+        np.cumsum(token_counts, out=offsets[1:])
+        hv["row_ids"][:] = row_ids
+        hv["tile_offsets"][:] = tile_offsets
+        hv["range_offsets"][:] = range_offsets
+        hv["shared_prefix"][:] = 0 if shared_prefix is None else shared_prefix
+        hv["ranges"][:] = ranges
         prepared["_dst"].copy_(prepared["_src"], non_blocking=True)
         self._copied.record(torch.cuda.current_stream(self.device))
         return prepared
