@@ -84,7 +84,8 @@ def reposition_kv_layers(
         position_pairs,
         cos_sin_cache,
     )
-    if not k_layout.is_cuda or any(t.device != k_layout.device for t in tensors):
+    index = k_layout.get_device()  # -1 for a CPU tensor
+    if index < 0 or any(t.get_device() != index for t in tensors):
         raise ValueError("Reposition tensors must be on one CUDA device")
     if k_layout.dtype not in (torch.float16, torch.bfloat16, torch.float32):
         raise ValueError("Context Reposition requires unquantized floating-point KV")
@@ -133,11 +134,11 @@ def reposition_kv_layers(
     if cos_sin_cache.dtype not in _native.DTYPE_CODE:
         raise ValueError("Reposition requires a native cos/sin cache matching rotary_dim")
     if error_flag is not None and (
-        error_flag.device != k_layout.device or error_flag.dtype != torch.int32
+        error_flag.get_device() != index or error_flag.dtype != torch.int32
     ):
         raise ValueError("error_flag must be an int32 tensor on the KV device")
     if count_device is not None and (
-        count_device.device != k_layout.device
+        count_device.get_device() != index
         or count_device.dtype != torch.int32
         or count_device.numel() < 1
     ):
@@ -171,7 +172,7 @@ def reposition_kv_layers(
         cos_sin_cache.shape[0],
         _native.ptr(error_flag),
         _native.REPOSITION_BULK_V if bulk_copy_v else 0,
-        _native.stream_of(k_layout.device),
+        _native.stream_of(index),
     )
     _native.check(status, "reposition_kv_layers")
 
