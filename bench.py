@@ -1186,6 +1186,9 @@ def bench_c5(dev, world, rank, warmup, steps, requests=8, layers=80, budget_gb=9
                      "peak": peak, "unit": "GB/s", "frac": round(achieved_min / peak, 4),
                      "peak_source": peak_kind, "algorithmic_bytes_per_launch": per_launch,
                      "ms_per_launch": round(launch_ms, 4),
+                     "traffic": ncu_traffic("c5", per_launch),
+                     "traffic_source": "profiles/reposition_c5.md (one-request, 10-layer cut, "
+                                       "traffic / algorithmic ratio)",
                      "reposition_ms_per_step": round(rep_ms, 4), "per": "GPU (slowest rank)"},
         "gpu_launches_per_step": 3 + len(chunks),
         "clocks": clock_info,
