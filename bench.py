@@ -334,6 +334,54 @@ def triton_versus_ours(ref, k_ptrs, v_ptrs, k0, v0, src, dst, pairs, cache, step
             "ours_gb_per_s": round(our_bytes / (t_ours / 1e3) / 1e9, 1)}
 
 
+def flashinfer_versus_ours(attn, q, k_pool, v_pool, indptr, indices, sinks, out, steps, stream):
+    """One decode layer through the reference's runtime path and through
+    ours, on the same pools, indices and sinks: FlashInfer's
+    BatchDecodeWithPagedKVCacheWrapper (page size 1, tensor-core variant, the
+    one SGLang takes for GQA groups of 4+ at 16-bit KV) returning the
+    log2-sum-exp, then the reference backend's in-place sink correction
+    o *= sigmoid(lse * ln 2 - sink) (akv/system/sglang.patch:1535-1551).
+    Planning is outside the timed calls on both sides.  Returns ms of each,
+    the ratio and the largest output difference; None when FlashInfer cannot
+    be imported or built here."""
+    try:
+        import flashinfer
+
+        bs, hq, d = q.shape
+        work = torch.zeros(128 << 20, dtype=torch.uint8, device=q.device)
+        wrapper = flashinfer.BatchDecodeWithPagedKVCacheWrapper(work, kv_layout="NHD",
+                                                               use_tensor_cores=True)
+        wrapper.plan(torch.from_numpy(np.asarray(indptr, np.int32)).to(q.device), indices,
+                     torch.ones(bs, dtype=torch.int32, device=q.device), hq, k_pool.shape[1],
+                     d, 1, pos_encoding_mode="NONE", q_data_type=torch.bfloat16,
+                     kv_data_type=torch.bfloat16, sm_scale=attn.sm_scale)
+        kv = (k_pool.unsqueeze(1), v_pool.unsqueeze(1))
+        fi_out = torch.empty_like(out)
+        fi_lse = torch.empty(bs, hq, dtype=torch.float32, device=q.device)
+
+        def theirs():
+            o, lse = wrapper.run(q, kv, out=fi_out, lse=fi_lse, return_lse=True)
+            o.mul_(torch.sigmoid(lse * 0.6931471805599453 - sinks.float()).unsqueeze(-1))
+
+        theirs()
+        torch.cuda.synchronize()
+    except Exception as exc:  # library missing or its JIT build failing
+        return {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:160]}"}
+
+    def ours():
+        attn.run(q, k_pool, v_pool, indices, sinks=sinks, out=out)
+
+    t_ref = time_launches(theirs, steps, stream)
+    t_ours = time_launches(ours, steps, stream)
+    theirs()
+    ours()
+    torch.cuda.synchronize()
+    diff = float((out.float() - fi_out.float()).abs().max())
+    return {"flashinfer": flashinfer.__version__, "variant": "tensor cores + sink correction",
+            "flashinfer_ms": round(t_ref, 4), "ours_ms": round(t_ours, 4),
+            "speedup": round(t_ref / t_ours, 2), "max_abs_diff": round(diff, 5)}
+
+
 def cpu_reference_step(prog, rows, layers, heads, dim, cache_np, sample, rng, threads):
     """One step of the reference's CPU path: its C++ event compiler
     (oracle/_ref) + numpy decode view + the reposition restatement over a
@@ -612,7 +660,7 @@ def run_ours(args):
         c5 = bench_c5(dev, world, rank, 2, max(3, min(args.steps, 10)))
         c3 = bench_c3(dev, world, rank, 3, max(5, min(args.steps, 20)))
         attention = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
-                                    max(5, min(args.steps // 20, 20)))
+                                    max(5, min(args.steps // 20, 20)), compare=world == 1)
         attention_paged = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                           max(5, min(args.steps // 20, 20)), layout="paged16")
         compiler = bench_compiler(dev, world, rank, 3, 20)
@@ -695,6 +743,9 @@ def run_ours(args):
             tri = sec.get("triton_reference")
             if isinstance(tri, dict) and "speedup" in tri:
                 item["vs_triton"] = tri["speedup"]
+            fi = (sec.get("reference_runtime_decode") or {}).get("full_layer")
+            if isinstance(fi, dict) and "speedup" in fi:
+                item["vs_flashinfer"] = fi["speedup"]
             kinds = sec.get("reposition_by_kind") or {}
             if "copy_on_write" in kinds:
                 item["cow_frac"] = kinds["copy_on_write"]["frac"]
@@ -712,7 +763,7 @@ def run_ours(args):
 
 
 def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1,
-                    layout="random"):
+                    layout="random", compare=False):
     """c4: batch 128, 64 query / 8 KV heads (split 8/N per rank), head_dim 64,
     bf16, lognormal KV lengths (median 8192, sigma 1.0, max 65536), 36 layers
     alternating sliding window 128 and full attention, per-head sinks.  One
@@ -724,7 +775,11 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1,
     at a random slot (a page_size 1 pool after much churn; the worst case
     for DRAM locality).  "paged16": a page_size 16 pool (the layout the
     paged Drop keeps): a request's keys fill its own 16-slot pages in order,
-    the pages at random places in the pool."""
+    the pages at random places in the pool.
+
+    ``compare``: also time the reference's runtime decode (FlashInfer plus
+    the sink correction) on one full and one sliding-window layer, outside
+    the timed step."""
     from akv_b200 import workloads
     from akv_b200.context_attention import DecodeAttention
 
@@ -799,6 +854,16 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1,
     step_bytes = (layers // 2) * (full_bytes + swa_bytes) * world
     peak, peak_kind = measured_peak()
     achieved = full_bytes / (full_ms / 1e3) / 1e9
+    runtime_ref = None
+    if compare and layers >= 2:
+        # The reference's runtime decode on one full and one sliding-window
+        # layer (outside the timed step).
+        runtime_ref = {
+            "full_layer": flashinfer_versus_ours(full, q, *pools[1], full_indptr, full_idx,
+                                                 sinks, out, max(steps, 10), stream),
+            "sliding_window_layer": flashinfer_versus_ours(swa, q, *pools[0], swa_indptr,
+                                                           swa_idx, sinks, out,
+                                                           max(steps, 10), stream)}
     del pools
     torch.cuda.empty_cache()
     return {
@@ -816,6 +881,7 @@ def bench_attention(dev, world, rank, warmup, steps, seed=0, layers=36, shard=1,
                      "algorithmic_bytes_per_launch": full_bytes,
                      "ms_per_launch": round(full_ms, 4)},
         "gpu_launches_per_step": layers + (layers // 2 if full.split else 0),
+        "reference_runtime_decode": runtime_ref,
     }
 
 
@@ -1949,7 +2015,7 @@ def main():
         torch.cuda.set_device(dev)
         res = bench_attention(dev, world, rank, max(3, args.warmup), max(3, args.steps // 20),
                               layers=args.layers or 36, shard=args.shard,
-                              layout=args.slot_layout)
+                              layout=args.slot_layout, compare=world == 1)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:

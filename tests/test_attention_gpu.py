@@ -2,11 +2,11 @@
 
 Checked against the float64 CPU oracle and a plain PyTorch fp32 reference
 of the same op, within the tolerance the path states for attention:
-atol 2e-3, rtol 1e-2 on the bf16 output.  (The reference's own decode
-kernels -- FlashInfer / FA3 -- are upstream and not vendored, so the
-attention oracle is a restatement of the math, not pinned to a reference
-run; the sink correction itself is pinned to the reference's
-flash_attention_with_sink by tests/test_oracle_golden.py.)
+atol 2e-3, rtol 1e-2 on the bf16 output.  The sink correction itself is
+pinned to the reference's flash_attention_with_sink by
+tests/test_oracle_golden.py, and the kernel to the reference's runtime
+decode path (FlashInfer plus the sink patch) by
+tests/test_flashinfer_pin_gpu.py.
 """
 
 import numpy as np
