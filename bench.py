@@ -298,6 +298,110 @@ def reference_triton():
     return mods
 
 
+def reference_context_metadata():
+    """The reference's ``ContextAttentionMetadata`` class (the native-plan
+    builder of its FlashInfer / FA3 context path, context_backend.py:171-222),
+    loaded unmodified from the reference package in baseline/_ref under
+    stand-in ``sglang`` package names that are removed again; None when the
+    package is not installed."""
+    import importlib.util
+    import types
+
+    sg = os.path.join(ROOT, "baseline", "_ref", "akv", "system", "sglang")
+    files = [("sglang.srt.context_system.request_storage", "srt/context_system/request_storage.py"),
+             ("sglang.srt.context_system.occurrence", "srt/context_system/occurrence.py"),
+             ("sglang.srt.layers.attention.context_backend",
+              "srt/layers/attention/context_backend.py")]
+    if not all(os.path.exists(os.path.join(sg, rel)) for _, rel in files):
+        return None
+    from akv_b200 import context_page_table, context_reposition
+
+    saved = {k: v for k, v in sys.modules.items() if k == "sglang" or k.startswith("sglang.")}
+    try:
+        for pkg in ("sglang", "sglang.kernels", "sglang.kernels.ops",
+                    "sglang.kernels.ops.attention", "sglang.srt", "sglang.srt.context_system",
+                    "sglang.srt.layers", "sglang.srt.layers.attention"):
+            sys.modules[pkg] = types.ModuleType(pkg)
+        sys.modules["sglang.kernels.ops.attention.context_reposition"] = context_reposition
+        sys.modules["sglang.kernels.ops.attention.context_page_table"] = context_page_table
+        mod = None
+        for name, rel in files:
+            spec = importlib.util.spec_from_file_location(name, os.path.join(sg, rel))
+            mod = importlib.util.module_from_spec(spec)
+            sys.modules[name] = mod
+            spec.loader.exec_module(mod)
+        return mod.ContextAttentionMetadata
+    except Exception:
+        return None
+    finally:
+        for k in [k for k in sys.modules if k == "sglang" or k.startswith("sglang.")]:
+            del sys.modules[k]
+        sys.modules.update(saved)
+
+
+def flashinfer_prefill_versus_ours(att, q, k_pool, v_pool, kv_idx, births, qo, kv, qpos, kpos,
+                                   window, sinks, out, steps, stream, run_ours):
+    """One context-prefill layer through the reference's runtime path and
+    through ours, same pools, slots, positions and sinks.  The reference
+    (sglang.patch:1303-1331): ``ContextAttentionMetadata.native_plan`` (its
+    own code, built once per forward, outside the timing) gives ragged
+    segments and the gathered key slots; per layer it gathers K and V at
+    those slots, runs FlashInfer's ragged prefill (backend "fa2", causal,
+    window_left) with the lse and applies the sink correction.  Returns ms
+    of that layer sequence, of the FlashInfer launch alone, of ours, and
+    the largest output difference; an "unavailable" note when the reference
+    package or FlashInfer is missing here."""
+    meta_cls = reference_context_metadata()
+    if meta_cls is None:
+        return {"unavailable": "the reference package is not installed in baseline/_ref"}
+    try:
+        import flashinfer
+
+        dev = q.device
+        hq, hkv, d = q.shape[1], k_pool.shape[1], q.shape[2]
+        t64 = lambda a: torch.as_tensor(np.asarray(a, np.int64), device=dev)  # noqa: E731
+        q_lengths = tuple(int(v) for v in np.diff(qo))
+        meta = meta_cls(t64(qo), t64(kv), kv_idx.long(), t64(qpos), t64(kpos), q_lengths,
+                        int(qo[-1]), max(q_lengths),
+                        (np.asarray(qo, np.int64), np.asarray(kv, np.int64), None,
+                         np.asarray(qpos, np.int64), np.asarray(kpos, np.int64)))
+        cpu_qo, cpu_kv, _, _, slots, _, _ = meta.native_plan(births.long(), window)
+        work = torch.zeros(128 << 20, dtype=torch.uint8, device=dev)
+        wrapper = flashinfer.BatchPrefillWithRaggedKVCacheWrapper(work, "NHD", backend="fa2")
+        wrapper.plan(cpu_qo, cpu_kv, hq, hkv, d, causal=True, window_left=window,
+                     logits_soft_cap=0.0, sm_scale=att.sm_scale, q_data_type=torch.bfloat16,
+                     kv_data_type=torch.bfloat16)
+        k_g, v_g = k_pool[slots], v_pool[slots]
+        fi_out = torch.empty_like(q)
+        fi_lse = torch.empty(q.shape[0], hq, dtype=torch.float32, device=dev)
+
+        def kernel_only():
+            wrapper.run(q, k_g, v_g, out=fi_out, lse=fi_lse, return_lse=True)
+
+        def theirs():
+            o, lse = wrapper.run(q, k_pool[slots], v_pool[slots], out=fi_out, lse=fi_lse,
+                                 return_lse=True)
+            o.mul_(torch.sigmoid(lse * 0.6931471805599453 - sinks.float()).unsqueeze(-1))
+
+        theirs()
+        torch.cuda.synchronize()
+    except Exception as exc:  # library missing or its JIT build failing
+        return {"unavailable": f"{type(exc).__name__}: {str(exc).splitlines()[0][:160]}"}
+    t_layer = time_launches(theirs, steps, stream)
+    t_kernel = time_launches(kernel_only, steps, stream)
+    t_ours = time_launches(run_ours, steps, stream)
+    theirs()
+    run_ours()
+    torch.cuda.synchronize()
+    diff = float((out.float() - fi_out.float()).abs().max())
+    return {"flashinfer": flashinfer.__version__, "segments": len(cpu_qo) - 1,
+            "gathered_keys": int(slots.numel()),
+            "flashinfer_layer_ms": round(t_layer, 4), "flashinfer_kernel_ms": round(t_kernel, 4),
+            "ours_ms": round(t_ours, 4), "speedup": round(t_layer / t_ours, 2),
+            "speedup_vs_kernel_alone": round(t_kernel / t_ours, 2),
+            "max_abs_diff": round(diff, 5)}
+
+
 def time_launches(fn, steps, stream, warmup=2):
     """Mean CUDA-event time of ``fn()`` over ``steps`` back-to-back calls
     (after ``warmup`` untimed calls), in ms."""
@@ -664,7 +768,7 @@ def run_ours(args):
         attention_paged = bench_attention(dev, world, rank, max(3, min(args.warmup, 5)),
                                           max(5, min(args.steps // 20, 20)), layout="paged16")
         compiler = bench_compiler(dev, world, rank, 3, 20)
-        prefill = bench_prefill(dev, world, rank, 3, 5)
+        prefill = bench_prefill(dev, world, rank, 3, 5, compare=world == 1)
         gather = bench_active_slots(dev, world, rank, 3, 20)
         occurrence = bench_occurrence(dev, world, rank, 3, 20)
         metadata = bench_decode_metadata(dev, world, rank, 3, 20)
@@ -743,7 +847,8 @@ def run_ours(args):
             tri = sec.get("triton_reference")
             if isinstance(tri, dict) and "speedup" in tri:
                 item["vs_triton"] = tri["speedup"]
-            fi = (sec.get("reference_runtime_decode") or {}).get("full_layer")
+            fi = (sec.get("reference_runtime_decode") or sec.get("reference_runtime_prefill")
+                  or {}).get("full_layer")
             if isinstance(fi, dict) and "speedup" in fi:
                 item["vs_flashinfer"] = fi["speedup"]
             kinds = sec.get("reposition_by_kind") or {}
@@ -1315,13 +1420,17 @@ def measured_tensor_peak():
         return 1590.0, "fallback"
 
 
-def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0, head_dim=64):
+def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0, head_dim=64,
+                  compare=False):
     """c4p: prefill of a new agent turn over the compacted cache -- 16
     requests, each a compacted prefix (lognormal length, median 8192, with
     position holes from dropped tokens) plus 1,024 new tokens; GPT-OSS-120B
     shape (64 query / 8 KV heads split 8/N per rank, head_dim 64), sinks,
     36 layers alternating sliding window 128 and full attention.  Tensor
-    bound: FLOPs = 4 * head_dim per visible (query, key, query head)."""
+    bound: FLOPs = 4 * head_dim per visible (query, key, query head).
+    ``compare``: also time the reference's runtime context prefill
+    (its native plan + FlashInfer ragged prefill + sink correction) on one
+    full and one sliding-window layer, outside the timed step."""
     from akv_b200 import workloads
     from akv_b200.context_prefill import ContextPrefillAttention
 
@@ -1385,6 +1494,17 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0,
     step_flops = (layers // 2) * 4.0 * d * hq * (full.visible + swa.visible) * world
     peak, peak_kind = measured_tensor_peak()
     achieved = full_flops / (full_ms / 1e3) / 1e12
+    runtime_ref = None
+    if compare and layers >= 2:
+        # The reference's runtime context prefill on one sliding-window and
+        # one full layer (outside the timed step).
+        runtime_ref = {}
+        for name, i, att, win in (("full_layer", 1, full, -1),
+                                  ("sliding_window_layer", 0, swa, window)):
+            kp, vp = pools[i % 2]
+            runtime_ref[name] = flashinfer_prefill_versus_ours(
+                att, q, kp, vp, kv_idx, births, qo, kv, qpos, kpos, win, sinks, out,
+                max(steps, 3), stream, lambda i=i: layer(i))
     cpu = None
     if rank == 0 and world == 1:
         # Torch fp32 on the host cores over a bounded sample (the reference
@@ -1430,6 +1550,7 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0,
                      "ms_per_launch": round(full_ms, 4)},
         "gpu_launches_per_step": layers,
         "cpu_baseline": cpu,
+        "reference_runtime_prefill": runtime_ref,
     }
 
 
@@ -1961,7 +2082,8 @@ def main():
         torch.cuda.set_device(dev)
         res = bench_prefill(dev, world, rank, max(3, min(args.warmup, 5)),
                             max(3, min(args.steps, 20)), layers=args.layers or 36,
-                            variant=args.variant, head_dim=args.head_dim)
+                            variant=args.variant, head_dim=args.head_dim,
+                            compare=world == 1)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:

@@ -1,4 +1,5 @@
-"""Decode attention pinned to the reference's runtime decode path.
+"""Decode and context-prefill attention pinned to the reference's runtime
+attention path (FlashInfer plus the sink correction of its SGLang patch).
 
 The reference serves decode through SGLang's FlashInfer backend with its
 sink patch (akv/system/sglang.patch:1535-1551): FlashInfer's
@@ -24,6 +25,10 @@ two decode variants, and the tolerances follow what each computes:
 
 This build's lse includes the sink, so it must equal
 logaddexp(lse_flashinfer * ln 2, sink).
+
+The prefill half (below) builds the reference's ragged segments with its
+own ``ContextAttentionMetadata.native_plan`` and runs FlashInfer's ragged
+prefill over them; its tolerances are stated there.
 """
 
 import math
@@ -162,3 +167,80 @@ def test_matches_flashinfer_on_a_dropped_cache_layout():
     torch.cuda.synchronize()
     assert int(attn.error_flag.item()) == 0
     torch.testing.assert_close(out.float(), ref_out.float(), atol=ATOL, rtol=RTOL)
+
+
+# Prefill: the reference's native FlashInfer path for context attention
+# (sglang.patch:1303-1331): ContextAttentionMetadata.native_plan
+# (context_backend.py:184-222) turns the occurrence metadata into ragged
+# segments -- one per query block, or one per query where a sliding window
+# meets position gaps -- and gathers their keys; FlashInfer's ragged prefill
+# (backend "fa2", causal, window_left = the window) runs over them, then the
+# same sink correction.  The plan is the reference's own code, loaded from
+# the reference package in baseline/_ref.
+
+PREFILL_CASES = [
+    # (prefix lens, query lens, hkv, d, window, sinks, gap): gap 1 keeps every
+    # request's positions consecutive (one ragged segment per request).
+    ([300, 0, 1000, 17], [40, 33, 1, 200], 8, 64, -1, True, 5),
+    ([300, 0, 1000, 17], [40, 33, 1, 200], 8, 64, 128, True, 5),
+    ([2000, 5], [300, 64], 8, 64, 7, False, 5),
+    ([64, 128], [16, 17], 2, 128, -1, True, 5),
+    ([900], [130], 1, 128, 100, True, 5),
+    ([5000, 3000, 1], [96, 250, 70], 8, 64, 128, True, 1),
+    ([3000, 700, 0], [130, 200, 33], 8, 128, 128, True, 1),
+    ([4000, 1500], [700, 300], 8, 64, -1, True, 1),
+]
+
+
+def _flashinfer_prefill(reference_backend, x, hkv, d, window, sinks, scale):
+    dev = x["q"].device
+    hq = 8 * hkv
+    t64 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int64)).to(dev)  # noqa: E731
+    cpu_fields = (x["qo"], x["kv"], None, x["qpos"].astype(np.int64),
+                  x["kpos"].astype(np.int64))
+    q_lengths = tuple(int(v) for v in np.diff(x["qo"]))
+    metadata = reference_backend.ContextAttentionMetadata(
+        t64(x["qo"]), t64(x["kv"]), t64(x["kv_idx"]), t64(x["qpos"]), t64(x["kpos"]),
+        q_lengths, int(x["qo"][-1]), max(q_lengths), cpu_fields)
+    cpu_qo, cpu_kv, _, _, slots, _, _ = metadata.native_plan(t64(x["births"]), window)
+    work = torch.zeros(128 << 20, dtype=torch.uint8, device=dev)
+    wrapper = flashinfer.BatchPrefillWithRaggedKVCacheWrapper(work, "NHD", backend="fa2")
+    wrapper.plan(cpu_qo, cpu_kv, hq, hkv, d, causal=True, window_left=window,
+                 logits_soft_cap=0.0, sm_scale=scale, q_data_type=torch.bfloat16,
+                 kv_data_type=torch.bfloat16)
+    o, lse = wrapper.run(x["q"], x["k_pool"][slots], x["v_pool"][slots], return_lse=True)
+    if sinks is not None:
+        o.mul_(torch.sigmoid(lse * LN2 - sinks.float()).unsqueeze(-1))
+    return o, lse
+
+
+@pytest.mark.parametrize("case", range(len(PREFILL_CASES)))
+def test_prefill_matches_flashinfer_through_the_reference_native_plan(reference_backend, case):
+    """FlashInfer's fa2 prefill rounds P to bf16 for its PV product; this
+    build's prefill kernels carry P as a bf16 hi + lo pair (P to about 16
+    bits).  So this build's output is held to the path's tolerance against
+    the exact fp32 attention, and to that tolerance plus the bound of
+    FlashInfer's P rounding, 2^-8 * sum_i p_i |v_i| per element, against the
+    reference's runtime output."""
+    from test_prefill_gpu import make_batch, run_ours, torch_reference
+
+    prefix, queries, hkv, d, window, use_sinks, gap = PREFILL_CASES[case]
+    rng = np.random.default_rng(100 + case)
+    x = make_batch(rng, prefix, queries, hkv, d, gap=gap)
+    sinks = (2.0 * torch.randn(8 * hkv, device="cuda")) if use_sinks else None
+    scale = 1.0 / math.sqrt(d)
+    lse = torch.empty(x["q"].shape[0], 8 * hkv, device="cuda")
+    out, _ = run_ours(x, hkv, d, window, sinks, lse=lse)
+    ref, ref_lse2 = _flashinfer_prefill(reference_backend, x, hkv, d, window, sinks, scale)
+    torch.cuda.synchronize()
+    exact = torch_reference(x, window, sinks, scale)
+    torch.testing.assert_close(out.float(), exact, atol=ATOL, rtol=RTOL)
+    p_abs_v = torch_reference(dict(x, v_pool=x["v_pool"].abs()), window, sinks, scale)
+    bound = ATOL + RTOL * ref.float().abs() + BF16_ROUND * p_abs_v
+    excess = (out.float() - ref.float()).abs() - bound
+    assert float(excess.max()) <= 0.0, f"max excess {float(excess.max()):.3g}"
+    expect_lse = ref_lse2.float() * LN2
+    if use_sinks:
+        expect_lse = torch.logaddexp(expect_lse, sinks.float()[None, :])
+    # FlashInfer's ragged prefill also sums bf16-rounded P into its denominator.
+    torch.testing.assert_close(lse, expect_lse, atol=3.9e-3, rtol=0)

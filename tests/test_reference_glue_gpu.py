@@ -7,7 +7,8 @@ The reference imports its kernels lazily under
 ``akv_b200.context_reposition`` / ``akv_b200.context_page_table`` and the
 reference's unmodified ``context_backend.py`` (with its ``occurrence.py``
 and ``request_storage.py``) is loaded from the reference package installed
-in baseline/_ref; the test is skipped when it is not installed.  Then the
+in baseline/_ref (the ``reference_backend`` fixture of conftest.py); the test
+is skipped when it is not installed.  Then the
 reference's own classes run on the GPU:
 
 * ``ContextModelBinding.reposition_existing`` (:432-472): layers grouped by
@@ -21,53 +22,15 @@ K/V are compared bit for bit with the oracle's reposition, the page tables
 with a numpy statement of context_page_table.py.
 """
 
-import importlib.util
-import os
-import sys
-import types
 from types import SimpleNamespace
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import ROOT
 
 pytestmark = pytest.mark.gpu
 
-SG = os.path.join(ROOT, "baseline", "_ref", "akv", "system", "sglang")
-
-
-@pytest.fixture(scope="module")
-def backend():
-    path = os.path.join(SG, "srt", "layers", "attention", "context_backend.py")
-    if not os.path.exists(path):
-        pytest.skip("the reference package is not installed in baseline/_ref")
-    from akv_b200 import context_page_table, context_reposition
-
-    saved = {k: v for k, v in sys.modules.items() if k == "sglang" or k.startswith("sglang.")}
-    for pkg in ("sglang", "sglang.kernels", "sglang.kernels.ops", "sglang.kernels.ops.attention",
-                "sglang.srt", "sglang.srt.context_system", "sglang.srt.layers",
-                "sglang.srt.layers.attention"):
-        sys.modules[pkg] = types.ModuleType(pkg)
-    sys.modules["sglang.kernels.ops.attention.context_reposition"] = context_reposition
-    sys.modules["sglang.kernels.ops.attention.context_page_table"] = context_page_table
-
-    def load(name, rel):
-        spec = importlib.util.spec_from_file_location(name, os.path.join(SG, rel))
-        mod = importlib.util.module_from_spec(spec)
-        sys.modules[name] = mod
-        spec.loader.exec_module(mod)
-        return mod
-
-    load("sglang.srt.context_system.request_storage", "srt/context_system/request_storage.py")
-    load("sglang.srt.context_system.occurrence", "srt/context_system/occurrence.py")
-    mod = load("sglang.srt.layers.attention.context_backend",
-               "srt/layers/attention/context_backend.py")
-    yield mod
-    for k in [k for k in sys.modules if k == "sglang" or k.startswith("sglang.")]:
-        del sys.modules[k]
-    sys.modules.update(saved)
 
 
 class Translator:
@@ -130,13 +93,13 @@ def _compare(kv, ks, vs):
 
 
 @pytest.mark.parametrize("rotary", [64, 32])
-def test_reposition_existing_through_the_reference_binding(backend, rotary):
+def test_reposition_existing_through_the_reference_binding(reference_backend, rotary):
     from akv_b200.rope import yarn_cos_sin_cache
 
     dev = torch.device("cuda")
     cache = yarn_cos_sin_cache(8192, rotary, 150000.0, 32.0, 4096).to(dev)
     model, pool, kv = _model(4, 6000, 8, 64, rotary, cache, dev, seed=3)
-    binding = backend.ContextModelBinding(model, pool, Translator(), page_size=1)
+    binding = reference_backend.ContextModelBinding(model, pool, Translator(), page_size=1)
     src, dst, pairs = _transitions(np.random.default_rng(1), 1500, 6000, 8000)
     ks, vs = _expected(kv, src, dst, pairs, cache, rotary)
     binding.reposition_existing(torch.from_numpy(src.astype(np.int64)).to(dev),
@@ -146,13 +109,13 @@ def test_reposition_existing_through_the_reference_binding(backend, rotary):
     _compare(kv, ks, vs)
 
 
-def test_bind_and_layer_copies_through_the_reference_binding(backend):
+def test_bind_and_layer_copies_through_the_reference_binding(reference_backend):
     from akv_b200.rope import yarn_cos_sin_cache
 
     dev = torch.device("cuda")
     cache = yarn_cos_sin_cache(8192, 64, 150000.0, 32.0, 4096).to(dev)
     model, pool, kv = _model(3, 5000, 8, 64, 64, cache, dev, seed=4)
-    binding = backend.ContextModelBinding(model, pool, Translator(), page_size=1)
+    binding = reference_backend.ContextModelBinding(model, pool, Translator(), page_size=1)
     src, dst, pairs = _transitions(np.random.default_rng(2), 900, 5000, 8000)
     ks, vs = _expected(kv, src, dst, pairs, cache, 64)
     inputs = SimpleNamespace(
@@ -194,7 +157,7 @@ def _decode_expect(layouts, table, rows, generated, window=None):
     return out, np.asarray(lens)
 
 
-def test_decode_registry_through_the_reference_code(backend):
+def test_decode_registry_through_the_reference_code(reference_backend):
     from oracle import oracle
 
     dev = torch.device("cuda")
@@ -205,7 +168,7 @@ def test_decode_registry_through_the_reference_code(backend):
     width = int((prompts + generated).max())
     table_np = rng.integers(1, 1 << 20, size=(batch + 3, width)).astype(np.int32)
     translator = Translator(torch.from_numpy(table_np).to(dev))
-    registry = backend.ContextDecodeRegistry(translator, SimpleNamespace())
+    registry = reference_backend.ContextDecodeRegistry(translator, SimpleNamespace())
     reqs, layouts, raw_lengths = [], [], []
     for b in range(batch):
         t = int(prompts[b])
