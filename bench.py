@@ -144,6 +144,32 @@ def algorithmic_bytes(prog, heads_local, layers, dim, rot, elem=2):
     return reposition, drop
 
 
+NOMINAL_PEAKS = {"GB/s": 8000.0, "TFLOP/s": 2250.0}  # B200 HBM3e; dense bf16
+
+
+def with_nominal_fractions(obj):
+    """Every ``roofline`` object in ``obj`` also gets its achieved figure as
+    a fraction of the B200's nominal peak (8 TB/s HBM3e, 2.25 PFLOP/s dense
+    bf16) beside the fraction of the measured one."""
+    if isinstance(obj, dict):
+        roof = obj.get("roofline")
+        if isinstance(roof, dict) and roof.get("unit") in NOMINAL_PEAKS and \
+                isinstance(roof.get("achieved"), (int, float)):
+            roof["nominal_peak"] = NOMINAL_PEAKS[roof["unit"]]
+            roof["frac_of_nominal"] = round(roof["achieved"] / roof["nominal_peak"], 4)
+        for v in obj.values():
+            with_nominal_fractions(v)
+    elif isinstance(obj, list):
+        for v in obj:
+            with_nominal_fractions(v)
+    return obj
+
+
+def emit(line):
+    """Print one result line (JSON) with the nominal-peak fractions added."""
+    print(json.dumps(with_nominal_fractions(line)), flush=True)
+
+
 def measured_peak():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -588,7 +614,7 @@ def run_reference(args):
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -859,7 +885,7 @@ def run_ours(args):
                     item["cow_vs_triton"] = tri["speedup"]
             summary[name] = item
         line["summary"] = summary
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
 
@@ -2085,7 +2111,7 @@ def main():
                             variant=args.variant, head_dim=args.head_dim,
                             compare=world == 1)
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            emit(res)
         if world > 1:
             import torch.distributed as dist
 
@@ -2098,7 +2124,7 @@ def main():
         torch.cuda.set_device(dev)
         res = bench_compiler(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            emit(res)
         if world > 1:
             import torch.distributed as dist
 
@@ -2111,7 +2137,7 @@ def main():
         fn = bench_decode_metadata if args.workload == "c4m" else bench_active_slots
         res = fn(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            emit(res)
         if world > 1:
             import torch.distributed as dist
 
@@ -2124,7 +2150,7 @@ def main():
         torch.cuda.set_device(dev)
         res = bench_occurrence(dev, world, rank, max(3, args.warmup), max(3, min(args.steps, 50)))
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            emit(res)
         if world > 1:
             import torch.distributed as dist
 
@@ -2139,7 +2165,7 @@ def main():
                               layers=args.layers or 36, shard=args.shard,
                               layout=args.slot_layout, compare=world == 1)
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            emit(res)
         if world > 1:
             import torch.distributed as dist
 
@@ -2154,7 +2180,7 @@ def main():
         res = bench_c5(dev, world, rank, max(2, args.warmup), max(3, min(args.steps, 30)),
                        requests=args.requests or 8, layers=args.layers or 80)
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            emit(res)
         if world > 1:
             import torch.distributed as dist
 
@@ -2170,7 +2196,7 @@ def main():
                        page_sizes=(args.page_size,), layers=args.layers or 36, cpu=False,
                        requests=args.requests or 64, shard=args.shard)
         if rank == 0:
-            print(json.dumps(res[args.page_size]), flush=True)
+            emit(res[args.page_size])
         if world > 1:
             import torch.distributed as dist
 
