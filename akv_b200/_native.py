@@ -74,6 +74,7 @@ SIGNATURES = {
         _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
     ],
     "akv_occurrence_advance_indices": [_P, _P],
+    "akv_drop_read_view": [_P, _P, _P, _I64, _P, _P, _I32, _P, _P],
     "akv_drop_compact_static_max_requests": [],
     "akv_drop_compact_static_max_tiles": [],
     "akv_drop_compact_static": [

@@ -27,6 +27,7 @@ host-to-device copy.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -89,11 +90,40 @@ class DropResult:
     freed_slots: torch.Tensor
     totals: torch.Tensor
     status: torch.Tensor
+    kept_host: int | None = None  # kept tokens, when the host knows them
 
     @property
     def transition_count(self) -> torch.Tensor:
         """One-element int32 device view: ``count_device`` for reposition."""
         return self.totals[1:2]
+
+    def read_view(self, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Copy the decode view to host memory in one library call
+        (``akv_drop_read_view``), stream-ordered after the call: one int32
+        vector ``[raw_indices(kept) | active_positions(kept) |
+        active_offsets(n + 1) | next_position(n) | totals(4) | status]`` for
+        n requests, into ``out`` (pinned, for an asynchronous copy) or a new
+        pinned tensor.  ``kept`` is the host's count for a validated program
+        (``kept_host``), else every token of the call (entries past
+        ``totals[0]`` are then unused).  ``stream``: a torch stream (default:
+        the current one); record an event on it and wait before reading
+        ``out``."""
+        n = len(self.next_position)
+        kept = self.kept_host if self.kept_host is not None else len(self.keep_mask)
+        size = 2 * kept + 2 * n + 6
+        if out is None:
+            out = torch.empty(size, dtype=torch.int32, pin_memory=True)
+        elif out.dtype != torch.int32 or out.device.type != "cpu" or out.numel() < size or \
+                not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous host int32 tensor of {size} elements")
+        handle = _native.stream_of(self.totals.device) if stream is None else \
+            ctypes.c_void_p(stream.cuda_stream)
+        status = _native.lib.akv_drop_read_view(
+            out.data_ptr(), _native.ptr(self.raw_indices), _native.ptr(self.active_positions),
+            kept, _native.ptr(self.active_offsets), _native.ptr(self.next_position), n,
+            _native.ptr(self.totals), handle)
+        _native.check(status, "drop_read_view")
+        return out
 
     def check(self) -> None:
         """Read the device status (synchronises) and raise on failure."""
@@ -292,6 +322,9 @@ class DropCompactor:
             if len(self._prepared) > 64:
                 self._prepared.clear()
             self._prepared[key] = prepared
+        # Kept tokens: known on the host once the ranges are validated
+        # (half-open, disjoint).
+        prepared["kept"] = total - int((ranges[1::2] - ranges[0::2]).sum()) if validate else None
         self._copied.synchronize()
         hv = prepared["_host_views"]
         offsets = hv["token_offsets"]
@@ -320,6 +353,7 @@ class DropCompactor:
             cached = (key,) + self._launch_args(prepared, req_to_token, ring)
             prepared["_launch"] = cached
         _, args, result = cached
+        result.kept_host = prepared.get("kept")
         page_size = prepared.get("page_size", 1)
         if page_size == 1:
             status = _native.lib.akv_drop_compact(*args, _native.stream_of(self.device))
@@ -407,7 +441,7 @@ def launch_static(compactor, prepared, req_to_token, ring) -> DropResult:
         transition_destination=c.transition_destination,
         transition_pairs=c.transition_pairs, transition_raw=c.transition_raw,
         freed_offsets=off3[2, : nreq + 1], freed_slots=c.freed_slots,
-        totals=c.counters[:4], status=c.counters[4:5],
+        totals=c.counters[:4], status=c.counters[4:5], kept_host=prepared.get("kept"),
     )
 
 

@@ -775,3 +775,33 @@ extern "C" int akv_drop_compact_static(
                           transition_raw, freed_offsets, freed_slots, totals, status, scratch,
                           stream);
 }
+
+// The decode view of one call, read back to host memory: five
+// stream-ordered device-to-host copies into one int32 vector, so a serving
+// loop reads a Drop's result with one library call (no launch, no sync).
+extern "C" int akv_drop_read_view(int32_t* host_out, const int32_t* raw_indices,
+                                  const int32_t* active_positions, int64_t kept,
+                                  const int32_t* active_offsets, const int32_t* next_position,
+                                  int32_t n_requests, const int32_t* counters, void* stream) {
+  if (host_out == nullptr || kept < 0 || n_requests < 0 || active_offsets == nullptr ||
+      counters == nullptr || (kept > 0 && (raw_indices == nullptr || active_positions == nullptr)) ||
+      (n_requests > 0 && next_position == nullptr))
+    return AKV_ERR_INVALID;
+  const auto s = static_cast<cudaStream_t>(stream);
+  const struct {
+    const int32_t* src;
+    int64_t count;
+  } parts[] = {{raw_indices, kept},
+               {active_positions, kept},
+               {active_offsets, (int64_t)n_requests + 1},
+               {next_position, n_requests},
+               {counters, 5}};
+  int32_t* dst = host_out;
+  for (const auto& part : parts) {
+    if (part.count > 0 && cudaMemcpyAsync(dst, part.src, (size_t)part.count * sizeof(int32_t),
+                                          cudaMemcpyDeviceToHost, s) != cudaSuccess)
+      return AKV_ERR_CUDA;
+    dst += part.count;
+  }
+  return AKV_OK;
+}

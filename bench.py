@@ -711,7 +711,8 @@ def run_ours(args):
     # the GPU; every step still pays its own H2D and D2H.  The decode view
     # is final once the drop kernels end, so its read-back runs on a second
     # stream beside the reposition launch; the next step's drop waits for it.
-    n_out = 2 * kept + prog.requests + 5
+    # [raw(kept) | positions(kept) | offsets(n + 1) | next(n) | totals(4) | status]
+    n_out = 2 * kept + 2 * prog.requests + 6
     a_host = [torch.empty(n_out, dtype=torch.int32, pin_memory=True) for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
     viewed = torch.cuda.Event()
@@ -739,14 +740,9 @@ def run_ours(args):
         reposition_kv_layers(k_ptrs, v_ptrs, k_pools[0], v_pools[0], res.transition_source,
                              res.transition_destination, res.transition_pairs, cache,
                              count_device=res.transition_count)
-        buf = a_host[i % 2]
         readback.wait_event(viewed)
-        with torch.cuda.stream(readback):
-            buf[:kept].copy_(res.raw_indices[:kept], non_blocking=True)
-            buf[kept: 2 * kept].copy_(res.active_positions[:kept], non_blocking=True)
-            buf[2 * kept: 2 * kept + prog.requests].copy_(res.next_position, non_blocking=True)
-            buf[2 * kept + prog.requests:].copy_(comp.counters, non_blocking=True)
-            done[i % 2].record(readback)
+        res.read_view(a_host[i % 2], stream=readback)  # one library call, five copies
+        done[i % 2].record(readback)
         if i > 0:
             done[(i - 1) % 2].synchronize()
             check(a_host[(i - 1) % 2])
@@ -1207,7 +1203,8 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
         # H2D copy + launches, and the decode view read back every step.  As
         # in a serving loop (and the c2 e2e), the host issues step i + 1
         # before it waits for the read-back of step i (two pinned buffers).
-        views = [torch.empty(2 * kept + 1, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        n_view = 2 * kept + 2 * prog.requests + 6  # the layout of DropResult.read_view
+        views = [torch.empty(n_view, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         read = [torch.cuda.Event() for _ in range(2)]
         dist_barrier(world)
         torch.cuda.synchronize()
@@ -1222,10 +1219,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                                  r2.transition_destination, r2.transition_pairs, cache,
                                  count_device=r2.transition_count, page_size=ps,
                                  bulk_copy_v=bulk_v)
-            view = views[i % 2]
-            view[:kept].copy_(r2.raw_indices[:kept], non_blocking=True)
-            view[kept: 2 * kept].copy_(r2.active_positions[:kept], non_blocking=True)
-            view[2 * kept:].copy_(r2.status, non_blocking=True)
+            r2.read_view(views[i % 2])
             read[i % 2].record(stream)
             if i > 0:
                 read[(i - 1) % 2].synchronize()
@@ -1254,7 +1248,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
                        "restore": "rows + ring head restored on the device each step"},
             "e2e": {"value": round(step_bytes * e2e_steps / e2e_s / 1e9, 2), "unit": UNIT,
                     "h2d_bytes_per_step": prepared["h2d_bytes"],
-                    "d2h_bytes_per_step": 8 * kept + 4},
+                    "d2h_bytes_per_step": 4 * n_view},
             "breakdown_ms": {"drop_compact": round(drop_ms, 4), "reposition": round(rep_ms, 4)},
             "reposition_by_kind": split,
             "roofline": {"bound": "hbm", "kernel": "reposition_kernel",

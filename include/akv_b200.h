@@ -252,6 +252,24 @@ int akv_drop_compact_static(
     int32_t* freed_slots, int32_t* totals, int32_t* status, void* stream);
 
 /*
+ * The decode view of one akv_drop_compact (or _paged / _static) call read
+ * back to host memory, stream-ordered after it on `stream`: one int32 vector
+ *   [raw_indices(kept) | active_positions(kept) | active_offsets(n_requests + 1)
+ *    | next_position(n_requests) | totals(4) | status]
+ * at host_out (pinned memory makes the copies asynchronous).  `counters` is
+ * the call's totals pointer, with the status word right after it.  This is
+ * the host-side result the reference builds with
+ * ContextDecodeLayout.from_layout (srt/context_system/occurrence.py:47-66),
+ * here for a layout computed on the device.  `kept` is the host's count of
+ * kept tokens (known from a validated program) or any larger value up to the
+ * buffers' capacity.  Copies only: no launch, no synchronisation.
+ */
+int akv_drop_read_view(int32_t* host_out, const int32_t* raw_indices,
+                       const int32_t* active_positions, int64_t kept,
+                       const int32_t* active_offsets, const int32_t* next_position,
+                       int32_t n_requests, const int32_t* counters, void* stream);
+
+/*
  * General event compiler for a batch of request programs.  Replaces
  * compile_radix_reposition_layout and count_radix_reposition_transitions
  * (akv/system/sglang/kernels/ops/attention/context_plan.py:80-532) as called

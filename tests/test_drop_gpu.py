@@ -312,3 +312,56 @@ def test_same_shape_programs_restage_through_one_compactor():
         n = int(res.totals[1].item())
         np.testing.assert_array_equal(res.transition_source[:n].cpu().numpy(), want["src"])
     assert handles[0] is handles[1] is handles[2]
+
+
+@pytest.mark.parametrize("validate", [True, False])
+def test_read_view_copies_the_decode_view_in_one_call(validate):
+    """``DropResult.read_view`` (C ABI akv_drop_read_view): the host vector
+    holds the device's raw indices and positions (the first ``kept``, the
+    host's count for a validated program, else every token), the CSR
+    offsets, next positions, totals and status, in that order, and the
+    oracle's decode view; the copies run on the stream given."""
+    from oracle import oracle
+    from akv_b200 import workloads
+    from akv_b200.context_drop import DropCompactor, FreeSlotRing
+
+    dev = torch.device("cuda")
+    prog = workloads.c3_program(requests=6, max_len=7000, seed=9)
+    rows, nslots = workloads.slot_rows(np.random.default_rng(9), prog)
+    free = np.arange(nslots, nslots + int(prog.shared_prefix.sum()) + 8, dtype=np.int32)
+    nreq = prog.requests
+    table = np.zeros((nreq + 1, int(prog.token_counts.max())), np.int32)
+    for r in range(nreq):
+        table[r + 1, : len(rows[r])] = rows[r]
+    rtt = torch.from_numpy(table).to(dev)
+    ring = FreeSlotRing(torch.from_numpy(free), capacity=len(free) + prog.total_tokens + 1,
+                        device=dev)
+    comp = DropCompactor(prog.total_tokens, nreq, len(prog.ranges) // 2, dev)
+    res = comp.run(prog.token_counts, prog.range_offsets, prog.ranges, rtt,
+                   np.arange(1, nreq + 1), ring, shared_prefix=prog.shared_prefix,
+                   validate=validate)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    out = res.read_view(stream=side)
+    side.synchronize()
+    want = oracle.drop_compact(prog.token_counts, prog.range_offsets, prog.ranges, rows,
+                               shared_prefix=prog.shared_prefix, free_ring=free, free_head=0,
+                               free_tail=len(free))
+    kept = sum(len(x) for x in want["raw_indices"])
+    assert res.kept_host == (kept if validate else None)
+    k = kept if validate else prog.total_tokens
+    host = out.numpy()
+    assert len(host) == 2 * k + 2 * nreq + 6
+    np.testing.assert_array_equal(host[:kept], np.concatenate(want["raw_indices"]))
+    np.testing.assert_array_equal(host[k: k + kept], np.concatenate(want["active_positions"]))
+    o = 2 * k
+    np.testing.assert_array_equal(host[o: o + nreq + 1], res.active_offsets.cpu().numpy())
+    np.testing.assert_array_equal(np.diff(host[o: o + nreq + 1]),
+                                  [len(x) for x in want["raw_indices"]])
+    o += nreq + 1
+    np.testing.assert_array_equal(host[o: o + nreq], want["next_position"])
+    o += nreq
+    np.testing.assert_array_equal(host[o: o + 4], res.totals.cpu().numpy())
+    assert host[o] == kept and host[o + 4] == 0
+    with pytest.raises(ValueError):
+        res.read_view(out=torch.empty(3, dtype=torch.int32))
