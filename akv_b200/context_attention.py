@@ -74,11 +74,13 @@ class DecodeAttention:
         """Work list from host-known CSR offsets of the key lists.
 
         With ``items_per_cta`` (default ``ITEMS_PER_CTA``) the launch is
-        persistent: ``ctas`` CTAs (all that fit on the GPU at once) each run a
-        list of items, the key ranges cut ``items_per_cta`` times finer than
-        one range per CTA and dealt to the CTAs longest first in a
-        back-and-forth order, so that every CTA ends at about the same time.
-        ``items_per_cta=0`` launches one CTA per item instead."""
+        persistent when there are more items than resident CTAs: ``ctas``
+        CTAs (all that fit on the GPU at once) each run a list of items, the
+        key ranges cut ``items_per_cta`` times finer than one range per CTA
+        and dealt to the CTAs longest first in a back-and-forth order, so
+        that every CTA ends at about the same time.  ``items_per_cta=0`` (or
+        a work list no longer than the resident CTAs) launches one CTA per
+        item instead."""
         indptr = np.asarray(kv_indptr_host, np.int64)
         lengths = np.diff(indptr)
         batch = len(lengths)
@@ -110,7 +112,11 @@ class DecodeAttention:
         work = np.asarray(items, np.int32).reshape(-1, 4)
         n = len(work)
         ctas = 0
-        if per_cta > 0 and n > 0:
+        # With no more items than resident CTAs each item gets a CTA of its
+        # own either way; the plain launch then skips the per-CTA list (one
+        # dependent load: a sliding-window layer of the c4 batch, 128 items,
+        # 16.5 instead of 19.6 us).
+        if per_cta > 0 and n > self.ctas:
             ctas = min(self.ctas, n)
             i = np.arange(n)
             lap, pos = i // ctas, i % ctas

@@ -43,7 +43,7 @@ def torch_reference(q, k_pool, v_pool, indptr, indices, sinks, scale):
     return out, lse
 
 
-def _case(lengths, hkv, d, sinks, seed=0, chunk=None, slots=None):
+def _case(lengths, hkv, d, sinks, seed=0, chunk=None, slots=None, ctas=None):
     from akv_b200.context_attention import DecodeAttention
 
     dev = torch.device("cuda")
@@ -60,7 +60,8 @@ def _case(lengths, hkv, d, sinks, seed=0, chunk=None, slots=None):
     indices = rng.integers(1, slots, size=total).astype(np.int32)
     sk = torch.randn(hq, generator=g) if sinks else None
     scale = 1.0 / np.sqrt(d)
-    attn = DecodeAttention(hq, hkv, d, bs, dev)
+    attn = DecodeAttention(hq, hkv, d, bs, dev, ctas=ctas,
+                           max_items=4096 if ctas is not None else None)
     lse = torch.empty(bs, hq, device=dev)
     out = attn.plan(indptr, chunk=chunk).run(
         q.to(dev), k_pool.to(dev), v_pool.to(dev), torch.from_numpy(indices).to(dev),
@@ -85,11 +86,13 @@ def test_decode_attention_matches_torch_fp32(hkv, d, sinks):
     _case(lengths, hkv, d, sinks, seed=hkv * 10 + d)
 
 
+@pytest.mark.parametrize("ctas", [None, 3])
 @pytest.mark.parametrize("chunk", [32, 96, 1024])
-def test_decode_attention_split_and_combine(chunk):
-    """Requests split into several key ranges combine to the same result."""
+def test_decode_attention_split_and_combine(chunk, ctas):
+    """Requests split into several key ranges combine to the same result,
+    with one CTA per range and with 3 persistent CTAs running lists."""
     lengths = [3000, 1, 33, 700, 0, 4097]
-    _case(lengths, 8, 64, True, seed=chunk, chunk=chunk)
+    _case(lengths, 8, 64, True, seed=chunk, chunk=chunk, ctas=ctas)
 
 
 def test_decode_attention_matches_float64_oracle():
