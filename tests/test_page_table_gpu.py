@@ -226,3 +226,58 @@ def test_decode_indices_padded_table_matches_oracle(window, batch, median):
         HAS_START=starts is not None)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(out.cpu().numpy(), want.astype(np.int32))
+
+
+@pytest.mark.parametrize("window", [None, 128])
+def test_decode_metadata_replays_from_a_cuda_graph(window):
+    """The reference keeps its decode registry capture-stable so a decode
+    step's metadata launches can live in a CUDA graph
+    (context_backend.py:667-672): here the metadata launches of one step
+    are captured once, then the sequence lengths grow in place between
+    replays, as decode steps do; every replay equals the oracle."""
+    from oracle import oracle
+    from akv_b200.context_page_table import build_decode_metadata, context_window_lengths
+
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(21)
+    host, reg, table, rows, seq = _c4_registry(dev, rng, batch=96, median=1500)
+    steps = 4
+    # ordinary requests read their table row directly: keep them inside it
+    seq = np.minimum(seq, table.shape[1] - steps - 1)
+    cap = int((seq + steps).sum())
+    d_table = torch.from_numpy(table).to(dev)
+    d_rows = torch.from_numpy(rows).to(dev)
+    d_seq = torch.from_numpy(seq).to(dev)
+    kv_indptr = torch.empty(len(seq) + 1, dtype=torch.int32, device=dev)
+    kv_indices = torch.full((cap,), -7, dtype=torch.int32, device=dev)
+    lens = torch.empty(len(seq), dtype=torch.int64, device=dev)
+    starts = torch.empty(len(seq), dtype=torch.int64, device=dev)
+    wl = torch.empty(len(seq), dtype=torch.int64, device=dev)
+
+    def step():
+        build_decode_metadata(reg.rows, d_table, d_rows, d_seq, kv_indptr, kv_indices,
+                              window=window, lengths_out=lens, starts_out=starts)
+        if window is not None:
+            context_window_lengths[(len(seq),)](reg.rows, d_rows, d_seq, wl, window)
+
+    step()  # first launch outside the capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(steps):
+        seq = seq + 1
+        d_seq.copy_(torch.from_numpy(seq))
+        graph.replay()
+        torch.cuda.synchronize()
+        lengths = seq if window is None else oracle.window_lengths(host, rows, seq, window)
+        indptr = np.concatenate(([0], np.cumsum(lengths)))
+        want = oracle.decode_indices(host, table, rows, lengths, indptr, int(indptr[-1]),
+                                     starts=None if window is None else seq - lengths)
+        np.testing.assert_array_equal(kv_indptr.cpu().numpy(), indptr)
+        np.testing.assert_array_equal(kv_indices[: int(indptr[-1])].cpu().numpy(),
+                                      want.astype(np.int32))
+        if window is not None:
+            np.testing.assert_array_equal(lens.cpu().numpy(), lengths)
+            np.testing.assert_array_equal(wl.cpu().numpy(), lengths)
+    del graph
