@@ -328,8 +328,8 @@ def reference_context_metadata():
     """The reference's ``ContextAttentionMetadata`` class (the native-plan
     builder of its FlashInfer / FA3 context path, context_backend.py:171-222),
     loaded unmodified from the reference package in baseline/_ref under
-    stand-in ``sglang`` package names that are removed again; None when the
-    package is not installed."""
+    stand-in ``sglang`` package names that are removed again; a one-line
+    reason instead when the package is not installed or does not load."""
     import importlib.util
     import types
 
@@ -339,7 +339,7 @@ def reference_context_metadata():
              ("sglang.srt.layers.attention.context_backend",
               "srt/layers/attention/context_backend.py")]
     if not all(os.path.exists(os.path.join(sg, rel)) for _, rel in files):
-        return None
+        return "the reference package is not installed in baseline/_ref"
     from akv_b200 import context_page_table, context_reposition
 
     saved = {k: v for k, v in sys.modules.items() if k == "sglang" or k.startswith("sglang.")}
@@ -357,8 +357,8 @@ def reference_context_metadata():
             sys.modules[name] = mod
             spec.loader.exec_module(mod)
         return mod.ContextAttentionMetadata
-    except Exception:
-        return None
+    except Exception as exc:
+        return f"the reference's context_backend.py did not load: {type(exc).__name__}: {exc}"
     finally:
         for k in [k for k in sys.modules if k == "sglang" or k.startswith("sglang.")]:
             del sys.modules[k]
@@ -378,8 +378,8 @@ def flashinfer_prefill_versus_ours(att, q, k_pool, v_pool, kv_idx, births, qo, k
     the largest output difference; an "unavailable" note when the reference
     package or FlashInfer is missing here."""
     meta_cls = reference_context_metadata()
-    if meta_cls is None:
-        return {"unavailable": "the reference package is not installed in baseline/_ref"}
+    if isinstance(meta_cls, str):
+        return {"unavailable": meta_cls}
     try:
         import flashinfer
 
