@@ -148,9 +148,10 @@ def event_compiler_cases(ir):
     cases["prewarm"] = dict(token_ids=np.zeros(1, np.int64), drop_insert_offsets=i32([]),
                             drop_range_offsets=i32([0]), drop_ranges=i32([]),
                             reposition_raw_boundaries=i32([]), reposition_insert_offsets=i32([]))
-    cases["survey10"] = dict(token_ids=np.arange(10, dtype=np.int64), drop_insert_offsets=i32([5]),
-                             drop_range_offsets=i32([0, 1]), drop_ranges=i32([2, 5]),
-                             reposition_raw_boundaries=i32([7]), reposition_insert_offsets=i32([8]))
+    cases["ten_tokens"] = dict(token_ids=np.arange(10, dtype=np.int64),
+                               drop_insert_offsets=i32([5]), drop_range_offsets=i32([0, 1]),
+                               drop_ranges=i32([2, 5]), reposition_raw_boundaries=i32([7]),
+                               reposition_insert_offsets=i32([8]))
     cases["suffix_drop_ignored"] = dict(
         token_ids=np.arange(12, dtype=np.int64), drop_insert_offsets=i32([12]),
         drop_range_offsets=i32([0, 1]), drop_ranges=i32([8, 12]),

@@ -102,7 +102,7 @@ def test_drop_c2_full_size_matches_oracle():
     rows, nslots = workloads.slot_rows(np.random.default_rng(0), prog)
     res = _check(prog, rows, ring_free=np.arange(nslots, nslots + 16))
     totals = res.totals.cpu().tolist()
-    assert totals[1] == 38902 and totals[3] == 26425  # survey's seed-0 counts
+    assert totals[1] == 38902 and totals[3] == 26425  # the c2 program's seed-0 counts
 
 
 def test_drop_c3_shared_prefix_cow_matches_oracle():
