@@ -119,7 +119,10 @@ class ContextPrefillAttention:
         kernel for the shape (3 at head_dim 64, 4 at 128), 1 the mma.sync
         kernel, 2 the tcgen05 / TMEM kernel (head_dim 64), 3 its
         warp-specialised form (head_dim 64 and 128), 4 the warp-specialised
-        form with two query tiles per CTA."""
+        form with two query tiles per CTA; 5 and 6 the forms of 3 and 4 with
+        P rounded to bf16 for P.V (the precision of FlashInfer's prefill:
+        one MMA per key block instead of the hi + lo pair, |error| up to
+        2^-8 * sum p|v| more than the others)."""
         if q.dtype != torch.bfloat16 or k_pool.dtype != torch.bfloat16 or \
                 v_pool.dtype != torch.bfloat16:
             raise ValueError("context attention runs on bf16 q / K / V")

@@ -493,6 +493,17 @@ __device__ __forceinline__ void tmem_st32_sync(uint32_t taddr, const uint32_t* r
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// One store of 16 columns (P's hi words alone) and its wait.
+__device__ __forceinline__ void tmem_st16_sync(uint32_t ta, const uint32_t* a) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,"
+      "%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      "\n\ttcgen05.wait::st.sync.aligned;" ::"r"(ta),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]),
+      "r"(a[8]), "r"(a[9]), "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]),
+      "r"(a[15])
+      : "memory");
+}
 // Two stores of 16 columns (P's hi and lo words) and their wait.
 __device__ __forceinline__ void tmem_st16x2_sync(uint32_t ta, const uint32_t* a, uint32_t tb,
                                                  const uint32_t* b) {
@@ -931,7 +942,10 @@ __device__ __forceinline__ bool ws_wait(uint32_t bar, uint32_t parity, volatile 
   return true;
 }
 
-template <int D, int QT>
+// LO: P enters P.V as the bf16 pair hi + lo (two MMAs per key block, P to
+// about 16 bits); without it, as hi = RN_bf16(P) alone (one MMA), the
+// precision of FlashInfer's and most flash kernels' P.V.
+template <int D, int QT, bool LO>
 __global__ void __launch_bounds__(WsCfg<D, QT>::kThreads, WsCfg<D, QT>::kMinBlocks)
 prefill_attention_tc_ws_kernel(const PrefillParams p) {
   using C = WsCfg<D, QT>;
@@ -1061,7 +1075,8 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
               const uint64_t vd = D == 64 ? sw128_desc(vb + 2048 * k)
                                           : sw128_desc_mn(vb + 2048 * k, kTcKeys * 128);
               mma_ts(tmem + 256 * q + kColO, pb + 8 * k, vd, f16_idesc(D, 1), 1);
-              mma_ts(tmem + 256 * q + kColO, pb + 32 + 8 * k, vd, f16_idesc(D, 1), 1);
+              if constexpr (LO)
+                mma_ts(tmem + 256 * q + kColO, pb + 32 + 8 * k, vd, f16_idesc(D, 1), 1);
             }
             umma_commit(bar_o(q));
             if (u == n_tiles - 1) umma_commit(bar_done(q));
@@ -1244,11 +1259,14 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
         if (i & 2) rsb = f2_add(rsb, e);
         else rsa = f2_add(rsa, e);
         const uint32_t h = pack_bf16(e0, e1);
-        float d0, d1;
-        f2_unpack(f2_sub(e, f2_pack(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u))),
-                  d0, d1);
         hi[i / 2] = h;
-        lo[i / 2] = pack_bf16(d0, d1);
+        if constexpr (LO) {
+          float d0, d1;
+          f2_unpack(
+              f2_sub(e, f2_pack(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u))),
+              d0, d1);
+          lo[i / 2] = pack_bf16(d0, d1);
+        }
       }
       float rs0, rs1;
       f2_unpack(f2_add(rsa, rsb), rs0, rs1);
@@ -1269,7 +1287,10 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
           tmem_st32_sync(trow + kColO + kOCols * half + c, r);
         }
       }
-      tmem_st16x2_sync(sbuf + half * (kHalf / 2), hi, sbuf + 32 + half * (kHalf / 2), lo);
+      if constexpr (LO)
+        tmem_st16x2_sync(sbuf + half * (kHalf / 2), hi, sbuf + 32 + half * (kHalf / 2), lo);
+      else
+        tmem_st16_sync(sbuf + half * (kHalf / 2), hi);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_p(qt, tile & 1));
@@ -1324,15 +1345,15 @@ prefill_attention_tc_ws_kernel(const PrefillParams p) {
 
 // n_items counts 16-query items; with QT = 2 they come in pairs (the host
 // pads the list to an even length).
-template <int D, int QT>
+template <int D, int QT, bool LO = true>
 int launch_prefill_tc_ws(const PrefillParams& p, int n_items, int num_kv_heads, cudaStream_t s) {
   using C = WsCfg<D, QT>;
   if (n_items % QT) return AKV_ERR_INVALID;
-  if (cudaFuncSetAttribute(prefill_attention_tc_ws_kernel<D, QT>,
+  if (cudaFuncSetAttribute(prefill_attention_tc_ws_kernel<D, QT, LO>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
     return AKV_ERR_CUDA;
   if (n_items > 0)
-    prefill_attention_tc_ws_kernel<D, QT>
+    prefill_attention_tc_ws_kernel<D, QT, LO>
         <<<dim3(n_items / QT, num_kv_heads), C::kThreads, C::kSmem, s>>>(p);
   return launch_status();
 }
@@ -1416,7 +1437,7 @@ extern "C" int akv_context_attention(
                          (reinterpret_cast<uintptr_t>(out) & 15) == 0 && q_stride_token % 8 == 0 &&
                          q_stride_head % 8 == 0 && out_stride_token % 8 == 0 &&
                          out_stride_head % 8 == 0;
-  if (variant < 0 || variant > 4) return AKV_ERR_INVALID;
+  if (variant < 0 || variant > 6) return AKV_ERR_INVALID;
   // The tcgen05 kernels take row maxima of unscaled scores: sm_scale > 0.
   const bool tc_ok = aligned16 && sm_scale > 0.f;
   if (variant == 2 && !(tc_ok && head_dim == 64)) return AKV_ERR_UNSUPPORTED;
@@ -1432,6 +1453,15 @@ extern "C" int akv_context_attention(
   if (variant == 4) {
     if (head_dim == 64) return launch_prefill_tc_ws<64, 2>(p, n_items, num_kv_heads, s);
     if (head_dim == 128) return launch_prefill_tc_ws<128, 2>(p, n_items, num_kv_heads, s);
+  }
+  // 5, 6: the forms of 3 and 4 with P rounded to bf16 for P.V.
+  if (variant == 5) {
+    if (head_dim == 64) return launch_prefill_tc_ws<64, 1, false>(p, n_items, num_kv_heads, s);
+    if (head_dim == 128) return launch_prefill_tc_ws<128, 1, false>(p, n_items, num_kv_heads, s);
+  }
+  if (variant == 6) {
+    if (head_dim == 64) return launch_prefill_tc_ws<64, 2, false>(p, n_items, num_kv_heads, s);
+    if (head_dim == 128) return launch_prefill_tc_ws<128, 2, false>(p, n_items, num_kv_heads, s);
   }
   if (variant == 2) return launch_prefill_tc(p, n_items, num_kv_heads, s);
   switch (head_dim) {

@@ -1514,6 +1514,20 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0,
     step_flops = (layers // 2) * 4.0 * d * hq * (full.visible + swa.visible) * world
     peak, peak_kind = measured_tensor_peak()
     achieved = full_flops / (full_ms / 1e3) / 1e12
+    bf16_p = None
+    if variant == 0 and layers >= 2:
+        # The same full layer with P rounded to bf16 for P.V (variant 5, or 6
+        # at head_dim 128): FlashInfer's precision, one P.V MMA per key block.
+        fv = 6 if d == 128 else 5
+        kp, vp = pools[1]
+        fast_ms = time_launches(
+            lambda: full.run(q, kp, vp, kv_idx, births, t_qpos, t_kpos, sinks=sinks, out=out,
+                             variant=fv), max(steps, 3), stream)
+        full.check()
+        fast = full_flops / (fast_ms / 1e3) / 1e12
+        bf16_p = {"variant": fv, "p_in_pv": "bf16 (FlashInfer's precision; default: hi + lo)",
+                  "ms_per_launch": round(fast_ms, 4), "achieved": round(fast, 1),
+                  "unit": "TFLOP/s", "frac": round(fast / peak, 4)}
     runtime_ref = None
     if compare and layers >= 2:
         # The reference's runtime context prefill on one sliding-window and
@@ -1570,6 +1584,7 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0,
                      "ms_per_launch": round(full_ms, 4)},
         "gpu_launches_per_step": layers,
         "cpu_baseline": cpu,
+        "bf16_p_form": bf16_p,
         "reference_runtime_prefill": runtime_ref,
     }
 

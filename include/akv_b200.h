@@ -499,8 +499,11 @@ int akv_decode_attention(
  * variant: 0 = the faster kernel for the shape, 1 = the mma.sync kernel,
  * 2 = the tcgen05 / TMEM kernel (head_dim 64), 3 = its warp-specialised
  * form (head_dim 64 and 128), 4 = the warp-specialised form with the two
- * items of a pair in one CTA (n_items even); 2-4 need 16-byte aligned q and
- * out rows and sm_scale > 0 (AKV_ERR_UNSUPPORTED otherwise).
+ * items of a pair in one CTA (n_items even); 5 and 6 = the forms of 3 and 4
+ * with P rounded to bf16 for P.V (one MMA per key block instead of the hi +
+ * lo pair of the others: FlashInfer's precision, |error| <= 2^-8 sum p|v|
+ * more); 2-6 need 16-byte aligned q and out rows and sm_scale > 0
+ * (AKV_ERR_UNSUPPORTED otherwise).
  */
 int64_t akv_context_attention_query_block(void);
 int akv_context_attention(

@@ -2,8 +2,9 @@
 against a plain torch fp32 reference and the float64 oracle.
 
 Tolerance: atol 2e-3 / rtol 1e-2 on the bf16 output (bf16 inputs, fp32
-softmax and accumulation, P rounded to bf16 before P.V as every flash kernel
-does).
+softmax and accumulation; P enters P.V as a bf16 hi + lo pair, except in
+variants 5 and 6, which round it to bf16 like FlashInfer and get that
+rounding's bound on top, stated at their test).
 """
 
 import numpy as np
@@ -191,3 +192,43 @@ def test_plan_rejects_unsorted_positions():
     att = ContextPrefillAttention(64, 8, 64, "cuda")
     with pytest.raises(ValueError, match="increase"):
         att.plan([0, 2], [0, 2], [5, 6], [3, 3])
+
+
+@pytest.mark.parametrize("variant", [5, 6], ids=["tcgen05_ws_bf16p", "tcgen05_ws_2tiles_bf16p"])
+@pytest.mark.parametrize("case", range(len(CASES)))
+def test_prefill_bf16_p_forms_match_torch_within_their_bound(case, variant):
+    """Variants 5 and 6 round P to bf16 for P.V, as FlashInfer's prefill
+    does (one MMA per key block instead of the hi + lo pair): each output is
+    within atol 2e-3 + rtol 1e-2 |ref| plus that rounding's bound,
+    2^-8 * sum_i p_i |v_i|, of the exact fp32 attention."""
+    prefix, queries, hkv, d, window, use_sinks = CASES[case]
+    rng = np.random.default_rng(case)
+    x = make_batch(rng, prefix, queries, hkv, d)
+    sinks = torch.randn(8 * hkv, device="cuda") if use_sinks else None
+    scale = 1.0 / np.sqrt(d)
+    out, _ = run_ours(x, hkv, d, window, sinks, variant=variant)
+    want = torch_reference(x, window, sinks, scale)
+    p_abs_v = torch_reference(dict(x, v_pool=x["v_pool"].abs()), window, sinks, scale)
+    bound = ATOL + RTOL * want.abs() + 2.0 ** -8 * p_abs_v
+    excess = (out.float() - want).abs() - bound
+    assert float(excess.max()) <= 0.0, f"max excess {float(excess.max()):.3g}"
+
+
+@pytest.mark.parametrize("variant", [5, 6])
+def test_prefill_bf16_p_forms_keep_the_exact_lse(variant):
+    """The row sums of variants 5 and 6 add the fp32 exponentials, so their
+    log-sum-exp is as exact as the other kernels'."""
+    from oracle import oracle
+
+    rng = np.random.default_rng(42)
+    hkv, d, window = 2, 64, 33
+    x = make_batch(rng, [150, 40], [37, 20], hkv, d)
+    sinks = torch.randn(8 * hkv, device="cuda")
+    lse = torch.empty(x["q"].shape[0], 8 * hkv, device="cuda")
+    run_ours(x, hkv, d, window, sinks, lse=lse, variant=variant)
+    _, want_lse = oracle.prefill_attention(
+        x["q"].float().cpu().numpy(), x["k_pool"].float().cpu().numpy(),
+        x["v_pool"].float().cpu().numpy(), x["qo"], x["kv"], x["kv_idx"], x["births"],
+        x["qpos"], x["kpos"], sinks=sinks.cpu().numpy(), window=window)
+    full = np.logaddexp(want_lse, sinks.cpu().numpy()[None, :].astype(np.float64))
+    np.testing.assert_allclose(lse.cpu().numpy(), full, atol=1e-3, rtol=1e-4)
