@@ -91,7 +91,8 @@ def parse_args():
                         "GPU (8/N KV heads; a profiling aid, not a multi-GPU run)")
     p.add_argument("--variant", type=int, default=0,
                    help="c4p: prefill kernel (0 the default for the shape, 1 mma.sync, 2 tcgen05, "
-                        "3 tcgen05 warp-specialised, 4 the same with two query tiles per CTA)")
+                        "3 tcgen05 warp-specialised, 4 the same with two query tiles per CTA, "
+                        "5 / 6: 3 / 4 with P rounded to bf16 for P.V)")
     p.add_argument("--head-dim", type=int, default=64, choices=[64, 128],
                    help="c4p: head_dim of the prefill shape")
     p.add_argument("--page-size", type=int, default=1, choices=[1, 16],
@@ -1576,7 +1577,9 @@ def bench_prefill(dev, world, rank, warmup, steps, seed=0, layers=36, variant=0,
                    "positions": "prefix with holes (about a third dropped)"},
         "roofline": {"bound": "tensor",
                      "kernel": {1: "prefill_attention_kernel", 2: "prefill_attention_tc_kernel",
-                                4: "prefill_attention_tc_ws_kernel, two query tiles"}
+                                4: "prefill_attention_tc_ws_kernel, two query tiles",
+                                5: "prefill_attention_tc_ws_kernel, bf16 P",
+                                6: "prefill_attention_tc_ws_kernel, two query tiles, bf16 P"}
                      .get(variant, "prefill_attention_tc_ws_kernel") + " (full layer)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
