@@ -299,9 +299,13 @@ class DropCompactor:
         if row_ids.shape != (nreq,) or (shared_prefix is not None and
                                         np.shape(shared_prefix) != (nreq,)):
             raise ValueError("row_ids and shared_prefix must hold one entry per request")
-        tiles = (token_counts + TILE - 1) // TILE
-        tile_offsets = np.concatenate(([0], np.cumsum(tiles)))
-        n_tiles = int(tile_offsets[-1])
+        if nreq == 1:  # a single request: plain integers are cheaper than numpy
+            n_tiles = -(-total // TILE)
+            tile_offsets = (0, n_tiles)
+        else:
+            tiles = (token_counts + TILE - 1) // TILE
+            tile_offsets = np.concatenate(([0], np.cumsum(tiles)))
+            n_tiles = int(tile_offsets[-1])
         shared = shared_prefix is not None
         # One handle per layout and size: its device views (fixed offsets of
         # the staging buffer) and its cached launch arguments are reused by
