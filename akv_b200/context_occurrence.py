@@ -173,6 +173,27 @@ class SlotGather:
         self._tasks.append((out, idx, self._seg_objs[sid], literal))
         self._sized = None
 
+    def _add_fields(self, fields, segments):
+        """``_add`` for several outputs gathered from one segment set (the
+        fields of one request): one lookup of the set, then one task per
+        (out, indices) pair."""
+        fields = [(out, idx if type(idx) is np.ndarray and idx.ndim == 1
+                   else np.asarray(idx).reshape(-1)) for out, idx in fields]
+        m_max = max((idx.shape[0] for _, idx in fields), default=0)
+        sid = self._segment_set(segments, False, m_max)
+        if m_max > 2**31 - 1:
+            raise ValueError("a slot gather task holds at most 2^31 - 1 outputs")
+        flags, seg_obj = self._seg_flags[sid], self._seg_objs[sid]
+        out64 = _native.GATHER_OUT64
+        meta, idxs, tasks = self._meta, self._idx, self._tasks
+        for out, idx in fields:
+            m = idx.shape[0]
+            meta.append((m, out.data_ptr() if m else 0,
+                         flags | (out64 if out.dtype == torch.int64 else 0), sid))
+            idxs.append(idx)
+            tasks.append((out, idx, seg_obj, False))
+        self._sized = None
+
     def __len__(self):
         return len(self._tasks)
 
@@ -357,16 +378,15 @@ class _AdvancePlan:
             succ_slots = torch.empty(len(self.retained), dtype=dt, device=dev)
         if retired is None:
             retired = torch.empty(len(self.retired), dtype=dt, device=dev)
-        gather._add(occurrence_out, self.occurrences, seg)
-        gather._add(src_out, self.copy_src, seg)
-        gather._add(dst_out, self.copy_dst, seg)
-        gather._add(pairs_out, self.pairs, literal=True)
-        gather._add(succ_slots, self.retained, seg)
-        gather._add(retired, self.retired, seg)
+        fields = [(occurrence_out, self.occurrences), (src_out, self.copy_src),
+                  (dst_out, self.copy_dst), (succ_slots, self.retained),
+                  (retired, self.retired)]
         if self.swa is not None:
             if unused is None:
                 unused = torch.empty(len(self.unused_swa), dtype=dt, device=dev)
-            gather._add(unused, self.unused_swa, seg)
+            fields.append((unused, self.unused_swa))
+        gather._add_fields(fields, seg)
+        gather._add(pairs_out, self.pairs, literal=True)
         owned, canon, term, positions = self.successor
         state = self.state_type(
             succ_slots, owned, canon, term, positions, self.exact_prefix_len,

@@ -1737,21 +1737,17 @@ def bench_occurrence(dev, world, rank, warmup, steps, seed=0, requests=16, prefi
     occ_sizes = [len(r["occ"]) for r in reqs]
 
     def queue():
-        # the tasks OccurrenceBatch queues per request (its internal _add:
-        # per-request views of batch buffers it allocated, indices that fit
-        # int32 by construction)
+        # the tasks OccurrenceBatch queues per request (its internal
+        # _add_fields / _add: per-request views of batch buffers it
+        # allocated, indices that fit int32 by construction)
         g = SlotGather(dev)
         v_slots = out_slots.split_with_sizes(occ_sizes)
         v_src, v_dst, v_pairs = (i32[:n_copy].split(copies), i32[n_copy:2 * n_copy].split(copies),
                                  i32[2 * n_copy:].split(2 * copies))
         for j, r in enumerate(reqs):
-            seg = r["seg"]
-            g._add(v_slots[j], r["occ"], seg)
-            g._add(v_src[j], r["src"], seg)
-            g._add(v_dst[j], r["dst"], seg)
+            g._add_fields([(v_slots[j], r["occ"]), (v_src[j], r["src"]), (v_dst[j], r["dst"]),
+                           (succ[j], r["keep"]), (retired[j], r["release"])], r["seg"])
             g._add(v_pairs[j], r["pairs"], literal=True)
-            g._add(succ[j], r["keep"], seg)
-            g._add(retired[j], r["release"], seg)
         return g
 
     def ours():
