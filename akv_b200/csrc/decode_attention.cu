@@ -93,36 +93,60 @@ __device__ __forceinline__ void attend_item(const AttnParams& p, const int4 w,
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
 
-  // Each thread gathers kCpt 16-byte chunks of one key of every tile, so it
-  // needs one index per tile, and that index is loaded a tile ahead: the
-  // copies never wait on their own address.
+  // Gather of a tile's K and V rows into shared memory, kCpt 16-byte chunks
+  // per thread for each.  When the threads of one key span a 128-byte line
+  // or more (kTpk >= 8: four or more local heads), each thread copies chunks
+  // of one key, so it needs one index per tile.  With fewer heads a key's
+  // row is 128-256 bytes, and that split would leave every warp request a
+  // 32- or 64-byte piece of 16 different rows; there the chunks are dealt
+  // row-wise instead (consecutive threads take consecutive chunks of one
+  // key, a warp request covers whole 128-byte lines) and each thread needs
+  // the index of the kCpt keys it serves.  Either way the indices are
+  // loaded a tile ahead, so the copies never wait on their own address.
   constexpr int kTpk = C::kThreads / TK;        // threads per key
   constexpr int kCpt = C::kChunks / kTpk;       // chunks per thread (K, and as many of V)
   static_assert(C::kThreads % TK == 0 && C::kChunks % kTpk == 0, "tile split");
+  constexpr bool kRowWise = kTpk < 8;
+  static_assert(!kRowWise || C::kThreads % C::kChunks == 0, "row-wise split");
+  constexpr int kKpr = kRowWise ? C::kThreads / C::kChunks : 1;  // keys per row-wise round
+  constexpr int kNS = kRowWise ? kCpt : 1;                         // indices per thread
   const int my_key = tid / kTpk, my_q = tid - my_key * kTpk;
-  // Slot of this thread's key in `tile`, or -1 past the range end.
-  auto fetch_slot = [&](int tile) -> long long {
-    const int kk = kv_begin + tile * TK + my_key;
-    if (tile >= n_tiles || kk >= kv_end) return -1;
-    long long slot = __ldg(p.kv_indices + kk);
-    if (slot < 0 || slot >= p.num_slots) {  // never touch memory outside the pools
-      if (p.error_flag) *p.error_flag = 1;
-      slot = 0;
+  const int my_c = kRowWise ? tid % C::kChunks : 0;  // row-wise: this thread's chunk
+  // Tile-local key of index i of this thread.
+  auto key_of = [&](int i) { return kRowWise ? i * kKpr + tid / C::kChunks : my_key; };
+  struct Slots { long long v[kNS]; };
+  // Slots of this thread's keys in `tile`, -1 past the range end.
+  auto fetch_slot = [&](int tile) {
+    Slots r;
+#pragma unroll
+    for (int i = 0; i < kNS; ++i) {
+      const int kk = kv_begin + tile * TK + key_of(i);
+      long long slot = -1;
+      if (tile < n_tiles && kk < kv_end) {
+        slot = __ldg(p.kv_indices + kk);
+        if (slot < 0 || slot >= p.num_slots) {  // never touch memory outside the pools
+          if (p.error_flag) *p.error_flag = 1;
+          slot = 0;
+        }
+      }
+      r.v[i] = slot;
     }
-    return slot;
+    return r;
   };
-  auto issue_tile = [&](int s, long long slot) {
+  auto issue_tile = [&](int s, const Slots& slots) {
     const uint32_t kbase = smem_u32(smem + s * C::kStageBytes);
     const uint32_t vbase = kbase + C::kTileBytes;
-    const bool valid = slot >= 0;
-    const long long sl = valid ? slot : 0;
-    const int bytes = valid ? 16 : 0;  // zero-fill past the range end
 #pragma unroll
     for (int i = 0; i < kCpt; ++i) {
-      const int c = my_q + kTpk * i;
+      const long long slot = slots.v[kRowWise ? i : 0];
+      const bool valid = slot >= 0;
+      const long long sl = valid ? slot : 0;
+      const int bytes = valid ? 16 : 0;  // zero-fill past the range end
+      const int key = key_of(i);
+      const int c = kRowWise ? my_c : my_q + kTpk * i;
       const int head = c / C::kCph, cc = c - head * C::kCph;
-      const int phys = head * C::kCph + (cc ^ (my_key & 7));
-      const uint32_t off = my_key * C::kRowBytes + phys * 16;
+      const int phys = head * C::kCph + (cc ^ (key & 7));
+      const uint32_t off = key * C::kRowBytes + phys * 16;
       cp_async16(kbase + off, p.k + sl * p.k_ss + head * p.k_sh + cc * 8, bytes);
       cp_async16(vbase + off, p.v + sl * p.v_ss + head * p.v_sh + cc * 8, bytes);
     }
@@ -133,7 +157,7 @@ __device__ __forceinline__ void attend_item(const AttnParams& p, const int4 w,
     if (s < n_tiles) issue_tile(s, fetch_slot(s));
     cp_async_commit();
   }
-  long long next_slot = fetch_slot(NSTAGE - 1);
+  Slots next_slot = fetch_slot(NSTAGE - 1);
 
   // Q^T fragments of this warp's 8 query heads (B operand, k = dims).
   const int qh0 = warp * kGroup;
