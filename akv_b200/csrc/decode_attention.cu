@@ -37,9 +37,10 @@ constexpr int kGroup = 8;  // query heads per KV head (the MMA N)
 // 16-key stages, two of them, for every head count: 64 KiB of shared memory
 // for 8 KV heads of 64 dims (three CTAs per SM), proportionally less -- and
 // more CTAs per SM -- when tensor parallelism leaves fewer heads per GPU.
-// Measured on the c4 full layer: 8 heads 0.578 ms; 4 heads 0.371 ms (32-key
-// stages: 0.744), 2 heads 0.347 ms (0.642), 1 head 0.310 ms (0.435); 3 or
-// 4 stages were no better.  Also slower for 8 heads: 2 CTAs x 3 stages,
+// Measured on the c4 full layer (random slots): 8 heads 0.578 ms; 4 heads
+// 0.371 ms (32-key stages: 0.744); 2 heads 0.190 ms and 1 head 0.130 ms
+// with the row-wise gather (per-key split: 0.347 / 0.310; 32-key stages
+// were slower there too); 3 or 4 stages were no better.  Also slower for 8 heads: 2 CTAs x 3 stages,
 // 1 CTA x 32-key stages, per-warp rings (a key's 1 KiB row then reaches
 // DRAM as eight separate 128-byte requests) and a warp-specialised variant
 // with one cp.async.bulk per row and an mbarrier ring.
