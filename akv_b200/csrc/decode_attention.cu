@@ -38,9 +38,9 @@ constexpr int kGroup = 8;  // query heads per KV head (the MMA N)
 // for 8 KV heads of 64 dims (three CTAs per SM), proportionally less -- and
 // more CTAs per SM -- when tensor parallelism leaves fewer heads per GPU.
 // Measured on the c4 full layer (random slots): 8 heads 0.578 ms; 4 heads
-// 0.371 ms (32-key stages: 0.744); 2 heads 0.190 ms and 1 head 0.130 ms
-// with the row-wise gather (per-key split: 0.347 / 0.310; 32-key stages
-// were slower there too); 3 or 4 stages were no better.  Also slower for 8 heads: 2 CTAs x 3 stages,
+// 0.333 ms, 2 heads 0.190 ms and 1 head 0.130 ms with the row-wise gather
+// (below); 32-key stages (0.744 ms at 4 heads with the per-key split) and
+// 3 or 4 stages were no better.  Also slower for 8 heads: 2 CTAs x 3 stages,
 // 1 CTA x 32-key stages, per-warp rings (a key's 1 KiB row then reaches
 // DRAM as eight separate 128-byte requests) and a warp-specialised variant
 // with one cp.async.bulk per row and an mbarrier ring.
@@ -95,19 +95,21 @@ __device__ __forceinline__ void attend_item(const AttnParams& p, const int4 w,
   const int g = lane >> 2, t = lane & 3;
 
   // Gather of a tile's K and V rows into shared memory, kCpt 16-byte chunks
-  // per thread for each.  When the threads of one key span a 128-byte line
-  // or more (kTpk >= 8: four or more local heads), each thread copies chunks
-  // of one key, so it needs one index per tile.  With fewer heads a key's
-  // row is 128-256 bytes, and that split would leave every warp request a
-  // 32- or 64-byte piece of 16 different rows; there the chunks are dealt
-  // row-wise instead (consecutive threads take consecutive chunks of one
-  // key, a warp request covers whole 128-byte lines) and each thread needs
+  // per thread for each.  At eight local heads each thread copies chunks of
+  // one key (16 threads, 256 contiguous bytes of its 1 KiB row per warp
+  // request), so it needs one index per tile.  With fewer heads that split
+  // would leave a warp request 32-128 bytes of each of 16 different rows;
+  // there the chunks are dealt row-wise instead (consecutive threads take
+  // consecutive chunks of one key, so a request covers whole 128-byte lines
+  // and, at four heads, a key's whole 512-byte row) and each thread needs
   // the index of the kCpt keys it serves.  Either way the indices are
   // loaded a tile ahead, so the copies never wait on their own address.
+  // Measured on random slots: 1 / 2 / 4 heads 0.310 / 0.347 / 0.380 ms per
+  // c4 full layer with the per-key split, 0.130 / 0.190 / 0.333 row-wise.
   constexpr int kTpk = C::kThreads / TK;        // threads per key
   constexpr int kCpt = C::kChunks / kTpk;       // chunks per thread (K, and as many of V)
   static_assert(C::kThreads % TK == 0 && C::kChunks % kTpk == 0, "tile split");
-  constexpr bool kRowWise = kTpk < 8;
+  constexpr bool kRowWise = kTpk < 16;
   static_assert(!kRowWise || C::kThreads % C::kChunks == 0, "row-wise split");
   constexpr int kKpr = kRowWise ? C::kThreads / C::kChunks : 1;  // keys per row-wise round
   constexpr int kNS = kRowWise ? kCpt : 1;                         // indices per thread
