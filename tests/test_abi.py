@@ -78,6 +78,20 @@ def test_argument_errors_are_reported_before_any_launch():
         args = [0, None, None, 0, None, None, None, None, None, 0, 1, bad, None, 1]
         assert lib.akv_drop_compact_paged(*args, *([None] * 18)) == _native.AKV_ERR_INVALID
     assert lib.akv_occurrence_advance_indices(None, None) == _native.AKV_ERR_INVALID
+    # decode-view read-back: a missing host vector, a negative count, or a
+    # view without its device vectors is refused before any copy
+    import ctypes
+
+    buf = (ctypes.c_int32 * 16)()
+    p1 = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.akv_drop_read_view(None, p1, p1, 1, p1, p1, 1, p1, None) == \
+        _native.AKV_ERR_INVALID
+    assert lib.akv_drop_read_view(p1, p1, p1, -1, p1, p1, 1, p1, None) == \
+        _native.AKV_ERR_INVALID
+    assert lib.akv_drop_read_view(p1, None, None, 3, p1, p1, 1, p1, None) == \
+        _native.AKV_ERR_INVALID
+    assert lib.akv_drop_read_view(p1, p1, p1, 0, None, p1, 1, p1, None) == \
+        _native.AKV_ERR_INVALID
 
 
 def test_layout_batch_struct_matches_the_header():
