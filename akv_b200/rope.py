@@ -56,16 +56,20 @@ def yarn_cos_sin_cache(
     original_max_position: int,
     beta_fast: float = 32.0,
     beta_slow: float = 1.0,
+    truncate: bool = True,
 ) -> torch.Tensor:
+    """``truncate``: round the ramp's bounds out to whole dimensions (the
+    original form of the method); False keeps them fractional, as the
+    GPT-OSS checkpoints' rope settings ask ("truncate": false)."""
     half = rotary_dim // 2
     pos_freqs = base ** (torch.arange(0, rotary_dim, 2, dtype=torch.float32) / rotary_dim)
     extrapolation = 1.0 / pos_freqs
     interpolation = 1.0 / (scaling_factor * pos_freqs)
-    low = max(math.floor(_correction_dim(rotary_dim, beta_fast, base, original_max_position)), 0)
-    high = min(
-        math.ceil(_correction_dim(rotary_dim, beta_slow, base, original_max_position)),
-        rotary_dim - 1,
-    )
+    low = _correction_dim(rotary_dim, beta_fast, base, original_max_position)
+    high = _correction_dim(rotary_dim, beta_slow, base, original_max_position)
+    if truncate:
+        low, high = math.floor(low), math.ceil(high)
+    low, high = max(low, 0), min(high, rotary_dim - 1)
     if low == high:
         high += 0.001  # keep the ramp finite
     ramp = ((torch.arange(half, dtype=torch.float32) - low) / (high - low)).clamp(0, 1)

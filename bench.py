@@ -121,7 +121,7 @@ def cos_sin(name, dim, max_pos):
 
     rope = WORKLOADS[name][3]
     if rope == "yarn":
-        return yarn_cos_sin_cache(max_pos, dim, 150000.0, 32.0, 4096)
+        return yarn_cos_sin_cache(max_pos, dim, 150000.0, 32.0, 4096, truncate=False)
     return rope_cos_sin_cache(max_pos, dim, float(rope[4:]))
 
 
@@ -1101,7 +1101,7 @@ def bench_c3(dev, world, rank, warmup, steps, page_sizes=(1, 16), seed=0, layers
     v_pools = [torch.empty(pool_slots, heads, dim, device=dev, dtype=torch.bfloat16)
                for _ in range(layers)]
     k_ptrs, v_ptrs = layer_pointer_table(k_pools), layer_pointer_table(v_pools)
-    cache = yarn_cos_sin_cache(32768, dim, 150000.0, 32.0, 4096).to(dev)
+    cache = yarn_cos_sin_cache(32768, dim, 150000.0, 32.0, 4096, truncate=False).to(dev)
     stream = torch.cuda.current_stream(dev)
     peak, peak_kind = measured_peak()
     comp = DropCompactor(total, prog.requests, max(1, len(prog.ranges) // 2), dev)

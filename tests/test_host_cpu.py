@@ -151,3 +151,53 @@ def test_reference_compiler_matches_oracle_at_c2_size():
         np.testing.assert_array_equal(np.asarray(a[k]).astype(np.int64),
                                       np.asarray(b[k]).astype(np.int64), err_msg=k)
     assert a["next_position"] == b["next_position"]
+
+
+@pytest.mark.parametrize("truncate", [True, False])
+def test_yarn_table_matches_the_serving_stacks(truncate):
+    """The YaRN table of akv_b200.rope against the two serving-stack
+    implementations present in this image, for the GPT-OSS settings (head_dim 64,
+    theta 150,000, factor 32 over 4,096 positions, beta 32 / 1): vLLM's
+    YaRN rotary module's cos/sin buffer (the class SGLang's is adapted
+    from) and transformers' YaRN inverse frequencies and attention factor,
+    with the ramp bounds rounded out (truncate) and left fractional, as the
+    GPT-OSS checkpoints ask."""
+    import torch
+
+    from akv_b200.rope import yarn_cos_sin_cache
+
+    ours = yarn_cos_sin_cache(8192, 64, 150000.0, 32.0, 4096, truncate=truncate)
+    rope_mod = pytest.importorskip("vllm.model_executor.layers.rotary_embedding")
+    from vllm.model_executor.layers.rotary_embedding.common import yarn_get_mscale
+
+    # The class's own table methods, on an object holding the attributes its
+    # constructor sets (the constructor itself wants a vLLM device config).
+    yarn = rope_mod.YaRNScalingRotaryEmbedding
+
+    class Stand:
+        _compute_inv_freq = yarn._compute_inv_freq
+        _compute_cos_sin_cache = yarn._compute_cos_sin_cache
+
+    emb = Stand()
+    emb.rotary_dim, emb.base, emb.max_position_embeddings = 64, 150000.0, 4096
+    emb.scaling_factor, emb.extrapolation_factor, emb.attn_factor = 32.0, 1, 1
+    emb.beta_fast, emb.beta_slow, emb.truncate = 32, 1, truncate
+    emb.mscale = float(yarn_get_mscale(32.0))
+    theirs = emb._compute_cos_sin_cache()[:8192]
+    assert torch.equal(ours, theirs)  # bit for bit
+
+    from transformers import PretrainedConfig
+    from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+
+    cfg = PretrainedConfig()
+    cfg.hidden_size, cfg.num_attention_heads, cfg.head_dim = 64 * 64, 64, 64
+    cfg.max_position_embeddings = 131072
+    cfg.rope_parameters = {"rope_type": "yarn", "rope_theta": 150000.0, "factor": 32.0,
+                           "beta_fast": 32.0, "beta_slow": 1.0,
+                           "original_max_position_embeddings": 4096, "truncate": truncate}
+    inv_freq, attention_factor = ROPE_INIT_FUNCTIONS["yarn"](cfg, "cpu")
+    n = 100
+    pos = torch.arange(n, dtype=torch.float32)
+    ang = torch.outer(pos, inv_freq.float())
+    want = torch.cat((ang.cos(), ang.sin()), dim=-1) * attention_factor
+    torch.testing.assert_close(ours[:n], want, atol=2e-6, rtol=0)
